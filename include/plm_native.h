@@ -1,0 +1,113 @@
+/* C ABI of libplm_native.so: the B200 (sm_100a) kernels of the PLM decoding round.
+ *
+ * Conventions
+ *   - Every function returns an int status: PLM_OK (0) or a negative PLM_ERR_* code; plm_last_error() gives the
+ *     message of the calling thread's last failure.
+ *   - All tensor arguments are plain device pointers (bf16/f16 storage, fp32 or int32/int64 as stated) and sizes;
+ *     no framework types cross this boundary. `stream` is a cudaStream_t passed as void*.
+ *   - Launch functions only enqueue work on `stream`; they never synchronise, so they can be captured into a
+ *     CUDA graph. Device-side faults are not raised: a kernel that meets an index out of range or a wait that
+ *     runs out of time records a code in the context's device error word (plm_ctx_check reads it).
+ *   - A context (plm_ctx) owns the device error word and the split-reduction scratch. It is bound to the device
+ *     current at creation and must only be used from one host thread at a time.
+ *
+ * Reference interfaces replaced (paths inside justuswill/PLM-anon):
+ *   plm_gemm        plm/fast_gemm.py:82-97 (triton_linear) installed at plm/fast_gemm.py:100-113, and the
+ *                   vLLM unquantized linear it patches; epilogues fuse vLLM's SiluAndMul, rotary embedding and
+ *                   reshape_and_cache_flash (called from plm/decoder.py:250-259 through the Llama forward) and
+ *                   compute_logits + argmax (plm/decoder.py:318,362).
+ */
+#ifndef PLM_NATIVE_H
+#define PLM_NATIVE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PLM_ABI_VERSION 1
+
+enum plm_status {
+  PLM_OK = 0,
+  PLM_ERR_INVALID = -1,     /* bad argument (shape, pointer, dtype) */
+  PLM_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+  PLM_ERR_DEVICE = -3,      /* a kernel recorded an error in the device error word */
+  PLM_ERR_UNSUPPORTED = -4, /* a shape or option this build has no kernel for */
+  PLM_ERR_NOMEM = -5        /* device allocation failed */
+};
+
+enum plm_dtype { PLM_BF16 = 0, PLM_F16 = 1 };
+
+enum plm_epilogue {
+  PLM_EPI_STORE = 0,    /* out[r][n] = Y[r][n] in the model dtype */
+  PLM_EPI_SILU_MUL = 1, /* out[r][j] = silu(Y[r][j]) * Y[r][gate_offset + j], j < gate_offset */
+  PLM_EPI_QKV_ROPE = 2, /* neox RoPE on q,k; q -> q_out, k,v -> paged cache at slots[r] */
+  PLM_EPI_LOGITS = 3,   /* rows < n_verify: fp32 logits; other rows: per-tile (max, first index) */
+  PLM_EPI_TABLE = 4     /* table[n][a0 + r] = -Y[r][n] (the Voronoi cost table) */
+};
+
+typedef struct plm_ctx plm_ctx;
+
+/* Epilogue operands of plm_gemm (fields not used by the selected epilogue are ignored). */
+typedef struct plm_gemm_epilogue {
+  int32_t kind; /* enum plm_epilogue */
+  int32_t gate_offset;
+  /* PLM_EPI_QKV_ROPE */
+  void* q_out;
+  void* k_cache; /* [num_pages][num_kv_heads][page_size][head_dim] */
+  void* v_cache;
+  const int32_t* positions; /* [rows] */
+  const int64_t* slots;     /* [rows] physical slot = page * page_size + index in page */
+  const void* cos_sin;      /* [max_pos][head_dim] model dtype: cos | sin halves */
+  int32_t num_heads, num_kv_heads, head_dim, page_size;
+  int64_t num_slots;
+  int32_t max_pos;
+  /* PLM_EPI_LOGITS */
+  float* verify_logits; /* [n_verify][vocab] */
+  float* best_val;      /* [n_tiles][rows] */
+  int32_t* best_idx;    /* [n_tiles][rows] */
+  int32_t n_verify;
+  int32_t vocab;
+  /* PLM_EPI_TABLE */
+  void* table;
+  int32_t aux;
+  int32_t a0;
+} plm_gemm_epilogue;
+
+typedef struct plm_gemm_desc {
+  int32_t dtype;  /* enum plm_dtype */
+  const void* w;  /* [n_out][k] row-major weights */
+  int32_t n_out;
+  int32_t k;      /* multiple of 64 */
+  const void* x;  /* [x_rows][k] row-major activations, 16-byte aligned */
+  int32_t x_rows; /* allocated rows of x (>= rows) */
+  int32_t rows;   /* rows to compute, 1..256 */
+  void* out;      /* PLM_EPI_STORE / PLM_EPI_SILU_MUL output */
+  int32_t ldo;    /* output row stride in elements */
+  int32_t splits; /* 0 = choose automatically */
+  plm_gemm_epilogue epi;
+} plm_gemm_desc;
+
+/* ---- context ---- */
+int plm_ctx_create(plm_ctx** out);
+int plm_ctx_destroy(plm_ctx* ctx);
+/* Synchronises the device, then returns the device error word in *device_error and clears it. */
+int plm_ctx_check(plm_ctx* ctx, int32_t* device_error);
+/* Number of output tiles plm_gemm uses for (epilogue kind, n_out): the leading size of best_val/best_idx. */
+int plm_gemm_tiles(int32_t kind, int32_t n_out, int32_t gate_offset, int32_t* tiles);
+
+/* ---- kernels ---- */
+int plm_gemm(plm_ctx* ctx, const plm_gemm_desc* desc, void* stream);
+
+/* ---- diagnostics ---- */
+int plm_abi_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to n bytes). */
+int plm_last_error(char* buf, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PLM_NATIVE_H */

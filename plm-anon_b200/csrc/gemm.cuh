@@ -1,0 +1,375 @@
+// Skinny weight-streaming GEMM for the round: Y[rows, n_out] = X[rows, k] . W[n_out, k]^T, fp32 accumulation.
+//
+// The round has only W = k + k^2 query rows (56 at k = 7), so every weight byte is used by one MMA and the
+// kernel is bound by HBM bandwidth on the weight stream. The operands are swapped: a 128-row weight tile is the
+// MMA's M side (TMEM lanes = output features) and the round rows are its N side (TMEM columns = rows), so one
+// tcgen05.mma.kind::f16 of 128 x NTOK x 16 covers the whole round. Weight tiles (128 rows x 64 k, 16 KB) and
+// row tiles (NTOK rows x 64 k) are staged by TMA with the 128-byte swizzle into a STAGES-deep ring; one thread
+// issues TMA, one thread issues MMAs, and the four warps read the accumulator back with tcgen05.ld.
+//
+// Work is split over (output tile, k-split). With more than one split each CTA writes an fp32 partial tile to
+// scratch and the last CTA to arrive for a tile (arrival counter) sums the partials in split order, so the
+// result does not depend on arrival order. That CTA then runs the fused epilogue:
+//   kEpiStore    plain store in the model dtype;
+//   kEpiSiluMul  the gate_up projection with SiLU(gate) * up fused (tile = 64 gate rows + the matching 64 up rows);
+//   kEpiQkvRope  the qkv projection with neox RoPE on q and k, q written out, k and v scattered into the paged cache;
+//   kEpiLogits   the lm_head: verify rows as fp32 logits, proposal rows reduced to a per-tile (max, first index);
+//   kEpiTable    the Voronoi cost table, table[v][a] = -(aux_vocab[a] . lm_head[v]).
+// Weight loads are issued before griddepcontrol.wait, so under programmatic dependent launch they overlap the
+// tail of the previous kernel; everything that reads activations comes after it.
+#pragma once
+
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace plm {
+
+enum GemmEpilogueKind : int {
+  kEpiStore = 0,
+  kEpiSiluMul = 1,
+  kEpiQkvRope = 2,
+  kEpiLogits = 3,
+  kEpiTable = 4,
+};
+
+struct QkvEpilogue {
+  void* q_out;               // [rows][num_heads * head_dim]
+  void* k_cache;             // K plane: [num_pages][num_kv_heads][page_size][head_dim]
+  void* v_cache;             // V plane, same layout
+  const int32_t* positions;  // [rows] rotary position of each row
+  const int64_t* slots;      // [rows] physical slot = page * page_size + index within the page
+  const void* cos_sin;       // [max_pos][head_dim]: cos in [0, hd/2), sin in [hd/2, hd), model dtype
+  int num_heads, num_kv_heads, head_dim, page_size;
+  int64_t num_slots;         // num_pages * page_size
+  int max_pos;
+};
+
+struct LogitsEpilogue {
+  float* verify_logits;  // [n_verify][vocab]: fp32 copies of the model-dtype logits
+  float* best_val;       // [n_tiles][rows]: per-tile maximum of each proposal row
+  int32_t* best_idx;     // [n_tiles][rows]: its first index
+  int n_verify;
+  int vocab;
+};
+
+struct TableEpilogue {
+  void* table;  // [vocab][aux] model dtype
+  int aux;
+  int a0;       // aux item of this launch's row 0
+};
+
+struct GemmArgs {
+  int n_out;
+  int k;
+  int rows;
+  int n_tiles;
+  int splits;
+  int kb_per_split;
+  int gate_offset;  // kEpiSiluMul: first row of the up half inside W (the intermediate size)
+  void* out;
+  int ldo;
+  float* partial;   // split-K scratch [splits][n_tiles][NTOK][128]
+  int* counters;    // [n_tiles] arrival counters, zero between launches
+  int* err;
+  QkvEpilogue qkv;
+  LogitsEpilogue logits;
+  TableEpilogue table;
+};
+
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 128;
+constexpr int kStagePad = 129;  // fp32 staging row stride (odd: conflict-free both ways)
+
+template <int NTOK>
+struct GemmShape {
+  static constexpr int A_BYTES = 128 * kGemmBK * 2;
+  static constexpr int B_BYTES = NTOK * kGemmBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = NTOK <= 32 ? 32 : NTOK <= 64 ? 64 : NTOK <= 128 ? 128 : 256;
+  static_assert(NTOK % 16 == 0 && NTOK >= 16 && NTOK <= 256, "token tile must be a multiple of 16 in [16, 256]");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment for the 128-byte swizzle");
+};
+
+template <int NTOK, int STAGES>
+constexpr int gemm_smem_bytes() {
+  return STAGES * GemmShape<NTOK>::STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers, flags*/;
+}
+
+template <typename T, int NTOK, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    skinny_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                       const GemmArgs args) {
+  using Shape = GemmShape<NTOK>;
+  constexpr uint32_t IDESC = umma_idesc_f16(128, NTOK, std::is_same<T, __nv_bfloat16>::value);
+  static_assert(NTOK * kStagePad * 4 <= STAGES * Shape::STAGE_BYTES, "staging tile must fit in the ring");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Shape::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* done_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int total_kb = args.k / kGemmBK;
+  const int kb_begin = split * args.kb_per_split;
+  const int kb_end = (split == args.splits - 1) ? total_kb : kb_begin + args.kb_per_split;
+  const int nk = kb_end - kb_begin;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar + s, 1);
+      mbar_init(empty_bar + s, 1);
+    }
+    mbar_init(done_bar, 1);
+    flags[0] = 0;  // abort
+    flags[1] = 0;  // this CTA reduces the tile
+    flags[2] = 0;  // k-blocks issued by the producer
+    flags[3] = 0;  // k-blocks consumed by the MMA issuer
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, Shape::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  allow_dependents();
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    tma_prefetch_map(&map_w);
+    tma_prefetch_map(&map_x);
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint64_t pol_x = l2_policy_evict_last();
+    auto load_w = [&](int s, int kb) {
+      uint8_t* a = smem + s * Shape::STAGE_BYTES;
+      if (EPI == kEpiSiluMul) {
+        // 64 gate rows then the 64 up rows of the same intermediate features.
+        tma_load_2d(a, &map_w, full_bar + s, kb * kGemmBK, tile * 64, pol_w);
+        tma_load_2d(a + 64 * 128, &map_w, full_bar + s, kb * kGemmBK, args.gate_offset + tile * 64, pol_w);
+      } else {
+        tma_load_2d(a, &map_w, full_bar + s, kb * kGemmBK, tile * 128, pol_w);
+      }
+    };
+    auto load_x = [&](int s, int kb) {
+      uint8_t* b = smem + s * Shape::STAGE_BYTES + Shape::A_BYTES;
+      tma_load_2d(b, &map_x, full_bar + s, kb * kGemmBK, 0, pol_x);
+    };
+    const int pre = nk < STAGES ? nk : STAGES;
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(full_bar + i, Shape::STAGE_BYTES);
+      load_w(i, kb_begin + i);
+    }
+    grid_dependency_wait();  // the row operand is written by the previous kernel
+    for (int i = 0; i < pre; ++i) load_x(i, kb_begin + i);
+    int issued = pre;
+    for (int i = STAGES; i < nk; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(empty_bar + s, ((i / STAGES) - 1) & 1, args.err, kErrTimeoutEmpty)) {
+        // Stages already issued still land; the MMA issuer drains them before the CTA exits.
+        flags[0] = 1;
+        break;
+      }
+      mbar_arrive_expect_tx(full_bar + s, Shape::STAGE_BYTES);
+      load_w(s, kb_begin + i);
+      load_x(s, kb_begin + i);
+      issued = i + 1;
+    }
+    flags[2] = issued;
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int consumed = 0;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(full_bar + s, (i / STAGES) & 1, args.err, kErrTimeoutFull)) {
+        flags[0] = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(smem + s * Shape::STAGE_BYTES);
+      const uint32_t b_addr = a_addr + Shape::A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+        umma_f16(tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(empty_bar + s);
+      consumed = i + 1;
+    }
+    flags[3] = consumed;
+    umma_commit(done_bar);
+  }
+  grid_dependency_wait();
+
+  // ---------------- accumulator -> staging tile (fp32, [token][feature]) ----------------
+  const bool mma_ok = mbar_wait(done_bar, 0, args.err, kErrTimeoutDone);
+  tc_fence_after();
+  float* stage = reinterpret_cast<float*>(smem);
+  const int row = warp * 32 + lane;  // feature lane inside the 128-wide tile
+  const uint32_t t_warp = tmem + (uint32_t(warp * 32) << 16);
+  const int rows = args.rows;
+  bool have_tile = true;
+
+  if (args.splits == 1) {
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+      float v[32];
+      tmem_ld_32cols(t_warp + c0, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < rows) stage[(c0 + j) * kStagePad + row] = v[j];
+    }
+  } else {
+    float* mine = args.partial + (size_t(split) * args.n_tiles + tile) * NTOK * 128;
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+      float v[32];
+      tmem_ld_32cols(t_warp + c0, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < rows) __stcg(mine + (c0 + j) * 128 + row, v[j]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int old = atomicAdd(args.counters + tile, 1);
+      flags[1] = (old == args.splits - 1) ? 1 : 0;
+      if (old >= args.splits) record_error(args.err, kErrTimeoutSplit);
+    }
+    __syncthreads();
+    have_tile = flags[1] != 0;
+    if (have_tile) {
+      __threadfence();
+      const size_t split_stride = size_t(args.n_tiles) * NTOK * 128;
+      const float* base = args.partial + size_t(tile) * NTOK * 128;
+      for (int c = 0; c < rows; ++c) {
+        float acc = 0.f;
+        for (int s = 0; s < args.splits; ++s) acc += __ldcg(base + s * split_stride + c * 128 + row);
+        stage[c * kStagePad + row] = acc;
+      }
+      if (tid == 0) args.counters[tile] = 0;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (flags[0] != 0 && tid == 0) {
+    // Aborted: let every TMA copy this CTA issued but never consumed land before shared memory is released.
+    for (int i = flags[3]; i < flags[2]; ++i)
+      if (!mbar_wait(full_bar + (i % STAGES), (i / STAGES) & 1, args.err, kErrTimeoutFull)) break;
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Shape::TMEM_COLS);
+  }
+  __syncthreads();
+  if (!have_tile || !mma_ok || flags[0] != 0) return;
+
+  // ---------------- fused epilogues ----------------
+  if (EPI == kEpiStore) {
+    T* out = reinterpret_cast<T*>(args.out);
+    const int n0 = tile * 128;
+    const int feats = min(128, args.n_out - n0);
+    for (int idx = tid; idx < rows * 128; idx += kGemmThreads) {
+      const int c = idx >> 7, f = idx & 127;
+      if (f < feats) out[size_t(c) * args.ldo + n0 + f] = from_f32<T>(stage[c * kStagePad + f]);
+    }
+  } else if (EPI == kEpiSiluMul) {
+    T* out = reinterpret_cast<T*>(args.out);
+    const int j0 = tile * 64;
+    for (int idx = tid; idx < rows * 64; idx += kGemmThreads) {
+      const int c = idx >> 6, f = idx & 63;
+      const float g = round_to<T>(stage[c * kStagePad + f]);
+      const float u = round_to<T>(stage[c * kStagePad + 64 + f]);
+      const float act = g / (1.0f + expf(-g)) * u;
+      out[size_t(c) * args.ldo + j0 + f] = from_f32<T>(act);
+    }
+  } else if (EPI == kEpiQkvRope) {
+    const QkvEpilogue& q = args.qkv;
+    const int hd = q.head_dim, half = hd >> 1;
+    const int q_size = q.num_heads * hd, kv_size = q.num_kv_heads * hd;
+    const int n0 = tile * 128;
+    const T* cs = reinterpret_cast<const T*>(q.cos_sin);
+    for (int idx = tid; idx < rows * 128; idx += kGemmThreads) {
+      const int c = idx >> 7, f = idx & 127;
+      const int F = n0 + f;
+      const float x = round_to<T>(stage[c * kStagePad + f]);
+      const int d = F % hd;
+      float y = x;
+      if (F < q_size + kv_size) {
+        const int pos = q.positions[c];
+        if (pos < 0 || pos >= q.max_pos) {
+          record_error(args.err, kErrBadIndex);
+          continue;
+        }
+        const int dh = d < half ? d : d - half;
+        const int fp = d < half ? f + half : f - half;
+        const float xp = round_to<T>(stage[c * kStagePad + fp]);
+        const float cv = to_f32<T>(cs[size_t(pos) * hd + dh]);
+        const float sv = to_f32<T>(cs[size_t(pos) * hd + half + dh]);
+        y = d < half ? x * cv - xp * sv : x * cv + xp * sv;
+      }
+      if (F < q_size) {
+        reinterpret_cast<T*>(q.q_out)[size_t(c) * q_size + F] = from_f32<T>(y);
+      } else {
+        const bool is_k = F < q_size + kv_size;
+        const int g = (is_k ? F - q_size : F - q_size - kv_size) / hd;
+        const int64_t slot = q.slots[c];
+        if (slot < 0 || slot >= q.num_slots) {
+          record_error(args.err, kErrBadIndex);
+          continue;
+        }
+        const int64_t page = slot / q.page_size, within = slot % q.page_size;
+        T* plane = reinterpret_cast<T*>(is_k ? q.k_cache : q.v_cache);
+        plane[((page * q.num_kv_heads + g) * q.page_size + within) * hd + d] = from_f32<T>(y);
+      }
+    }
+  } else if (EPI == kEpiLogits) {
+    const LogitsEpilogue& L = args.logits;
+    const int n0 = tile * 128;
+    for (int idx = tid; idx < L.n_verify * 128; idx += kGemmThreads) {
+      const int c = idx >> 7, f = idx & 127;
+      if (c < rows && n0 + f < L.vocab)
+        L.verify_logits[size_t(c) * L.vocab + n0 + f] = round_to<T>(stage[c * kStagePad + f]);
+    }
+    for (int c = L.n_verify + warp; c < rows; c += kGemmThreads / 32) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int f = lane; f < 128; f += 32) {
+        const int v = n0 + f;
+        if (v < L.vocab) {
+          const float x = round_to<T>(stage[c * kStagePad + f]);
+          if (x > best || (x == best && v < bi)) {
+            best = x;
+            bi = v;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        L.best_val[size_t(tile) * rows + c] = best;
+        L.best_idx[size_t(tile) * rows + c] = bi;
+      }
+    }
+  } else if (EPI == kEpiTable) {
+    const TableEpilogue& tb = args.table;
+    T* table = reinterpret_cast<T*>(tb.table);
+    const int n0 = tile * 128;
+    const int feats = min(128, args.n_out - n0);
+    for (int idx = tid; idx < rows * 128; idx += kGemmThreads) {
+      const int f = idx / rows, c = idx % rows;
+      if (f < feats)
+        table[size_t(n0 + f) * tb.aux + tb.a0 + c] = from_f32<T>(-round_to<T>(stage[c * kStagePad + f]));
+    }
+  }
+}
+
+}  // namespace plm

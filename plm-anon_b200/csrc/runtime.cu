@@ -1,0 +1,166 @@
+// Context lifetime, error reporting and TMA descriptor encoding for libplm_native.so.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "runtime.h"
+
+namespace {
+thread_local char g_last_error[1024] = "";
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Split-reduction scratch of a context: enough for the widest launch of the round (lm_head over 50k features
+// at 3 splits and 64 rows is 38.6 MB).
+constexpr size_t kPartialFloats = size_t(16) << 20;  // 64 MB
+constexpr int kCounters = 8192;
+}  // namespace
+
+namespace plm {
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PLM_OK;
+  return fail(e == cudaErrorMemoryAllocation ? PLM_ERR_NOMEM : PLM_ERR_CUDA, "%s: %s (%s)", what,
+              cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(PLM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride_bytes & 15) != 0)
+    return fail(PLM_ERR_INVALID, "TMA operand must be 16-byte aligned (base %p, row stride %llu)", base,
+                (unsigned long long)row_stride_bytes);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType t = dtype == PLM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PLM_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] box [%u x %u]", int(r),
+                (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+  return PLM_OK;
+}
+
+void plan_splits(int tiles, int total_kb, int num_sms, int ctas_per_sm, int* splits, int* kb_per_split) {
+  const int slots = num_sms * ctas_per_sm;
+  int max_s = total_kb / 2;
+  if (max_s < 1) max_s = 1;
+  if (max_s > 32) max_s = 32;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= max_s; ++s) {
+    const long ctas = long(tiles) * s;
+    const long waves = (ctas + slots - 1) / slots;
+    const double eff = double(ctas) / double(waves * slots);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  int per = (total_kb + best - 1) / best;
+  *kb_per_split = per;
+  *splits = (total_kb + per - 1) / per;
+}
+
+}  // namespace plm
+
+using namespace plm;
+
+extern "C" {
+
+int plm_abi_version(void) { return PLM_ABI_VERSION; }
+
+int plm_last_error(char* buf, size_t n) {
+  if (buf == nullptr || n == 0) return PLM_ERR_INVALID;
+  strncpy(buf, g_last_error, n - 1);
+  buf[n - 1] = '\0';
+  return PLM_OK;
+}
+
+int plm_ctx_create(plm_ctx** out) {
+  if (out == nullptr) return fail(PLM_ERR_INVALID, "plm_ctx_create: null output");
+  *out = nullptr;
+  plm_ctx* c = new plm_ctx();
+  int st = check_cuda(cudaGetDevice(&c->device), "cudaGetDevice");
+  if (st == PLM_OK) st = check_cuda(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, c->device),
+                                    "cudaDeviceGetAttribute(sm count)");
+  if (st == PLM_OK)
+    st = check_cuda(cudaDeviceGetAttribute(&c->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device),
+                    "cudaDeviceGetAttribute(smem)");
+  if (st == PLM_OK) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, c->device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, c->device);
+    if (major != 10 || minor != 0)
+      st = fail(PLM_ERR_UNSUPPORTED, "libplm_native is built for sm_100a only; device %d is sm_%d%d", c->device,
+                major, minor);
+  }
+  if (st == PLM_OK) st = check_cuda(cudaMalloc(&c->err, sizeof(int)), "cudaMalloc(error word)");
+  if (st == PLM_OK) st = check_cuda(cudaMemset(c->err, 0, sizeof(int)), "cudaMemset(error word)");
+  if (st == PLM_OK) st = check_cuda(cudaMalloc(&c->partial, kPartialFloats * sizeof(float)), "cudaMalloc(scratch)");
+  if (st == PLM_OK) c->partial_floats = kPartialFloats;
+  if (st == PLM_OK) st = check_cuda(cudaMalloc(&c->counters, kCounters * sizeof(int)), "cudaMalloc(counters)");
+  if (st == PLM_OK) st = check_cuda(cudaMemset(c->counters, 0, kCounters * sizeof(int)), "cudaMemset(counters)");
+  if (st == PLM_OK) c->n_counters = kCounters;
+  if (st == PLM_OK) st = check_cuda(cudaDeviceSynchronize(), "plm_ctx_create");
+  if (st != PLM_OK) {
+    plm_ctx_destroy(c);
+    return st;
+  }
+  *out = c;
+  return PLM_OK;
+}
+
+int plm_ctx_destroy(plm_ctx* ctx) {
+  if (ctx == nullptr) return PLM_OK;
+  cudaFree(ctx->err);
+  cudaFree(ctx->partial);
+  cudaFree(ctx->counters);
+  delete ctx;
+  return PLM_OK;
+}
+
+int plm_ctx_check(plm_ctx* ctx, int32_t* device_error) {
+  if (ctx == nullptr || device_error == nullptr) return fail(PLM_ERR_INVALID, "plm_ctx_check: null argument");
+  int st = check_cuda(cudaDeviceSynchronize(), "plm_ctx_check: synchronize");
+  if (st != PLM_OK) return st;
+  int v = 0;
+  st = check_cuda(cudaMemcpy(&v, ctx->err, sizeof(int), cudaMemcpyDeviceToHost), "plm_ctx_check: read");
+  if (st != PLM_OK) return st;
+  *device_error = v;
+  if (v != 0) {
+    cudaMemset(ctx->err, 0, sizeof(int));
+    // A launch that stopped early may have left arrival counters mid-count.
+    cudaMemset(ctx->counters, 0, ctx->n_counters * sizeof(int));
+    cudaDeviceSynchronize();
+  }
+  return PLM_OK;
+}
+
+}  // extern "C"

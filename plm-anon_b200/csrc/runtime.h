@@ -1,0 +1,65 @@
+// Host-side runtime shared by the C-ABI entry points: the context, error reporting, TMA descriptor encoding and
+// launches with programmatic dependent launch enabled.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/plm_native.h"
+
+struct plm_ctx {
+  int device = 0;
+  int num_sms = 148;
+  int max_smem_optin = 0;
+  int* err = nullptr;           // device error word
+  float* partial = nullptr;     // split-reduction scratch (fp32)
+  size_t partial_floats = 0;
+  int* counters = nullptr;      // arrival counters, zero between launches
+  int n_counters = 0;
+};
+
+namespace plm {
+
+// Records a message for plm_last_error() and returns `status`.
+int fail(int status, const char* fmt, ...);
+// Returns PLM_OK or records the CUDA error (with `what`) and returns PLM_ERR_CUDA.
+int check_cuda(cudaError_t e, const char* what);
+
+// Encodes a 2-D tiled TMA descriptor over a row-major [outer][inner] tensor of 2-byte elements with the 128-byte
+// swizzle. Returns PLM_OK or an error status.
+int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+
+// Split count for a weight-streaming launch of `tiles` output tiles over `total_kb` k-blocks, so that the grid
+// fills whole waves of `ctas_per_sm` resident CTAs per SM. Every split gets at least one k-block.
+void plan_splits(int tiles, int total_kb, int num_sms, int ctas_per_sm, int* splits, int* kb_per_split);
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Internal GEMM launch used by plm_gemm and by the round engine (`map_w` encoded once per weight).
+int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,
+                cudaStream_t stream, bool pdl);
+int gemm_weight_map(CUtensorMap* map, const plm_gemm_desc& d);
+int gemm_row_map(CUtensorMap* map, const plm_gemm_desc& d);
+int gemm_token_tile(int rows);
+
+}  // namespace plm
