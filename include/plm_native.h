@@ -16,6 +16,9 @@
  *                   vLLM unquantized linear it patches; epilogues fuse vLLM's SiluAndMul, rotary embedding and
  *                   reshape_and_cache_flash (called from plm/decoder.py:250-259 through the Llama forward) and
  *                   compute_logits + argmax (plm/decoder.py:318,362).
+ *   plm_verify_decode  LogitVoronoiAuxiliary.decode_unmasked (plm/auxiliary.py:67-75) -> Voronoi.assign
+ *                   (plm/iterate.py:322-342), nucleus_acceptance / floor_acceptance (plm/decoder.py:71-82) and
+ *                   RoundDecoder._epilogue / _round0 bookkeeping (plm/decoder.py:351-365, 275-310, 384).
  */
 #ifndef PLM_NATIVE_H
 #define PLM_NATIVE_H
@@ -46,6 +49,15 @@ enum plm_epilogue {
   PLM_EPI_QKV_ROPE = 2, /* neox RoPE on q,k; q -> q_out, k,v -> paged cache at slots[r] */
   PLM_EPI_LOGITS = 3,   /* rows < n_verify: fp32 logits; other rows: per-tile (max, first index) */
   PLM_EPI_TABLE = 4     /* table[n][a0 + r] = -Y[r][n] (the Voronoi cost table) */
+};
+
+enum plm_accept_rule { PLM_RULE_NUCLEUS = 0, PLM_RULE_FLOOR = 1 };
+
+enum plm_book_mode {
+  PLM_BOOK_NONE = 0,        /* decode only */
+  PLM_BOOK_STEADY = 1,      /* steady round: acceptance, outputs, next pending, base/offset commit */
+  PLM_BOOK_ROUND0 = 2,      /* round 0: one verify row, nothing accepted */
+  PLM_BOOK_FIRST_TOKEN = 3  /* after the prefill: first token, request state reset */
 };
 
 typedef struct plm_ctx plm_ctx;
@@ -90,6 +102,56 @@ typedef struct plm_gemm_desc {
   plm_gemm_epilogue epi;
 } plm_gemm_desc;
 
+/* Round state the verify kernel's last CTA updates (plm/decoder.py:351-365, 275-310, 384). */
+typedef struct plm_bookkeeping {
+  int32_t mode; /* enum plm_book_mode */
+  int32_t k;
+  const float* best_val;   /* [n_tiles][rows] lm_head per-tile row maxima (PLM_EPI_LOGITS) */
+  const int32_t* best_idx; /* [n_tiles][rows] */
+  int32_t n_tiles;
+  int32_t rows;
+  int64_t* out; /* [out_cap] */
+  int64_t out_cap;
+  int64_t* base;
+  int64_t* offset;
+  int64_t* anchor;
+  int64_t* pending; /* [k - 1] */
+  int64_t* round_sequence; /* [seq_cap] */
+  int64_t seq_cap;
+  int64_t* sequence_step;
+  int64_t prompt_len;
+} plm_bookkeeping;
+
+/* One verify decode per row: Voronoi assignment of the row's logits (plm/iterate.py:322-342 through
+ * plm/auxiliary.py:67-75) and, for rows < n_accept, the relaxed acceptance rule (plm/decoder.py:71-82). */
+typedef struct plm_verify_desc {
+  int32_t dtype;
+  const float* logits; /* [n_rows][logits_stride] */
+  int32_t n_rows;
+  int32_t vocab;
+  int64_t logits_stride;
+  const void* table; /* [vocab][aux] */
+  int32_t aux;
+  const int64_t* aux_buf;
+  int64_t aux_len;
+  const int64_t* aux_base; /* device scalar (nullable) */
+  int32_t aux_row_offset;  /* row r reads aux_buf[*aux_base + aux_row_offset + r] */
+  const int64_t* pending;  /* [n_accept] */
+  int32_t n_accept;
+  int32_t rule; /* enum plm_accept_rule */
+  float threshold;
+  int32_t top_m, shortlist, rounds, sweeps;
+  double epsilon, refocus, endpoint;
+  int64_t* verify; /* [n_rows] */
+  int32_t* flags;  /* [n_rows] */
+  int32_t* dbg_tokens;
+  int32_t* dbg_counts;
+  float* dbg_bias;
+  float* dbg_stats;
+  int32_t* dbg_sigma;
+  plm_bookkeeping book;
+} plm_verify_desc;
+
 /* ---- context ---- */
 int plm_ctx_create(plm_ctx** out);
 int plm_ctx_destroy(plm_ctx* ctx);
@@ -100,6 +162,8 @@ int plm_gemm_tiles(int32_t kind, int32_t n_out, int32_t gate_offset, int32_t* ti
 
 /* ---- kernels ---- */
 int plm_gemm(plm_ctx* ctx, const plm_gemm_desc* desc, void* stream);
+/* Verify decode + acceptance + (optionally) the round bookkeeping, one CTA per row. */
+int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* desc, void* stream);
 
 /* ---- diagnostics ---- */
 int plm_abi_version(void);

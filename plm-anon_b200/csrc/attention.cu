@@ -1,0 +1,399 @@
+// Paged attention of the round's query rows under the round mask (replaces FlexAttention with the block mask of
+// plm/mask.py:23-29 as vLLM's backend calls it: vllm/v1/attention/backends/flex_attention.py:1070-1205).
+//
+// Grid (head, KV split, 64-row query tile), 4 warps; warp w owns query rows [16w, 16w + 16) of the tile.
+// Keys are visited in tiles of 64: each tile's K and V rows are gathered page by page through the block table
+// with 16-byte cp.async into XOR-swizzled shared memory (double buffered), S = Q K^T and O += P V run on tensor
+// cores (mma.m16n8k16 bf16, fp32 accumulation; P is rounded to bf16 for the second product), and the softmax is
+// online in base 2. Key kv is visible to row r (logical query offset + r) iff
+//     kv < offset + rows  and  (kv < offset  or  kv - offset <= depth[r]
+//                                 or  (kv - offset >= own_start[r]  and  kv <= offset + r)),
+// which is RoundMaskView for a round (depth / own_start from round_layout) and plain causal attention for a
+// prefill chunk (depth[r] = r). With more than one split every CTA writes an unnormalised partial (O, m, l) and
+// the last CTA of the (head, query tile) combines the splits in split order.
+#include "attention.h"
+#include "common.cuh"
+#include "runtime.h"
+
+namespace plm {
+namespace {
+
+constexpr int kKeysPerTile = 64;
+constexpr int kAttnThreads = 128;
+constexpr int kQRowsPerCta = 64;
+
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src, bool valid) {
+  const int size = valid ? 16 : 0;  // 0: zero-fill
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src), "r"(size)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Byte offset of (row, 16-byte chunk) in a swizzled tile with HD/8 chunks per row.
+template <int HD>
+__device__ __forceinline__ int swz(int row, int chunk) {
+  return row * (HD * 2) + ((chunk ^ (row & 7)) << 4);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const AttnArgs a) {
+  constexpr int CH = HD / 8;
+  constexpr int TILE_BYTES = kKeysPerTile * HD * 2;
+  constexpr int NT = kKeysPerTile / 8;  // key n-tiles per tile
+  constexpr int KS = HD / 16;           // k-steps over the head dim
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* kbuf[2] = {smem, smem + TILE_BYTES};
+  uint8_t* vbuf[2] = {smem + 2 * TILE_BYTES, smem + 3 * TILE_BYTES};
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int head = blockIdx.x, split = blockIdx.y, qt = blockIdx.z;
+  const int group = head / (a.num_heads / a.num_kv_heads);
+
+  grid_dependency_wait();
+  allow_dependents();
+
+  const int64_t offset = *a.offset;
+  const int64_t seq_len = offset + a.rows;
+  const int n_tiles = int((seq_len + kKeysPerTile - 1) / kKeysPerTile);
+  const int per = (n_tiles + a.splits - 1) / a.splits;
+  const int t0 = split * per;
+  const int t1 = min(n_tiles, t0 + per);
+
+  // ---- query fragments (A operand, rows r0 and r0 + 8 of this warp) ----
+  const int r0 = qt * kQRowsPerCta + warp * 16 + gq, r1 = r0 + 8;
+  const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  const size_t q_stride = size_t(a.num_heads) * HD;
+  uint32_t qf[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    const int col = kk * 16 + 2 * tq;
+    auto ld = [&](int rr, int c) -> uint32_t {
+      if (rr >= a.rows) return 0u;
+      return *reinterpret_cast<const uint32_t*>(q + size_t(rr) * q_stride + size_t(head) * HD + c);
+    };
+    qf[kk][0] = ld(r0, col);
+    qf[kk][1] = ld(r1, col);
+    qf[kk][2] = ld(r0, col + 8);
+    qf[kk][3] = ld(r1, col + 8);
+  }
+  const int dep0 = r0 < a.rows ? a.depth[r0] : -1, own0 = r0 < a.rows ? a.own_start[r0] : (1 << 30);
+  const int dep1 = r1 < a.rows ? a.depth[r1] : -1, own1 = r1 < a.rows ? a.own_start[r1] : (1 << 30);
+
+  const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
+  const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache);
+  auto issue = [&](int t, int buf) {
+#pragma unroll
+    for (int i = 0; i < (kKeysPerTile * CH) / kAttnThreads; ++i) {
+      const int idx = tid + i * kAttnThreads;
+      const int row = idx / CH, chunk = idx % CH;
+      const int64_t kv = int64_t(t) * kKeysPerTile + row;
+      bool valid = kv < seq_len;
+      size_t src = 0;
+      if (valid) {
+        const int64_t lp = kv / a.page_size;
+        const int page = lp < a.max_pages ? a.block_table[lp] : -1;
+        if (page < 0 || page >= a.num_pages) {
+          record_error(a.err, kErrBadIndex);
+          valid = false;
+        } else {
+          src = ((size_t(page) * a.num_kv_heads + group) * a.page_size + size_t(kv % a.page_size)) * HD + chunk * 8;
+        }
+      }
+      cp_async_16(kbuf[buf] + swz<HD>(row, chunk), kc + src, valid);
+      cp_async_16(vbuf[buf] + swz<HD>(row, chunk), vc + src, valid);
+    }
+    cp_async_commit();
+  };
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float scale = a.scale_log2;
+
+  if (t0 < t1) issue(t0, 0);
+  for (int t = t0; t < t1; ++t) {
+    const int buf = (t - t0) & 1;
+    if (t + 1 < t1) {
+      issue(t + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint8_t* kb = kbuf[buf];
+    const uint8_t* vb = vbuf[buf];
+
+    float s[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+      for (int jj = 0; jj < NT / 2; ++jj) {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = jj * 16 + (mi >> 1) * 8 + rr;
+        const int chunk = kk * 2 + (mi & 1);
+        uint32_t b[4];
+        ldmatrix_x4(b, kb + swz<HD>(row, chunk));
+        mma_bf16(s[2 * jj], qf[kk], b[0], b[1]);
+        mma_bf16(s[2 * jj + 1], qf[kk], b[2], b[3]);
+      }
+    }
+    // scale + mask
+    const int64_t kbase = int64_t(t) * kKeysPerTile;
+    const bool need_mask = kbase + kKeysPerTile > offset;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = s[j][e] * scale;
+        if (need_mask) {
+          const int64_t kv = kbase + j * 8 + 2 * tq + (e & 1);
+          const int rr = e < 2 ? r0 : r1;
+          const int dep = e < 2 ? dep0 : dep1, own = e < 2 ? own0 : own1;
+          bool vis = kv < seq_len;
+          if (vis && kv >= offset) {
+            const int64_t rel = kv - offset;
+            vis = rel <= dep || (rel >= own && rel <= rr);
+          }
+          if (!vis) v = -INFINITY;
+        }
+        s[j][e] = v;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float c0 = n0 == -INFINITY ? 1.f : exp2f(m0 - n0);
+    const float c1 = n1 == -INFINITY ? 1.f : exp2f(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      s[j][0] = n0 == -INFINITY ? 0.f : exp2f(s[j][0] - n0);
+      s[j][1] = n0 == -INFINITY ? 0.f : exp2f(s[j][1] - n0);
+      s[j][2] = n1 == -INFINITY ? 0.f : exp2f(s[j][2] - n1);
+      s[j][3] = n1 == -INFINITY ? 0.f : exp2f(s[j][3] - n1);
+      ps0 += s[j][0] + s[j][1];
+      ps1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * c0 + ps0;
+    l1 = l1 * c1 + ps1;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      o[j][0] *= c0;
+      o[j][1] *= c0;
+      o[j][2] *= c1;
+      o[j][3] *= c1;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < kKeysPerTile / 16; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int nn = 0; nn < HD / 16; ++nn) {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = kk * 16 + (mi & 1) * 8 + rr;
+        const int chunk = nn * 2 + (mi >> 1);
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, vb + swz<HD>(row, chunk));
+        mma_bf16(o[2 * nn], pa, b[0], b[1]);
+        mma_bf16(o[2 * nn + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  const size_t out_stride = size_t(a.num_heads) * HD;
+  if (a.splits == 1) {
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      const int col = head * HD + j * 8 + 2 * tq;
+      if (r0 < a.rows)
+        *reinterpret_cast<__nv_bfloat162*>(out + size_t(r0) * out_stride + col) =
+            __floats2bfloat162_rn(o[j][0] * inv0, o[j][1] * inv0);
+      if (r1 < a.rows)
+        *reinterpret_cast<__nv_bfloat162*>(out + size_t(r1) * out_stride + col) =
+            __floats2bfloat162_rn(o[j][2] * inv1, o[j][3] * inv1);
+    }
+    return;
+  }
+
+  // ---- split partials, combined by the last CTA of (head, query tile) ----
+  const int q_tiles = gridDim.z;
+  const size_t slot = (size_t(head) * q_tiles + qt) * a.splits + split;
+  float* po = a.partial + slot * kQRowsPerCta * HD;
+  float* pml = a.partial_ml + slot * kQRowsPerCta * 2;
+  const int lr0 = warp * 16 + gq, lr1 = lr0 + 8;
+#pragma unroll
+  for (int j = 0; j < HD / 8; ++j) {
+    const int col = j * 8 + 2 * tq;
+    __stcg(reinterpret_cast<float2*>(po + lr0 * HD + col), make_float2(o[j][0], o[j][1]));
+    __stcg(reinterpret_cast<float2*>(po + lr1 * HD + col), make_float2(o[j][2], o[j][3]));
+  }
+  if (tq == 0) {
+    __stcg(reinterpret_cast<float2*>(pml + lr0 * 2), make_float2(m0, l0));
+    __stcg(reinterpret_cast<float2*>(pml + lr1 * 2), make_float2(m1, l1));
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int c = head * q_tiles + qt;
+    const int old = atomicAdd(a.counters + c, 1);
+    s_last = old == a.splits - 1 ? 1 : 0;
+    if (old >= a.splits) record_error(a.err, kErrTimeoutSplit);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) a.counters[head * q_tiles + qt] = 0;
+
+  const size_t first = (size_t(head) * q_tiles + qt) * a.splits;
+  const int row = tid >> 1;
+  const int grow = qt * kQRowsPerCta + row;
+  const int c_begin = (tid & 1) * (HD / 2);
+  float mmax = -INFINITY;
+  for (int sp = 0; sp < a.splits; ++sp) mmax = fmaxf(mmax, __ldcg(a.partial_ml + (first + sp) * kQRowsPerCta * 2 + row * 2));
+  float lsum = 0.f;
+  for (int sp = 0; sp < a.splits; ++sp) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.partial_ml + (first + sp) * kQRowsPerCta * 2 + row * 2));
+    const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mmax);
+    lsum += w * ml.y;
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  if (grow < a.rows) {
+    for (int c = c_begin; c < c_begin + HD / 2; c += 2) {
+      float acc0 = 0.f, acc1 = 0.f;
+      for (int sp = 0; sp < a.splits; ++sp) {
+        const float mm = __ldcg(a.partial_ml + (first + sp) * kQRowsPerCta * 2 + row * 2);
+        const float w = mm == -INFINITY ? 0.f : exp2f(mm - mmax);
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(a.partial + (first + sp) * kQRowsPerCta * HD + row * HD + c));
+        acc0 += w * v.x;
+        acc1 += w * v.y;
+      }
+      *reinterpret_cast<__nv_bfloat162*>(out + size_t(grow) * out_stride + head * HD + c) =
+          __floats2bfloat162_rn(acc0 * inv, acc1 * inv);
+    }
+  }
+}
+
+template <int HD>
+int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool pdl) {
+  constexpr int SMEM = 4 * kKeysPerTile * HD * 2;
+  auto kernel = round_attention_kernel<HD>;
+  static bool attr = false;
+  if (!attr) {
+    int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
+                        "cudaFuncSetAttribute(attention smem)");
+    if (st != PLM_OK) return st;
+    attr = true;
+  }
+  return check_cuda(launch(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl, a),
+                    "round_attention_kernel");
+}
+
+}  // namespace
+
+int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys) {
+  const int ctas = num_heads * q_tiles;
+  int splits = (2 * num_sms + ctas - 1) / ctas;
+  const int max_tiles = int((max_keys + kKeysPerTile - 1) / kKeysPerTile);
+  if (splits > max_tiles) splits = max_tiles;
+  if (splits > 64) splits = 64;
+  return splits < 1 ? 1 : splits;
+}
+
+int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
+  if (a.head_dim != 64 && a.head_dim != 128) return fail(PLM_ERR_UNSUPPORTED, "attention: head_dim %d", a.head_dim);
+  if (a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads != 0)
+    return fail(PLM_ERR_INVALID, "attention: %d heads over %d kv heads", a.num_heads, a.num_kv_heads);
+  if (a.rows < 1 || a.rows > 1024) return fail(PLM_ERR_INVALID, "attention: rows %d", a.rows);
+  if (!a.q || !a.k_cache || !a.v_cache || !a.block_table || !a.offset || !a.depth || !a.own_start || !a.out)
+    return fail(PLM_ERR_INVALID, "attention: null operand");
+  const int q_tiles = (a.rows + kQRowsPerCta - 1) / kQRowsPerCta;
+  if (a.splits < 1) a.splits = 1;
+  const size_t need = size_t(a.num_heads) * q_tiles * a.splits * kQRowsPerCta * (a.head_dim + 2);
+  if (a.splits > 1 && (need > ctx->partial_floats || a.num_heads * q_tiles > ctx->n_counters - 1))
+    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits exceed the context scratch", a.splits);
+  a.partial = ctx->partial;
+  a.partial_ml = ctx->partial + size_t(a.num_heads) * q_tiles * a.splits * kQRowsPerCta * a.head_dim;
+  a.counters = ctx->counters;
+  a.err = ctx->err;
+  return a.head_dim == 128 ? launch_attention<128>(a, q_tiles, stream, pdl)
+                           : launch_attention<64>(a, q_tiles, stream, pdl);
+}
+
+}  // namespace plm
+
+using namespace plm;
+
+extern "C" int plm_attention(plm_ctx* ctx, const plm_attention_desc* d, void* stream) {
+  if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_attention: null argument");
+  if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_attention: only bf16 is built");
+  AttnArgs a = {};
+  a.q = d->q;
+  a.k_cache = d->k_cache;
+  a.v_cache = d->v_cache;
+  a.block_table = d->block_table;
+  a.max_pages = d->max_pages;
+  a.num_pages = d->num_pages;
+  a.page_size = d->page_size;
+  a.offset = d->offset;
+  a.rows = d->rows;
+  a.depth = d->depth;
+  a.own_start = d->own_start;
+  a.num_heads = d->num_heads;
+  a.num_kv_heads = d->num_kv_heads;
+  a.head_dim = d->head_dim;
+  a.scale_log2 = float(1.4426950408889634 / sqrt(double(d->head_dim)));
+  a.out = d->out;
+  const int q_tiles = (d->rows + kQRowsPerCta - 1) / kQRowsPerCta;
+  a.splits = d->splits > 0 ? d->splits : attention_splits(d->num_heads, q_tiles, ctx->num_sms, d->max_keys);
+  return attention_launch(ctx, a, static_cast<cudaStream_t>(stream), true);
+}

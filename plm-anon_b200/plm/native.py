@@ -44,6 +44,29 @@ class GemmDesc(ctypes.Structure):
                 ("epi", GemmEpilogue)]
 
 
+RULE_NUCLEUS, RULE_FLOOR = 0, 1
+BOOK_NONE, BOOK_STEADY, BOOK_ROUND0, BOOK_FIRST_TOKEN = range(4)
+
+
+class Bookkeeping(ctypes.Structure):
+    _fields_ = [("mode", c_int32), ("k", c_int32), ("best_val", c_void_p), ("best_idx", c_void_p),
+                ("n_tiles", c_int32), ("rows", c_int32), ("out", c_void_p), ("out_cap", c_int64),
+                ("base", c_void_p), ("offset", c_void_p), ("anchor", c_void_p), ("pending", c_void_p),
+                ("round_sequence", c_void_p), ("seq_cap", c_int64), ("sequence_step", c_void_p),
+                ("prompt_len", c_int64)]
+
+
+class VerifyDesc(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("logits", c_void_p), ("n_rows", c_int32), ("vocab", c_int32),
+                ("logits_stride", c_int64), ("table", c_void_p), ("aux", c_int32), ("aux_buf", c_void_p),
+                ("aux_len", c_int64), ("aux_base", c_void_p), ("aux_row_offset", c_int32), ("pending", c_void_p),
+                ("n_accept", c_int32), ("rule", c_int32), ("threshold", ctypes.c_float),
+                ("top_m", c_int32), ("shortlist", c_int32), ("rounds", c_int32), ("sweeps", c_int32),
+                ("epsilon", ctypes.c_double), ("refocus", ctypes.c_double), ("endpoint", ctypes.c_double),
+                ("verify", c_void_p), ("flags", c_void_p), ("dbg_tokens", c_void_p), ("dbg_counts", c_void_p),
+                ("dbg_bias", c_void_p), ("dbg_stats", c_void_p), ("dbg_sigma", c_void_p), ("book", Bookkeeping)]
+
+
 _lib: ctypes.CDLL | None = None
 
 # name -> (argtypes); every entry point returns int
@@ -55,6 +78,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_ctx_check": [c_void_p, POINTER(c_int32)],
     "plm_gemm_tiles": [c_int32, c_int32, c_int32, POINTER(c_int32)],
     "plm_gemm": [c_void_p, POINTER(GemmDesc), c_void_p],
+    "plm_verify_decode": [c_void_p, POINTER(VerifyDesc), c_void_p],
 }
 
 
@@ -144,3 +168,8 @@ def gemm(ctx: Context, w, x, rows: int, *, out=None, epi: GemmEpilogue | None = 
     desc = GemmDesc(dtype=PLM_BF16, w=ptr(w), n_out=w.shape[0], k=w.shape[1], x=ptr(x), x_rows=x.shape[0],
                     rows=rows, out=ptr(out), ldo=(out.stride(0) if out is not None else 0), splits=splits, epi=epi)
     check(library().plm_gemm(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_gemm")
+
+
+def verify_decode(ctx: Context, desc: VerifyDesc, stream=None) -> None:
+    """Enqueue plm_verify_decode (one CTA per row)."""
+    check(library().plm_verify_decode(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_verify_decode")
