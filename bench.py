@@ -1,0 +1,438 @@
+"""Benchmark of the PLM round step on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+Workload (the single-round microbenchmark): PLM-1.3B shape (24 layers, d 2048, 16x128
+MHA, SiLU-gated MLP 8192, vocab 50257), bf16 N(0, 0.02) weights from seed 0, k = 7 (7 verify + 49 proposal rows),
+exact match with Voronoi sampling, KV context of 1024 tokens in 16-token pages through a shuffled block table, K/V
+~ N(0, 1). A step is one steady round (a replay of the captured round graph); the state carries over between
+steps, so the context grows by the accepted tokens. Weights (3.4 GB) exceed L2, so no flush is needed.
+
+  value   accepted tokens/s over all GPUs, device-timed with CUDA events (inputs resident in HBM).
+  e2e     the same metric through the public API: RoundDecoder.generate on a 256-token prompt copied from pinned
+          host memory, 512 new tokens, with the per-round pinned-memory poll of the reference's decode loop and
+          the tokens read back (configs[2] per request).
+  roofline  the dominant kernel (skinny_gemm_kernel: every weight GEMM of the round, launched exactly as in the
+          round) timed live by CUDA events: weight bytes / time, against the measured HBM copy bandwidth.
+  round_roofline  all algorithmic bytes of a round (weights, KV read and written, Voronoi gathers) / round time.
+  cpu_baseline    the CPU oracle's round (oracle/model.py, torch on all host threads) on a bounded sample.
+
+Multi-GPU (torchrun, one process per GPU): replicas only — every rank runs the same workload on its own GPU
+(weak scaling), no data-path collective; the elapsed time is the maximum over ranks.
+``--impl reference`` times the reference arm: the CPU oracle round (the reference's path has no CPU
+implementation of its own) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "plm-anon_b200"), str(ROOT)]
+
+METRIC = "accepted tokens/sec/GPU at batch 1 (PLM-1.3B shape, k=7); round latency µs; %HBM"
+UNIT = "tokens/s"
+SHAPE, K, PAGE, CTX = "plm-1.3b", 7, 16, 1024
+PROMPT_E2E, TOKENS_E2E = 256, 512
+
+
+def _peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.device_index, self.samples, self.proc = device_index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.samples[0][2]) if self.samples[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def round_bytes(cfg, ctx: float, k: int) -> dict:
+    """Algorithmic HBM bytes of one round (the per-round figure of the roofline)."""
+    b = 2
+    hd, kvh, L = cfg.head_dim, cfg.num_kv_heads, cfg.num_layers
+    q_size, kv_size = cfg.num_heads * hd, kvh * hd
+    per_layer = ((q_size + 2 * kv_size) * cfg.hidden + cfg.hidden * q_size + 2 * cfg.intermediate * cfg.hidden
+                 + cfg.hidden * cfg.intermediate) * b
+    weights = L * per_layer + cfg.vocab * cfg.hidden * b
+    w = k + k * k
+    kv_read = ctx * L * 2 * kv_size * b
+    kv_write = w * L * 2 * kv_size * b
+    embed = w * cfg.hidden * b
+    voronoi = k * (2 * cfg.top_m * cfg.aux_vocab * b + cfg.top_m * 64 * b)
+    logits = 2 * k * cfg.vocab * 4
+    return {"weights": weights, "kv_read": kv_read, "kv_write": kv_write, "embed": embed, "voronoi": voronoi,
+            "logits": logits, "total": weights + kv_read + kv_write + embed + voronoi + logits}
+
+
+def _dist():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        return rank, world, local, dist
+    if torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return 0, 1, 0, None
+
+
+def _setup_decoder(seed: int = 0):
+    """The configs[1] workload: weights, a decoder over a shuffled pool, a 1024-token N(0, 1) context."""
+    import torch
+
+    from plm.decoder import RoundDecoder
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config(SHAPE)
+    weights = PLMWeights.random(cfg, seed=seed)
+    max_model_len = 2048
+    max_pages = -(-(max_model_len + 2 * (K + K * K) + PAGE) // PAGE)
+    num_pages = 2 * max_pages
+    page_bytes = cfg.num_layers * 2 * cfg.num_kv_heads * PAGE * cfg.head_dim * 2
+    g = torch.Generator().manual_seed(seed)
+    table = torch.randperm(num_pages, generator=g)[:max_pages].tolist()
+    decoder = RoundDecoder(weights, K, "nucleus", None, block_size=PAGE, kv_cache_bytes=num_pages * page_bytes,
+                           max_model_len=max_model_len, block_table=table)
+    decoder.prepare()
+    return cfg, weights, decoder
+
+
+def _seed_context(decoder, cfg, seed: int = 1) -> None:
+    """K/V ~ N(0, 1) bf16 over the pool, then the request state of a steady round at offset CTX."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kv = decoder.kv_cache
+    for layer in range(kv.shape[0]):
+        kv[layer].copy_(torch.randn(kv[layer].shape, generator=g, device="cuda", dtype=torch.float32).bfloat16())
+    decoder.offset_t.fill_(CTX)
+    decoder.base_t.fill_(2)
+    decoder.out.fill_(-1)
+    decoder.anchor.fill_(17)
+    decoder.pending.copy_(torch.randint(0, cfg.vocab, (K - 1,), generator=g, device="cuda"))
+    decoder._fill_aux(0)
+    torch.cuda.synchronize()
+
+
+def _gemm_graph(decoder, cfg):
+    """A graph of exactly the round's weight GEMM launches (same weights, buffers, epilogues and splits)."""
+    import torch
+
+    from plm import native
+
+    h, w, c = decoder, decoder.weights, cfg
+    ctx = native.Context()
+    rows = decoder.width
+    x = torch.zeros(256, c.hidden, dtype=torch.bfloat16, device="cuda")
+    xi = torch.zeros(256, c.intermediate, dtype=torch.bfloat16, device="cuda")
+    xa = torch.zeros(256, c.num_heads * c.head_dim, dtype=torch.bfloat16, device="cuda")
+    y = torch.zeros(256, max(c.hidden, c.intermediate), dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros(256, c.num_heads * c.head_dim, dtype=torch.bfloat16, device="cuda")
+    positions = torch.arange(rows, dtype=torch.int32, device="cuda") + CTX
+    slots = torch.arange(rows, dtype=torch.int64, device="cuda") + CTX
+    tiles = native.gemm_tiles(native.EPI_LOGITS, c.vocab)
+    logits = torch.zeros(K, c.vocab, dtype=torch.float32, device="cuda")
+    best_val = torch.zeros(tiles, rows, dtype=torch.float32, device="cuda")
+    best_idx = torch.zeros(tiles, rows, dtype=torch.int32, device="cuda")
+    kv = h.kv_cache
+
+    def body():
+        for layer in range(c.num_layers):
+            e = native.GemmEpilogue(kind=native.EPI_QKV_ROPE, q_out=q.data_ptr(), k_cache=kv[layer, 0].data_ptr(),
+                                    v_cache=kv[layer, 1].data_ptr(), positions=positions.data_ptr(),
+                                    slots=slots.data_ptr(), cos_sin=h.cos_sin.data_ptr(), num_heads=c.num_heads,
+                                    num_kv_heads=c.num_kv_heads, head_dim=c.head_dim, page_size=PAGE,
+                                    num_slots=h.num_pages * PAGE, max_pos=h.cos_sin.shape[0])
+            native.gemm(ctx, w.qkv[layer], x, rows, epi=e)
+            native.gemm(ctx, w.o[layer], xa, rows, out=y[:, : c.hidden])
+            native.gemm(ctx, w.gate_up[layer], x, rows, out=y[:, : c.intermediate],
+                        epi=native.GemmEpilogue(kind=native.EPI_SILU_MUL, gate_offset=c.intermediate))
+            native.gemm(ctx, w.down[layer], xi, rows, out=y[:, : c.hidden])
+        native.gemm(ctx, w.lm_head, x, rows,
+                    epi=native.GemmEpilogue(kind=native.EPI_LOGITS, verify_logits=logits.data_ptr(),
+                                            best_val=best_val.data_ptr(), best_idx=best_idx.data_ptr(), n_verify=K,
+                                            vocab=c.vocab))
+
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        body()
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    keep = (ctx, x, xi, xa, y, q, positions, slots, logits, best_val, best_idx)
+    return graph, keep, 4 * c.num_layers + 1
+
+
+def _time_graph(graph, reps: int) -> float:
+    import torch
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / reps
+
+
+def cpu_baseline(weights_gpu, decoder, cfg, rounds: int = 1) -> dict:
+    """The CPU oracle's steady round on the same model, context and state (oracle/model.py), all host threads."""
+    import numpy as np
+    import torch
+
+    from oracle import model as omodel
+    from oracle import voronoi as ov
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    shape = omodel.ModelShape(cfg.num_layers, cfg.hidden, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                              cfg.intermediate, cfg.vocab, cfg.aux_vocab, cfg.num_aux_tokens, cfg.rms_eps,
+                              cfg.rope_theta, decoder.cos_sin.shape[0])
+    named = {key: ([t.cpu() for t in v] if isinstance(v, list) else v.cpu()) for key, v in weights_gpu.named().items()}
+    table = decoder.handle.state()
+    block_table = torch.from_numpy(np.asarray(
+        __import__("plm.native", fromlist=["device_view"]).device_view(table.block_table, (decoder.max_pages,),
+                                                                       torch.int32).cpu().numpy()))
+    om = omodel.OracleModel(shape, named, "bfloat16", PAGE, decoder.num_pages, block_table.numpy(),
+                            cos_sin=decoder.cos_sin.cpu())
+    om.kv.copy_(decoder.kv_cache.float().cpu())
+    oracle = omodel.RoundOracle(om, decoder.table.float().cpu().numpy(), K, "nucleus", None,
+                                ov.VoronoiConfig(cfg.top_m, cfg.shortlist, cfg.rounds, cfg.sweeps),
+                                capacity=decoder.out.numel(), aux_stream=decoder.aux_buf.cpu().numpy())
+    st = oracle.state
+    st.offset, st.base = int(decoder.offset_t), int(decoder.base_t)
+    st.anchor, st.pending = int(decoder.anchor[0]), decoder.pending.cpu().numpy().copy()
+    tokens = 0
+    started = time.perf_counter()
+    for _ in range(rounds):
+        tokens += oracle.round() + 1
+    seconds = time.perf_counter() - started
+    return {"value": tokens / seconds, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{rounds} steady round(s) of the configs[1] workload (1.3B shape, k=7, ctx {CTX}) by the CPU "
+                      f"oracle (torch fp32 forward + numpy Voronoi), {seconds:.2f} s",
+            "seconds_per_round": seconds / rounds}
+
+
+def run_reference(args) -> None:
+    """Reference arm: the CPU oracle round (no GPU kernels of this repository on the timed path)."""
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config(SHAPE)
+    if torch.cuda.is_available():
+        cfg_, weights, decoder = _setup_decoder()
+        _seed_context(decoder, cfg)
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": "the workload is seeded on the GPU box"}))
+        return
+    steps, warm = max(1, min(args.steps, 3)), min(args.warmup, 1)
+    if warm:
+        cpu_baseline(weights, decoder, cfg, rounds=1)
+        _seed_context(decoder, cfg)
+    res = cpu_baseline(weights, decoder, cfg, rounds=steps)
+    line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+            "steps_requested": args.steps, "warmup": warm, "ms_per_step": 1000 * res["seconds_per_round"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "BASELINE configs[1]: single round, PLM-1.3B shape, k=7, ctx 1024, page 16, "
+                                   "shuffled block table; CPU oracle round", "model": SHAPE, "k": K},
+            "cpu_baseline": res, "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_native(args) -> None:
+    import torch
+
+    rank, world, local, dist = _dist()
+    cfg, weights, decoder = _setup_decoder()
+    _seed_context(decoder, cfg)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        decoder.graph.replay()
+    torch.cuda.synchronize()
+    decoder.check()
+    _seed_context(decoder, cfg)
+    base0, ctx0 = int(decoder.base_t), int(decoder.offset_t)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            decoder.graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    decoder.check()
+    tokens = int(decoder.base_t) - base0
+    ctx_mean = (ctx0 + int(decoder.offset_t)) / 2
+    if dist:
+        t = torch.tensor([elapsed_ms, float(tokens)], device="cuda")
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        elapsed_ms, total_tokens = float(mx[0]), float(t[1])
+    else:
+        total_tokens = float(tokens)
+    ms_per_step = elapsed_ms / args.steps
+    value = total_tokens / (elapsed_ms / 1000)
+
+    # dominant kernel: the round's weight GEMMs, timed live
+    graph, keep, gemm_launches = _gemm_graph(decoder, cfg)
+    gemm_ms = _time_graph(graph, max(5, args.steps // 2))
+    bytes_ = round_bytes(cfg, ctx_mean, K)
+    peak, peak_kind = _peaks()
+    achieved = bytes_["weights"] / (gemm_ms / 1000) / 1e9
+    round_achieved = bytes_["total"] / (ms_per_step / 1000) / 1e9
+    del graph, keep
+
+    # end to end through the public API (configs[2] per request)
+    e2e_reqs = max(1, min(3, args.steps // 10 or 1))
+    prompt = torch.randint(0, cfg.vocab, (PROMPT_E2E,), generator=torch.Generator().manual_seed(0)).pin_memory()
+    decoder.generate(prompt, TOKENS_E2E, seed=0, stop_at_eos=False)  # warm-up request
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_tokens, e2e_rounds = 0, 0
+    for i in range(e2e_reqs):
+        res = decoder.generate(prompt, TOKENS_E2E, seed=i, stop_at_eos=False)
+        e2e_tokens += len(res.token_ids)
+        e2e_rounds += res.steady_rounds
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s, float(e2e_tokens)], device="cuda")
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        e2e_s, e2e_tokens = float(mx[0]), float(t[1])
+    e2e_value = e2e_tokens / e2e_s
+
+    cpu = None
+    if rank == 0 and not args.skip_cpu:
+        _seed_context(decoder, cfg)
+        cpu = cpu_baseline(weights, decoder, cfg, rounds=1)
+
+    if rank == 0:
+        launches_per_round = 1 + 7 * cfg.num_layers + 2
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE configs[1]: single-round microbenchmark, PLM-1.3B shape, k=7 "
+                                   "(56 rows), exact match + Voronoi, ctx 1024 (+ accepted tokens), 16-token pages, "
+                                   "shuffled block table, K/V ~ N(0,1)", "model": SHAPE, "k": K, "rows": K + K * K,
+                       "ctx_start": CTX, "ctx_mean": ctx_mean, "page_size": PAGE, "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (3.4 GB weights per round), no flush"},
+            "round_us": 1000 * ms_per_step,
+            "tokens_per_round": total_tokens / (args.steps * world),
+            "roofline": {"bound": "hbm", "kernel": "skinny_gemm_kernel (all weight GEMMs of a round)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": peak_kind, "traffic": None, "bytes_per_round": bytes_["weights"],
+                         "ms_per_round": gemm_ms, "launches_per_round": gemm_launches},
+            "round_roofline": {"bound": "hbm", "achieved": round_achieved, "peak": peak, "unit": "GB/s",
+                               "frac": round_achieved / peak, "bytes_per_round": bytes_},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": PROMPT_E2E * 8,
+                    "d2h_bytes_per_step": int(e2e_rounds / e2e_reqs) * (8 + 8 * 1024) + TOKENS_E2E * 8,
+                    "step": f"one request: {PROMPT_E2E}-token prompt, {TOKENS_E2E} new tokens", "requests": e2e_reqs},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_round * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line))
+    decoder.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", default="native", choices=("native", "reference"))
+    parser.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "native":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

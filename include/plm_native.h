@@ -19,6 +19,14 @@
  *   plm_verify_decode  LogitVoronoiAuxiliary.decode_unmasked (plm/auxiliary.py:67-75) -> Voronoi.assign
  *                   (plm/iterate.py:322-342), nucleus_acceptance / floor_acceptance (plm/decoder.py:71-82) and
  *                   RoundDecoder._epilogue / _round0 bookkeeping (plm/decoder.py:351-365, 275-310, 384).
+ *   plm_attention   FlexAttention under RoundMaskView (plm/mask.py:23-29, installed at plm/decoder.py:148-150,
+ *                   165-169; vllm/v1/attention/backends/flex_attention.py:1070-1205).
+ *   plm_kv_append   reshape_and_cache_flash (flex_attention.py:1047-1068) at the slots of plm/decoder.py:347.
+ *   plm_add_rmsnorm vLLM RMSNorm with residual (fused_add_rms_norm) between the Llama sublayers.
+ *   plm_create / plm_round / plm_round0 / plm_prefill / plm_state
+ *                   RoundDecoder (plm/decoder.py:85-467): construction and state (88-146), the steady round
+ *                   (312-324), round 0 (275-310), the prefill (369-403); RoundConfig.build (plm/rounds.py:71-81)
+ *                   creates one. plm_set_aux_stream replaces _fill_aux (decoder.py:407-412).
  */
 #ifndef PLM_NATIVE_H
 #define PLM_NATIVE_H
@@ -149,8 +157,124 @@ typedef struct plm_verify_desc {
   float* dbg_bias;
   float* dbg_stats;
   int32_t* dbg_sigma;
+  int64_t* dbg_phase_ns; /* [n_rows][8] nanoseconds from kernel start to the end of each phase (diagnostic) */
   plm_bookkeeping book;
 } plm_verify_desc;
+
+/* Paged attention of `rows` query rows at logical KV indices [*offset, *offset + rows) under the round mask:
+ * key kv is visible to row r iff kv < *offset + rows and (kv < *offset or kv - *offset <= depth[r] or
+ * (kv - *offset >= own_start[r] and kv <= *offset + r)) (plm/mask.py:23-29). */
+typedef struct plm_attention_desc {
+  int32_t dtype;
+  const void* q;               /* [rows][num_heads][head_dim] */
+  const void* k_cache;         /* [num_pages][num_kv_heads][page_size][head_dim] */
+  const void* v_cache;
+  const int32_t* block_table;  /* [max_pages] */
+  int32_t max_pages, num_pages, page_size;
+  const int64_t* offset;       /* device scalar */
+  int32_t rows;
+  const int32_t* depth;        /* [rows] */
+  const int32_t* own_start;    /* [rows] */
+  int32_t num_heads, num_kv_heads, head_dim;
+  void* out;                   /* [rows][num_heads * head_dim] */
+  int32_t splits;              /* 0 = choose from max_keys */
+  int64_t max_keys;
+} plm_attention_desc;
+
+/* Scatter K/V rows [rows][num_kv_heads][head_dim] to logical KV indices *offset + r (reshape_and_cache_flash). */
+typedef struct plm_kv_append_desc {
+  int32_t dtype;
+  const void* k;
+  const void* v;
+  void* k_cache;
+  void* v_cache;
+  const int32_t* block_table;
+  int32_t max_pages, num_pages, page_size;
+  const int64_t* offset;
+  int32_t rows, num_kv_heads, head_dim;
+} plm_kv_append_desc;
+
+/* residual <- x + residual; normed <- RMSNorm(residual_fp32) * weight (vLLM fused_add_rms_norm). */
+typedef struct plm_add_rmsnorm_desc {
+  int32_t dtype;
+  const void* x;
+  void* residual;
+  void* normed;
+  const void* weight;
+  int32_t rows, hidden;
+  float eps;
+  int32_t gather_row; /* -1: none; else also copy that normed row to `gathered` */
+  void* gathered;
+} plm_add_rmsnorm_desc;
+
+/* ---- round engine (one handle = one request stream on one GPU, batch 1) ---- */
+typedef struct plm_handle plm_handle;
+
+/* Llama-architecture PLM (vLLM llama.py:81-314 with the auxiliary scheme of plm/auxiliary.py:17-75). */
+typedef struct plm_model_desc {
+  int32_t dtype;
+  int32_t num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate;
+  int32_t vocab;          /* text vocabulary: logits width */
+  int32_t aux_vocab;      /* auxiliary vocabulary size A (power of two, 32..4096) */
+  int32_t num_aux_tokens; /* ids in [vocab, vocab + num_aux_tokens) embed auxiliary vectors */
+  float rms_eps;
+  int32_t max_pos;        /* rows of the cos/sin table */
+  int32_t top_m, shortlist, rounds, sweeps;
+  double epsilon, refocus, endpoint;
+} plm_model_desc;
+
+/* Borrowed device pointers; they must stay valid for the handle's lifetime. */
+typedef struct plm_weight_ptrs {
+  const void* embed;      /* [>= vocab][hidden] */
+  const void* lm_head;    /* [>= vocab][hidden] */
+  const void* final_norm; /* [hidden] */
+  const void* aux_vocab;  /* [aux_vocab][hidden] */
+  const void* mask_aux;   /* [hidden] */
+  const void* cos_sin;    /* [max_pos][head_dim] */
+  const void* const* qkv; /* per layer [(heads + 2 kv_heads) * head_dim][hidden] */
+  const void* const* o;   /* per layer [hidden][heads * head_dim] */
+  const void* const* gate_up; /* per layer [2 intermediate][hidden] */
+  const void* const* down;    /* per layer [hidden][intermediate] */
+  const void* const* input_norm;
+  const void* const* post_norm;
+  const void* table;      /* optional [vocab][aux_vocab] Voronoi table; NULL: built at creation */
+} plm_weight_ptrs;
+
+typedef struct plm_round_desc {
+  int32_t k;              /* verify rows; the round has k + k^2 rows */
+  int32_t rule;           /* enum plm_accept_rule */
+  float threshold;        /* nucleus mass (<= 0: exact match) or probability floor */
+  int32_t page_size;
+  int32_t num_pages;      /* physical pages in the KV pool */
+  int32_t max_pages;      /* block-table entries (logical pages of one request) */
+  int64_t out_capacity;   /* output token buffer */
+  int64_t seq_capacity;   /* accepted-count record (0: 1 << 17) */
+  int64_t aux_len;        /* auxiliary cell stream (0: 8192) */
+  int32_t max_prefill;    /* rows per prefill chunk, 1..256 */
+} plm_round_desc;
+
+/* Device addresses of a handle's state, for readers and for seeding synthetic workloads. */
+typedef struct plm_state_ptrs {
+  int64_t* out;
+  int64_t* base;
+  int64_t* offset;
+  int64_t* anchor;
+  int64_t* pending;
+  int64_t* round_sequence;
+  int64_t* sequence_step;
+  int64_t* aux_buf;
+  int32_t* block_table;
+  float* verify_logits;  /* [k][vocab] */
+  float* best_val;       /* [lm_tiles][width] */
+  int32_t* best_idx;
+  int64_t* verify;
+  int32_t* flags;
+  void* hidden_normed;   /* [row_capacity][hidden]: final-norm output of the last forward */
+  void* kv_cache;        /* [layers][2][num_pages][kv_heads][page_size][head_dim] */
+  void* table;
+  int64_t out_capacity, seq_capacity, aux_len, plane_elems;
+  int32_t width, lm_tiles, row_capacity;
+} plm_state_ptrs;
 
 /* ---- context ---- */
 int plm_ctx_create(plm_ctx** out);
@@ -164,6 +288,24 @@ int plm_gemm_tiles(int32_t kind, int32_t n_out, int32_t gate_offset, int32_t* ti
 int plm_gemm(plm_ctx* ctx, const plm_gemm_desc* desc, void* stream);
 /* Verify decode + acceptance + (optionally) the round bookkeeping, one CTA per row. */
 int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* desc, void* stream);
+int plm_attention(plm_ctx* ctx, const plm_attention_desc* desc, void* stream);
+int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* desc, void* stream);
+int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* desc, void* stream);
+
+/* ---- round engine ---- */
+int plm_create(const plm_model_desc* model, const plm_weight_ptrs* weights, const plm_round_desc* round,
+               plm_handle** out);
+int plm_destroy(plm_handle* h);
+int plm_set_block_table(plm_handle* h, const int32_t* table_host, int32_t n);
+int plm_set_aux_stream(plm_handle* h, const int64_t* cells, int64_t n, void* stream);
+int plm_load_prompt(plm_handle* h, const int64_t* ids, int64_t n, void* stream);
+/* Causal prefill of the loaded prompt, then the first token and the request state of round 0. */
+int plm_prefill(plm_handle* h, void* stream);
+int plm_round0(plm_handle* h, void* stream);
+/* One steady round: forward of k + k^2 rows, lm_head, verify decode, acceptance, commit. Graph-capturable. */
+int plm_round(plm_handle* h, void* stream);
+int plm_state(plm_handle* h, plm_state_ptrs* out);
+int plm_check(plm_handle* h, int32_t* device_error);
 
 /* ---- diagnostics ---- */
 int plm_abi_version(void);

@@ -5,12 +5,12 @@
 // Keys are visited in tiles of 64: each tile's K and V rows are gathered page by page through the block table
 // with 16-byte cp.async into XOR-swizzled shared memory (double buffered), S = Q K^T and O += P V run on tensor
 // cores (mma.m16n8k16 bf16, fp32 accumulation; P is rounded to bf16 for the second product), and the softmax is
-// online in base 2. Key kv is visible to row r (logical query offset + r) iff
+// online in base 2. The KV splits of one (head, query tile) form a thread-block cluster whose partial results are
+// combined through distributed shared memory. Key kv is visible to row r (logical query offset + r) iff
 //     kv < offset + rows  and  (kv < offset  or  kv - offset <= depth[r]
 //                                 or  (kv - offset >= own_start[r]  and  kv <= offset + r)),
 // which is RoundMaskView for a round (depth / own_start from round_layout) and plain causal attention for a
-// prefill chunk (depth[r] = r). With more than one split every CTA writes an unnormalised partial (O, m, l) and
-// the last CTA of the (head, query tile) combines the splits in split order.
+// prefill chunk (depth[r] = r).
 #include "attention.h"
 #include "common.cuh"
 #include "runtime.h"
@@ -70,7 +70,6 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* kbuf[2] = {smem, smem + TILE_BYTES};
   uint8_t* vbuf[2] = {smem + 2 * TILE_BYTES, smem + 3 * TILE_BYTES};
-  __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
@@ -265,62 +264,77 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
     return;
   }
 
-  // ---- split partials, combined by the last CTA of (head, query tile) ----
-  const int q_tiles = gridDim.z;
-  const size_t slot = (size_t(head) * q_tiles + qt) * a.splits + split;
-  float* po = a.partial + slot * kQRowsPerCta * HD;
-  float* pml = a.partial_ml + slot * kQRowsPerCta * 2;
+  // ---- split partials, combined over the cluster of the (head, query tile) ----
+  // Each CTA leaves its unnormalised partial (O, m, l) in its own shared memory (the K/V buffers are free now);
+  // after a cluster barrier rank r combines rows [r * 64 / S, (r + 1) * 64 / S) over all ranks in rank order through
+  // distributed shared memory; a second barrier keeps every partial alive until all rows are combined.
+  float* po = reinterpret_cast<float*>(smem);                              // [64][HD]
+  float* pml = reinterpret_cast<float*>(smem + kQRowsPerCta * HD * 4);     // [64][2]
+  float* wts = pml + kQRowsPerCta * 2;                                     // [64 / S rows][S] weights, then 1/L
   const int lr0 = warp * 16 + gq, lr1 = lr0 + 8;
 #pragma unroll
   for (int j = 0; j < HD / 8; ++j) {
     const int col = j * 8 + 2 * tq;
-    __stcg(reinterpret_cast<float2*>(po + lr0 * HD + col), make_float2(o[j][0], o[j][1]));
-    __stcg(reinterpret_cast<float2*>(po + lr1 * HD + col), make_float2(o[j][2], o[j][3]));
+    *reinterpret_cast<float2*>(po + lr0 * HD + col) = make_float2(o[j][0], o[j][1]);
+    *reinterpret_cast<float2*>(po + lr1 * HD + col) = make_float2(o[j][2], o[j][3]);
   }
   if (tq == 0) {
-    __stcg(reinterpret_cast<float2*>(pml + lr0 * 2), make_float2(m0, l0));
-    __stcg(reinterpret_cast<float2*>(pml + lr1 * 2), make_float2(m1, l1));
+    *reinterpret_cast<float2*>(pml + lr0 * 2) = make_float2(m0, l0);
+    *reinterpret_cast<float2*>(pml + lr1 * 2) = make_float2(m1, l1);
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int c = head * q_tiles + qt;
-    const int old = atomicAdd(a.counters + c, 1);
-    s_last = old == a.splits - 1 ? 1 : 0;
-    if (old >= a.splits) record_error(a.err, kErrTimeoutSplit);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (tid == 0) a.counters[head * q_tiles + qt] = 0;
-
-  const size_t first = (size_t(head) * q_tiles + qt) * a.splits;
-  const int row = tid >> 1;
-  const int grow = qt * kQRowsPerCta + row;
-  const int c_begin = (tid & 1) * (HD / 2);
-  float mmax = -INFINITY;
-  for (int sp = 0; sp < a.splits; ++sp) mmax = fmaxf(mmax, __ldcg(a.partial_ml + (first + sp) * kQRowsPerCta * 2 + row * 2));
-  float lsum = 0.f;
-  for (int sp = 0; sp < a.splits; ++sp) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.partial_ml + (first + sp) * kQRowsPerCta * 2 + row * 2));
-    const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mmax);
-    lsum += w * ml.y;
-  }
-  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-  if (grow < a.rows) {
-    for (int c = c_begin; c < c_begin + HD / 2; c += 2) {
-      float acc0 = 0.f, acc1 = 0.f;
-      for (int sp = 0; sp < a.splits; ++sp) {
-        const float mm = __ldcg(a.partial_ml + (first + sp) * kQRowsPerCta * 2 + row * 2);
-        const float w = mm == -INFINITY ? 0.f : exp2f(mm - mmax);
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(a.partial + (first + sp) * kQRowsPerCta * HD + row * HD + c));
-        acc0 += w * v.x;
-        acc1 += w * v.y;
+  cluster_sync();
+  const int S = a.splits;
+  const uint32_t rank = cluster_rank();
+  const int rpc = kQRowsPerCta / S;
+  const int row_begin = int(rank) * rpc;
+  if (tid < rpc) {
+    const int row = row_begin + tid;
+    float ms[8], ls[8], mmax = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < 8; ++sp) {
+      ms[sp] = -INFINITY;
+      ls[sp] = 0.f;
+      if (sp < S) {
+        const float2 ml = ld_dsmem_f32x2(cluster_map(pml + row * 2, uint32_t(sp)));
+        ms[sp] = ml.x;
+        ls[sp] = ml.y;
+        mmax = fmaxf(mmax, ml.x);
       }
+    }
+    float lsum = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < 8; ++sp) {
+      const float w = (sp < S && ms[sp] != -INFINITY) ? exp2f(ms[sp] - mmax) : 0.f;
+      if (sp < S) wts[tid * (S + 1) + sp] = w;
+      lsum += w * ls[sp];
+    }
+    wts[tid * (S + 1) + S] = lsum > 0.f ? 1.f / lsum : 0.f;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < rpc * (HD / 2); idx += kAttnThreads) {
+    const int lr = idx / (HD / 2), c = (idx % (HD / 2)) * 2;
+    const int row = row_begin + lr;
+    const uint32_t off = uint32_t(row * HD + c) * 4u;
+    float2 part[8];
+#pragma unroll
+    for (int sp = 0; sp < 8; ++sp)
+      part[sp] = sp < S ? ld_dsmem_f32x2(cluster_map(po, uint32_t(sp)) + off) : make_float2(0.f, 0.f);
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < 8; ++sp) {
+      if (sp < S) {
+        const float w = wts[lr * (S + 1) + sp];
+        acc0 += w * part[sp].x;
+        acc1 += w * part[sp].y;
+      }
+    }
+    const int grow = qt * kQRowsPerCta + row;
+    const float inv = wts[lr * (S + 1) + S];
+    if (grow < a.rows)
       *reinterpret_cast<__nv_bfloat162*>(out + size_t(grow) * out_stride + head * HD + c) =
           __floats2bfloat162_rn(acc0 * inv, acc1 * inv);
-    }
   }
+  cluster_sync();
 }
 
 template <int HD>
@@ -334,7 +348,8 @@ int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool p
     if (st != PLM_OK) return st;
     attr = true;
   }
-  return check_cuda(launch(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl, a),
+  return check_cuda(launch_ex(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl,
+                              a.splits, a),
                     "round_attention_kernel");
 }
 
@@ -342,11 +357,10 @@ int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool p
 
 int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys) {
   const int ctas = num_heads * q_tiles;
-  int splits = (2 * num_sms + ctas - 1) / ctas;
   const int max_tiles = int((max_keys + kKeysPerTile - 1) / kKeysPerTile);
-  if (splits > max_tiles) splits = max_tiles;
-  if (splits > 64) splits = 64;
-  return splits < 1 ? 1 : splits;
+  int splits = 1;
+  while (splits < 8 && ctas * splits < 2 * num_sms && 2 * splits <= max_tiles) splits *= 2;
+  return splits;
 }
 
 int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
@@ -358,12 +372,8 @@ int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
     return fail(PLM_ERR_INVALID, "attention: null operand");
   const int q_tiles = (a.rows + kQRowsPerCta - 1) / kQRowsPerCta;
   if (a.splits < 1) a.splits = 1;
-  const size_t need = size_t(a.num_heads) * q_tiles * a.splits * kQRowsPerCta * (a.head_dim + 2);
-  if (a.splits > 1 && (need > ctx->partial_floats || a.num_heads * q_tiles > ctx->n_counters - 1))
-    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits exceed the context scratch", a.splits);
-  a.partial = ctx->partial;
-  a.partial_ml = ctx->partial + size_t(a.num_heads) * q_tiles * a.splits * kQRowsPerCta * a.head_dim;
-  a.counters = ctx->counters;
+  if (a.splits > 8 || (a.splits & (a.splits - 1)) != 0)
+    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits (a power of two <= 8)", a.splits);
   a.err = ctx->err;
   return a.head_dim == 128 ? launch_attention<128>(a, q_tiles, stream, pdl)
                            : launch_attention<64>(a, q_tiles, stream, pdl);

@@ -182,6 +182,34 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, float (&v)[32]) {
 }
 
 // ----------------------------------------------------------------------------------------------------------------
+// Thread-block clusters: rank, barrier and distributed shared memory loads (no TMA, no multicast).
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster must execute this (it is a hardware barrier, like __syncthreads).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address of `local` (an address in this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_dsmem_f32x2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+
+// ----------------------------------------------------------------------------------------------------------------
 // Element helpers: the model's storage dtype is bf16 or f16; arithmetic is fp32.
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);

@@ -1,0 +1,232 @@
+// Row-wise kernels of the round: the prologue (ids, auxiliary cells, embeddings, rotary positions, KV slots)
+// fused with the first RMSNorm, the residual-add RMSNorm between sublayers, and a standalone paged KV append.
+#include "common.cuh"
+#include "elementwise.h"
+#include "runtime.h"
+
+namespace plm {
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr int kMaxPerThread = 16;  // hidden <= 4096
+
+__device__ __forceinline__ float block_sum_rows(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = 0.f;
+  for (int w = 0; w < int(blockDim.x >> 5); ++w) r += red[w];
+  return r;
+}
+
+// One CTA per row. Writes residual (the embedding, model dtype) and normed = RMSNorm(embedding) * w.
+//   ids: steady round [anchor, pending..., V x k^2]; round 0 [anchor, V x (W-1)]; prefill chunk prompt[offset + r].
+//   Rows whose id lies in [V, V + num_aux_tokens) take auxiliary_vocabulary[min(cell, A - 1)] (mask_auxiliary if
+//   the cell is the sentinel A), all others embed_tokens[clamp(id, 0, V - 1)] (plm/decoder.py:264-268, 331-349;
+//   plm/auxiliary.py:50-54). The row's rotary position is offset + rel_positions[r] and its KV slot the physical
+//   slot of logical index offset + r through the block table (plm/decoder.py:340, 347).
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueArgs a) {
+  __shared__ float red[32];
+  __shared__ int64_t s_id, s_cell;
+  const int r = blockIdx.x, tid = threadIdx.x;
+  grid_dependency_wait();
+  allow_dependents();
+  const int64_t offset = *a.offset;
+  if (tid == 0) {
+    int64_t id = a.vocab, cell = a.aux;  // proposal placeholder; masked sentinel cell
+    int64_t position = offset + (a.rel_positions != nullptr ? a.rel_positions[r] : r);
+    if (a.mode == kProloguePrefill) {
+      const int64_t p = offset + r;
+      if (p < 0 || p >= a.prompt_cap) {
+        record_error(a.err, kErrBadIndex);
+        id = 0;
+      } else {
+        id = a.prompt[p];
+      }
+    } else {
+      if (r == 0) id = *a.anchor;
+      else if (a.mode == kPrologueSteady && r < a.k) id = a.pending[r - 1];
+      const int64_t rel_aux = a.rel_aux[r];
+      if (rel_aux >= 0) {
+        const int64_t index = *a.base + rel_aux;
+        if (index < 0 || index >= a.aux_len) {
+          record_error(a.err, kErrBadIndex);
+          cell = 0;
+        } else {
+          cell = a.aux_buf[index];
+        }
+      }
+    }
+    if (position < 0 || position >= a.max_pos) {
+      record_error(a.err, kErrBadIndex);
+      position = 0;
+    }
+    a.positions[r] = int32_t(position);
+    const int64_t logical = offset + r;
+    const int64_t lp = logical / a.page_size;
+    const int page = (logical >= 0 && lp < a.max_pages) ? a.block_table[lp] : -1;
+    if (page < 0 || page >= a.num_pages) {
+      record_error(a.err, kErrBadIndex);
+      a.slots[r] = -1;
+    } else {
+      a.slots[r] = int64_t(page) * a.page_size + logical % a.page_size;
+    }
+    s_id = id;
+    s_cell = cell;
+  }
+  __syncthreads();
+  const int64_t id = s_id;
+  const bool aux_row = id >= a.vocab && id < int64_t(a.vocab) + a.num_aux_tokens;
+  const T* src;
+  if (aux_row) {
+    const int64_t cell = s_cell;
+    if (cell == a.aux) {
+      src = reinterpret_cast<const T*>(a.mask_aux);
+    } else {
+      const int64_t c = cell < 0 ? 0 : (cell > a.aux - 1 ? a.aux - 1 : cell);
+      src = reinterpret_cast<const T*>(a.aux_vocab) + size_t(c) * a.hidden;
+    }
+  } else {
+    const int64_t tok = id < 0 ? 0 : (id > a.vocab - 1 ? a.vocab - 1 : id);
+    src = reinterpret_cast<const T*>(a.embed) + size_t(tok) * a.hidden;
+  }
+  T* res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
+  T* nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
+  const T* w = reinterpret_cast<const T*>(a.norm_weight);
+  float v[kMaxPerThread];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxPerThread; ++j) {
+    const int i = tid + j * kRowThreads;
+    v[j] = 0.f;
+    if (i < a.hidden) {
+      const T e = src[i];
+      res[i] = e;
+      v[j] = to_f32<T>(e);
+      ss += v[j] * v[j];
+    }
+  }
+  ss = block_sum_rows(ss, red);
+  const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
+#pragma unroll
+  for (int j = 0; j < kMaxPerThread; ++j) {
+    const int i = tid + j * kRowThreads;
+    if (i < a.hidden) nrm[i] = from_f32<T>(round_to<T>(v[j] * rstd) * to_f32<T>(w[i]));
+  }
+}
+
+// One CTA per row: residual <- x + residual; normed <- RMSNorm(x + residual) * w (vLLM fused_add_rms_norm:
+// the sum is formed in fp32, stored rounded as the new residual, and normalised unrounded). With gather_row >= 0
+// the normed row `gather_row` is also copied to `gathered` (the prefill's last prompt row).
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs a) {
+  __shared__ float red[32];
+  const int r = blockIdx.x, tid = threadIdx.x;
+  grid_dependency_wait();
+  allow_dependents();
+  const T* x = reinterpret_cast<const T*>(a.x) + size_t(r) * a.hidden;
+  T* res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
+  T* nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
+  const T* w = reinterpret_cast<const T*>(a.weight);
+  T* gathered = (r == a.gather_row && a.gathered != nullptr) ? reinterpret_cast<T*>(a.gathered) : nullptr;
+  float v[kMaxPerThread];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxPerThread; ++j) {
+    const int i = tid + j * kRowThreads;
+    v[j] = 0.f;
+    if (i < a.hidden) {
+      v[j] = to_f32<T>(x[i]) + to_f32<T>(res[i]);
+      res[i] = from_f32<T>(v[j]);
+      ss += v[j] * v[j];
+    }
+  }
+  ss = block_sum_rows(ss, red);
+  const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
+#pragma unroll
+  for (int j = 0; j < kMaxPerThread; ++j) {
+    const int i = tid + j * kRowThreads;
+    if (i < a.hidden) {
+      const T out = from_f32<T>(round_to<T>(v[j] * rstd) * to_f32<T>(w[i]));
+      nrm[i] = out;
+      if (gathered != nullptr) gathered[i] = out;
+    }
+  }
+}
+
+// Scatter K and V rows [rows][kv_heads][head_dim] to logical KV indices offset + r through the block table
+// (the write vLLM's reshape_and_cache_flash performs at plm/decoder.py:347's slots). One warp per (row, kv head),
+// 16-byte stores.
+template <typename T>
+__global__ void kv_append_kernel(const KvAppendArgs a) {
+  grid_dependency_wait();
+  allow_dependents();
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= a.rows * a.num_kv_heads) return;
+  const int r = warp_global / a.num_kv_heads, g = warp_global % a.num_kv_heads;
+  const int64_t logical = *a.offset + r;
+  const int64_t lp = logical / a.page_size;
+  const int page = (logical >= 0 && lp < a.max_pages) ? a.block_table[lp] : -1;
+  if (page < 0 || page >= a.num_pages) {
+    if (lane == 0) record_error(a.err, kErrBadIndex);
+    return;
+  }
+  const size_t dst = ((size_t(page) * a.num_kv_heads + g) * a.page_size + size_t(logical % a.page_size)) * a.head_dim;
+  const size_t src = (size_t(r) * a.num_kv_heads + g) * a.head_dim;
+  const int vecs = a.head_dim / 8;  // 16-byte vectors of 8 elements
+  for (int c = lane; c < vecs; c += 32) {
+    reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.k_cache) + dst)[c] =
+        reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.k) + src)[c];
+    reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.v_cache) + dst)[c] =
+        reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.v) + src)[c];
+  }
+}
+
+}  // namespace
+
+int prologue_launch(const PrologueArgs& a, int rows, cudaStream_t stream, bool pdl) {
+  if (a.hidden > kRowThreads * kMaxPerThread) return fail(PLM_ERR_UNSUPPORTED, "prologue: hidden %d", a.hidden);
+  return check_cuda(launch(embed_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
+                    "embed_norm_kernel");
+}
+
+int add_norm_launch(const AddNormArgs& a, int rows, cudaStream_t stream, bool pdl) {
+  if (a.hidden > kRowThreads * kMaxPerThread) return fail(PLM_ERR_UNSUPPORTED, "add_norm: hidden %d", a.hidden);
+  return check_cuda(launch(add_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
+                    "add_norm_kernel");
+}
+
+int kv_append_launch(const KvAppendArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.head_dim % 8 != 0) return fail(PLM_ERR_UNSUPPORTED, "kv_append: head_dim %d", a.head_dim);
+  const int warps = a.rows * a.num_kv_heads;
+  const int blocks = (warps * 32 + 255) / 256;
+  return check_cuda(launch(kv_append_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream, pdl, a),
+                    "kv_append_kernel");
+}
+
+}  // namespace plm
+
+using namespace plm;
+
+extern "C" int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* d, void* stream) {
+  if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_kv_append: null argument");
+  if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_kv_append: only bf16 is built");
+  if (!d->k || !d->v || !d->k_cache || !d->v_cache || !d->block_table || !d->offset || d->rows < 1)
+    return fail(PLM_ERR_INVALID, "plm_kv_append: null operand or no rows");
+  KvAppendArgs a = {d->k,         d->v,         d->k_cache,   d->v_cache,  d->block_table, d->max_pages,
+                    d->num_pages, d->page_size, d->offset,    d->rows,     d->num_kv_heads, d->head_dim,
+                    ctx->err};
+  return kv_append_launch(a, static_cast<cudaStream_t>(stream), true);
+}
+
+extern "C" int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* d, void* stream) {
+  if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null argument");
+  if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_add_rmsnorm: only bf16 is built");
+  if (!d->x || !d->residual || !d->normed || !d->weight || d->rows < 1 || d->hidden < 1)
+    return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null operand");
+  AddNormArgs a = {d->x, d->residual, d->normed, d->weight, d->hidden, d->eps, d->gather_row, d->gathered};
+  return add_norm_launch(a, d->rows, static_cast<cudaStream_t>(stream), true);
+}

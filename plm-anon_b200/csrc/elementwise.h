@@ -1,0 +1,66 @@
+// Argument blocks of the row-wise kernels (elementwise.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace plm {
+
+enum PrologueMode : int { kPrologueSteady = 0, kPrologueRound0 = 1, kProloguePrefill = 2 };
+
+struct PrologueArgs {
+  int mode;
+  int k;
+  int vocab, aux, num_aux_tokens, hidden;
+  float eps;
+  const int64_t* offset;       // device scalar: logical KV index of row 0
+  const int64_t* base;         // device scalar: output position of verify row 0
+  const int64_t* anchor;
+  const int64_t* pending;      // [k - 1]
+  const int64_t* rel_positions;  // [rows] (nullable: r)
+  const int64_t* rel_aux;      // [rows] (-1: no auxiliary cell)
+  const int64_t* aux_buf;
+  int64_t aux_len;
+  const int64_t* prompt;       // prefill: prompt token ids
+  int64_t prompt_cap;
+  const void* embed;
+  const void* aux_vocab;
+  const void* mask_aux;
+  const void* norm_weight;     // layer 0 input_layernorm
+  const int32_t* block_table;
+  int max_pages, num_pages, page_size, max_pos;
+  void* residual;              // [rows][hidden]
+  void* normed;                // [rows][hidden]
+  int32_t* positions;          // [rows]
+  int64_t* slots;              // [rows]
+  int* err;
+};
+
+struct AddNormArgs {
+  const void* x;
+  void* residual;
+  void* normed;
+  const void* weight;
+  int hidden;
+  float eps;
+  int gather_row;  // -1: none
+  void* gathered;
+};
+
+struct KvAppendArgs {
+  const void* k;  // [rows][num_kv_heads][head_dim]
+  const void* v;
+  void* k_cache;  // [num_pages][num_kv_heads][page_size][head_dim]
+  void* v_cache;
+  const int32_t* block_table;
+  int max_pages, num_pages, page_size;
+  const int64_t* offset;
+  int rows, num_kv_heads, head_dim;
+  int* err;
+};
+
+int prologue_launch(const PrologueArgs& a, int rows, cudaStream_t stream, bool pdl);
+int add_norm_launch(const AddNormArgs& a, int rows, cudaStream_t stream, bool pdl);
+int kv_append_launch(const KvAppendArgs& a, cudaStream_t stream, bool pdl);
+
+}  // namespace plm

@@ -41,8 +41,6 @@ GemmArgs make_args(plm_ctx* ctx, const plm_gemm_desc& d, int tiles, int splits, 
   a.gate_offset = d.epi.gate_offset;
   a.out = d.out;
   a.ldo = d.ldo;
-  a.partial = ctx->partial;
-  a.counters = ctx->counters;
   a.err = ctx->err;
   const plm_gemm_epilogue& e = d.epi;
   a.qkv = QkvEpilogue{e.q_out,     e.k_cache,      e.v_cache,  e.positions, e.slots,     e.cos_sin,
@@ -67,24 +65,16 @@ int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, c
   }
   const int tiles = tiles_for(EPI, d.n_out, d.epi.gate_offset);
   const int total_kb = d.k / kGemmBK;
-  int splits = 1, kb_per = total_kb;
-  if (d.splits > 0) {
-    splits = d.splits < total_kb ? d.splits : total_kb;
-    kb_per = (total_kb + splits - 1) / splits;
-    splits = (total_kb + kb_per - 1) / kb_per;
-  } else {
-    plan_splits(tiles, total_kb, ctx->num_sms, SMEM <= 113 * 1024 ? 2 : 1, &splits, &kb_per);
-  }
-  // Keep the fp32 partials inside the context's scratch.
-  while (splits > 1 && size_t(splits) * tiles * NTOK * 128 > ctx->partial_floats) {
-    kb_per *= 2;
-    splits = (total_kb + kb_per - 1) / kb_per;
-  }
-  if (splits > 1 && tiles > ctx->n_counters)
-    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d tiles exceed the context's %d split counters", tiles,
-                ctx->n_counters);
+  int splits = d.splits > 0 ? d.splits : gemm_cluster_splits(tiles, total_kb, ctx->num_sms);
+  if (splits > 8 || (splits & (splits - 1)) != 0 || splits > total_kb)
+    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits (a power of two <= 8 and <= k/64)", splits);
+  if (NTOK > 128) splits = 1;  // the staging area holds no reduced slice for the widest tiles
+  const int kb_per = (total_kb + splits - 1) / splits;
+  if (kb_per * (splits - 1) >= total_kb)
+    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits leave an empty split of %d k-blocks", splits, total_kb);
   GemmArgs args = make_args(ctx, d, tiles, splits, kb_per);
-  return check_cuda(launch(kernel, dim3(tiles, splits), dim3(kGemmThreads), SMEM, stream, pdl, *map_w, *map_x, args),
+  return check_cuda(launch_ex(kernel, dim3(tiles, splits), dim3(kGemmThreads), SMEM, stream, pdl, splits, *map_w,
+                              *map_x, args),
                     "skinny_gemm_kernel launch");
 }
 

@@ -5,11 +5,13 @@
 // MMA's M side (TMEM lanes = output features) and the round rows are its N side (TMEM columns = rows), so one
 // tcgen05.mma.kind::f16 of 128 x NTOK x 16 covers the whole round. Weight tiles (128 rows x 64 k, 16 KB) and
 // row tiles (NTOK rows x 64 k) are staged by TMA with the 128-byte swizzle into a STAGES-deep ring; one thread
-// issues TMA, one thread issues MMAs, and the four warps read the accumulator back with tcgen05.ld.
+// issues TMA (warp 0), one thread issues MMAs (warp 1), and the four warps read the accumulator back with
+// tcgen05.ld.
 //
-// Work is split over (output tile, k-split). With more than one split each CTA writes an fp32 partial tile to
-// scratch and the last CTA to arrive for a tile (arrival counter) sums the partials in split order, so the
-// result does not depend on arrival order. That CTA then runs the fused epilogue:
+// Work is split over (output tile, k-split). The k-splits of a tile run as one thread-block cluster: each CTA keeps
+// its fp32 partial tile in its own shared memory and, after a cluster barrier, reduces one slice of the token
+// columns over all ranks in rank order through distributed shared memory, so the result does not depend on timing
+// and no global scratch is involved. Each CTA then runs the fused epilogue on its slice:
 //   kEpiStore    plain store in the model dtype;
 //   kEpiSiluMul  the gate_up projection with SiLU(gate) * up fused (tile = 64 gate rows + the matching 64 up rows);
 //   kEpiQkvRope  the qkv projection with neox RoPE on q and k, q written out, k and v scattered into the paged cache;
@@ -69,8 +71,6 @@ struct GemmArgs {
   int gate_offset;  // kEpiSiluMul: first row of the up half inside W (the intermediate size)
   void* out;
   int ldo;
-  float* partial;   // split-K scratch [splits][n_tiles][NTOK][128]
-  int* counters;    // [n_tiles] arrival counters, zero between launches
   int* err;
   QkvEpilogue qkv;
   LogitsEpilogue logits;
@@ -91,9 +91,18 @@ struct GemmShape {
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment for the 128-byte swizzle");
 };
 
+// Bytes before the barriers: the TMA ring, or after the main loop the fp32 staging tile plus (with a split) the
+// reduced slice of at most half the columns, whichever is larger. Splits are only used for NTOK <= 128.
+template <int NTOK, int STAGES>
+constexpr int gemm_bar_offset() {
+  constexpr int ring = STAGES * GemmShape<NTOK>::STAGE_BYTES;
+  constexpr int staging = (NTOK <= 128 ? NTOK + NTOK / 2 : NTOK) * kStagePad * 4;
+  return ((ring > staging ? ring : staging) + 7) & ~7;
+}
+
 template <int NTOK, int STAGES>
 constexpr int gemm_smem_bytes() {
-  return STAGES * GemmShape<NTOK>::STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers, flags*/;
+  return gemm_bar_offset<NTOK, STAGES>() + 1024 /*alignment slack*/ + 256 /*barriers, flags*/;
 }
 
 template <typename T, int NTOK, int STAGES, int EPI>
@@ -102,11 +111,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                        const GemmArgs args) {
   using Shape = GemmShape<NTOK>;
   constexpr uint32_t IDESC = umma_idesc_f16(128, NTOK, std::is_same<T, __nv_bfloat16>::value);
-  static_assert(NTOK * kStagePad * 4 <= STAGES * Shape::STAGE_BYTES, "staging tile must fit in the ring");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Shape::STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + gemm_bar_offset<NTOK, STAGES>());
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* done_bar = empty_bar + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -138,12 +146,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *tmem_slot;
   allow_dependents();
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    tma_prefetch_map(&map_w);
-    tma_prefetch_map(&map_x);
-    const uint64_t pol_w = l2_policy_evict_first();
-    const uint64_t pol_x = l2_policy_evict_last();
+  // Role warps are kept converged: lane 0 waits and issues, the other lanes park in __shfl_sync, so no lane spins
+  // in a barrier wait beside the issuing lane.
+  auto warp_wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(bar, parity, args.err, code) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  };
+  if (warp == 0) {
+    // ---------------- TMA producer warp ----------------
+    uint64_t pol_w = 0, pol_x = 0;
+    if (lane == 0) {
+      tma_prefetch_map(&map_w);
+      tma_prefetch_map(&map_x);
+      pol_w = l2_policy_evict_first();
+      pol_x = l2_policy_evict_last();
+    }
     auto load_w = [&](int s, int kb) {
       uint8_t* a = smem + s * Shape::STAGE_BYTES;
       if (EPI == kEpiSiluMul) {
@@ -159,102 +177,80 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tma_load_2d(b, &map_x, full_bar + s, kb * kGemmBK, 0, pol_x);
     };
     const int pre = nk < STAGES ? nk : STAGES;
-    for (int i = 0; i < pre; ++i) {
-      mbar_arrive_expect_tx(full_bar + i, Shape::STAGE_BYTES);
-      load_w(i, kb_begin + i);
+    if (lane == 0) {
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(full_bar + i, Shape::STAGE_BYTES);
+        load_w(i, kb_begin + i);
+      }
     }
     grid_dependency_wait();  // the row operand is written by the previous kernel
-    for (int i = 0; i < pre; ++i) load_x(i, kb_begin + i);
+    if (lane == 0)
+      for (int i = 0; i < pre; ++i) load_x(i, kb_begin + i);
     int issued = pre;
     for (int i = STAGES; i < nk; ++i) {
       const int s = i % STAGES;
-      if (!mbar_wait(empty_bar + s, ((i / STAGES) - 1) & 1, args.err, kErrTimeoutEmpty)) {
-        // Stages already issued still land; the MMA issuer drains them before the CTA exits.
-        flags[0] = 1;
+      if (!warp_wait(empty_bar + s, ((i / STAGES) - 1) & 1, kErrTimeoutEmpty)) {
+        // Stages already issued still land; they are drained before the CTA reuses shared memory.
+        if (lane == 0) flags[0] = 1;
         break;
       }
-      mbar_arrive_expect_tx(full_bar + s, Shape::STAGE_BYTES);
-      load_w(s, kb_begin + i);
-      load_x(s, kb_begin + i);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full_bar + s, Shape::STAGE_BYTES);
+        load_w(s, kb_begin + i);
+        load_x(s, kb_begin + i);
+      }
       issued = i + 1;
     }
-    flags[2] = issued;
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
+    if (lane == 0) flags[2] = issued;
+  } else if (warp == 1) {
+    // ---------------- MMA warp ----------------
     int consumed = 0;
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES;
-      if (!mbar_wait(full_bar + s, (i / STAGES) & 1, args.err, kErrTimeoutFull)) {
-        flags[0] = 1;
+      if (!warp_wait(full_bar + s, (i / STAGES) & 1, kErrTimeoutFull)) {
+        if (lane == 0) flags[0] = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t a_addr = smem_u32(smem + s * Shape::STAGE_BYTES);
-      const uint32_t b_addr = a_addr + Shape::A_BYTES;
+      if (lane == 0) {
+        const uint32_t a_addr = smem_u32(smem + s * Shape::STAGE_BYTES);
+        const uint32_t b_addr = a_addr + Shape::A_BYTES;
 #pragma unroll
-      for (int kk = 0; kk < kGemmBK / 16; ++kk) {
-        umma_f16(tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC,
-                 (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+          umma_f16(tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC,
+                   (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(empty_bar + s);
       }
-      umma_commit(empty_bar + s);
+      __syncwarp();
       consumed = i + 1;
     }
-    flags[3] = consumed;
-    umma_commit(done_bar);
+    if (lane == 0) {
+      flags[3] = consumed;
+      umma_commit(done_bar);
+    }
+    __syncwarp();
   }
   grid_dependency_wait();
 
-  // ---------------- accumulator -> staging tile (fp32, [token][feature]) ----------------
-  const bool mma_ok = mbar_wait(done_bar, 0, args.err, kErrTimeoutDone);
+  // ---------------- accumulator -> this CTA's staging tile (fp32, [token][feature]) ----------------
+  const bool mma_ok = warp_wait(done_bar, 0, kErrTimeoutDone);
   tc_fence_after();
   float* stage = reinterpret_cast<float*>(smem);
   const int row = warp * 32 + lane;  // feature lane inside the 128-wide tile
   const uint32_t t_warp = tmem + (uint32_t(warp * 32) << 16);
   const int rows = args.rows;
-  bool have_tile = true;
-
-  if (args.splits == 1) {
-    for (int c0 = 0; c0 < rows; c0 += 32) {
-      float v[32];
-      tmem_ld_32cols(t_warp + c0, v);
+  for (int c0 = 0; c0 < rows; c0 += 32) {
+    float v[32];
+    tmem_ld_32cols(t_warp + c0, v);
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < rows) stage[(c0 + j) * kStagePad + row] = v[j];
-    }
-  } else {
-    float* mine = args.partial + (size_t(split) * args.n_tiles + tile) * NTOK * 128;
-    for (int c0 = 0; c0 < rows; c0 += 32) {
-      float v[32];
-      tmem_ld_32cols(t_warp + c0, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < rows) __stcg(mine + (c0 + j) * 128 + row, v[j]);
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int old = atomicAdd(args.counters + tile, 1);
-      flags[1] = (old == args.splits - 1) ? 1 : 0;
-      if (old >= args.splits) record_error(args.err, kErrTimeoutSplit);
-    }
-    __syncthreads();
-    have_tile = flags[1] != 0;
-    if (have_tile) {
-      __threadfence();
-      const size_t split_stride = size_t(args.n_tiles) * NTOK * 128;
-      const float* base = args.partial + size_t(tile) * NTOK * 128;
-      for (int c = 0; c < rows; ++c) {
-        float acc = 0.f;
-        for (int s = 0; s < args.splits; ++s) acc += __ldcg(base + s * split_stride + c * 128 + row);
-        stage[c * kStagePad + row] = acc;
-      }
-      if (tid == 0) args.counters[tile] = 0;
-    }
+    for (int j = 0; j < 32; ++j)
+      if (c0 + j < rows) stage[(c0 + j) * kStagePad + row] = v[j];
   }
   tc_fence_before();
   __syncthreads();
   if (flags[0] != 0 && tid == 0) {
-    // Aborted: let every TMA copy this CTA issued but never consumed land before shared memory is released.
+    // Aborted: let every TMA copy this CTA issued but never consumed land before shared memory is reused.
     for (int i = flags[3]; i < flags[2]; ++i)
       if (!mbar_wait(full_bar + (i % STAGES), (i / STAGES) & 1, args.err, kErrTimeoutFull)) break;
   }
@@ -262,38 +258,73 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Shape::TMEM_COLS);
   }
-  __syncthreads();
-  if (!have_tile || !mma_ok || flags[0] != 0) return;
+  const bool ok = mma_ok && flags[0] == 0;
+
+  // ---------------- split reduction over the cluster ----------------
+  // The `splits` CTAs of a tile form one cluster. After the barrier, rank r sums the partial tiles of all ranks,
+  // in rank order, for its slice of token columns [c_begin, c_end), reading peers' staging tiles through
+  // distributed shared memory; a second barrier keeps every staging tile alive until all slices are read.
+  const int S = args.splits;
+  const uint32_t rank = S > 1 ? cluster_rank() : 0;
+  const int cs = (rows + S - 1) / S;
+  const int c_begin = min(rows, int(rank) * cs), c_end = min(rows, c_begin + cs);
+  float* red = stage;
+  if (S > 1) {
+    red = stage + rows * kStagePad;
+    cluster_sync();
+    uint32_t peer[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) peer[s] = s < S ? cluster_map(stage, uint32_t(s)) : 0u;
+    for (int idx = tid; idx < (c_end - c_begin) * 128; idx += kGemmThreads) {
+      const int c = c_begin + (idx >> 7), f = idx & 127;
+      const uint32_t off = uint32_t(c * kStagePad + f) * 4u;
+      float part[8];
+#pragma unroll
+      for (int s = 0; s < 8; ++s) part[s] = s < S ? ld_dsmem_f32(peer[s] + off) : 0.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        if (s < S) acc += part[s];
+      red[(c - c_begin) * kStagePad + f] = acc;
+    }
+    cluster_sync();
+  } else {
+    __syncthreads();
+  }
+  if (!ok) return;
+  // From here `red` holds the finished tile for token columns [c_begin, c_end), local column c - c_begin.
 
   // ---------------- fused epilogues ----------------
+  const int ncols = c_end - c_begin;
   if (EPI == kEpiStore) {
     T* out = reinterpret_cast<T*>(args.out);
     const int n0 = tile * 128;
     const int feats = min(128, args.n_out - n0);
-    for (int idx = tid; idx < rows * 128; idx += kGemmThreads) {
-      const int c = idx >> 7, f = idx & 127;
-      if (f < feats) out[size_t(c) * args.ldo + n0 + f] = from_f32<T>(stage[c * kStagePad + f]);
+    for (int idx = tid; idx < ncols * 128; idx += kGemmThreads) {
+      const int lc = idx >> 7, f = idx & 127;
+      if (f < feats) out[size_t(c_begin + lc) * args.ldo + n0 + f] = from_f32<T>(red[lc * kStagePad + f]);
     }
   } else if (EPI == kEpiSiluMul) {
     T* out = reinterpret_cast<T*>(args.out);
     const int j0 = tile * 64;
-    for (int idx = tid; idx < rows * 64; idx += kGemmThreads) {
-      const int c = idx >> 6, f = idx & 63;
-      const float g = round_to<T>(stage[c * kStagePad + f]);
-      const float u = round_to<T>(stage[c * kStagePad + 64 + f]);
+    for (int idx = tid; idx < ncols * 64; idx += kGemmThreads) {
+      const int lc = idx >> 6, f = idx & 63;
+      const float g = round_to<T>(red[lc * kStagePad + f]);
+      const float u = round_to<T>(red[lc * kStagePad + 64 + f]);
       const float act = g / (1.0f + expf(-g)) * u;
-      out[size_t(c) * args.ldo + j0 + f] = from_f32<T>(act);
+      out[size_t(c_begin + lc) * args.ldo + j0 + f] = from_f32<T>(act);
     }
   } else if (EPI == kEpiQkvRope) {
     const QkvEpilogue& q = args.qkv;
     const int hd = q.head_dim, half = hd >> 1;
     const int q_size = q.num_heads * hd, kv_size = q.num_kv_heads * hd;
     const int n0 = tile * 128;
-    const T* cs = reinterpret_cast<const T*>(q.cos_sin);
-    for (int idx = tid; idx < rows * 128; idx += kGemmThreads) {
-      const int c = idx >> 7, f = idx & 127;
+    const T* cs_tab = reinterpret_cast<const T*>(q.cos_sin);
+    for (int idx = tid; idx < ncols * 128; idx += kGemmThreads) {
+      const int lc = idx >> 7, f = idx & 127;
+      const int c = c_begin + lc;
       const int F = n0 + f;
-      const float x = round_to<T>(stage[c * kStagePad + f]);
+      const float x = round_to<T>(red[lc * kStagePad + f]);
       const int d = F % hd;
       float y = x;
       if (F < q_size + kv_size) {
@@ -304,9 +335,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         const int dh = d < half ? d : d - half;
         const int fp = d < half ? f + half : f - half;
-        const float xp = round_to<T>(stage[c * kStagePad + fp]);
-        const float cv = to_f32<T>(cs[size_t(pos) * hd + dh]);
-        const float sv = to_f32<T>(cs[size_t(pos) * hd + half + dh]);
+        const float xp = round_to<T>(red[lc * kStagePad + fp]);
+        const float cv = to_f32<T>(cs_tab[size_t(pos) * hd + dh]);
+        const float sv = to_f32<T>(cs_tab[size_t(pos) * hd + half + dh]);
         y = d < half ? x * cv - xp * sv : x * cv + xp * sv;
       }
       if (F < q_size) {
@@ -327,18 +358,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (EPI == kEpiLogits) {
     const LogitsEpilogue& L = args.logits;
     const int n0 = tile * 128;
-    for (int idx = tid; idx < L.n_verify * 128; idx += kGemmThreads) {
-      const int c = idx >> 7, f = idx & 127;
-      if (c < rows && n0 + f < L.vocab)
-        L.verify_logits[size_t(c) * L.vocab + n0 + f] = round_to<T>(stage[c * kStagePad + f]);
+    const int nv_end = min(c_end, L.n_verify);
+    for (int idx = tid; idx < max(0, nv_end - c_begin) * 128; idx += kGemmThreads) {
+      const int lc = idx >> 7, f = idx & 127;
+      if (n0 + f < L.vocab)
+        L.verify_logits[size_t(c_begin + lc) * L.vocab + n0 + f] = round_to<T>(red[lc * kStagePad + f]);
     }
-    for (int c = L.n_verify + warp; c < rows; c += kGemmThreads / 32) {
+    for (int c = max(c_begin, L.n_verify) + warp; c < c_end; c += kGemmThreads / 32) {
+      const int lc = c - c_begin;
       float best = -INFINITY;
       int bi = 0x7fffffff;
       for (int f = lane; f < 128; f += 32) {
         const int v = n0 + f;
         if (v < L.vocab) {
-          const float x = round_to<T>(stage[c * kStagePad + f]);
+          const float x = round_to<T>(red[lc * kStagePad + f]);
           if (x > best || (x == best && v < bi)) {
             best = x;
             bi = v;
@@ -364,10 +397,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     T* table = reinterpret_cast<T*>(tb.table);
     const int n0 = tile * 128;
     const int feats = min(128, args.n_out - n0);
-    for (int idx = tid; idx < rows * 128; idx += kGemmThreads) {
-      const int f = idx / rows, c = idx % rows;
+    for (int idx = tid; idx < ncols * 128; idx += kGemmThreads) {
+      const int f = idx / ncols, lc = idx % ncols;
       if (f < feats)
-        table[size_t(n0 + f) * tb.aux + tb.a0 + c] = from_f32<T>(-round_to<T>(stage[c * kStagePad + f]));
+        table[size_t(n0 + f) * tb.aux + tb.a0 + c_begin + lc] = from_f32<T>(-round_to<T>(red[lc * kStagePad + f]));
     }
   }
 }

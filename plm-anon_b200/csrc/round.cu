@@ -1,0 +1,649 @@
+// The round engine behind the C ABI: one handle = one request stream on one GPU (batch 1, like the reference's
+// RoundDecoder, plm/decoder.py:85-467). The handle owns the paged KV pool, the block table, the activation buffers,
+// the round layouts, the loop-carried state (out, base, offset, anchor, pending, round_sequence) and the Voronoi
+// cost table; the weights are borrowed device pointers.
+//
+// plm_round / plm_round0 / plm_prefill only enqueue kernels on the caller's stream (programmatic dependent launch
+// between consecutive kernels, no host synchronisation), so a caller can capture plm_round into a CUDA graph and
+// replay it once per round, as the reference replays its captured steady round (decoder.py:312-324, 414-439).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <vector>
+
+#include "attention.h"
+#include "elementwise.h"
+#include "runtime.h"
+#include "verify.h"
+
+namespace plm {
+namespace {
+
+constexpr int kUnreachable = 1 << 30;  // plm/mask.py:14
+constexpr int kMaxPrefillRows = 256;
+
+template <typename Tp>
+int dev_alloc(Tp** p, size_t count, const char* what) {
+  return check_cuda(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(Tp)), what);
+}
+
+}  // namespace
+}  // namespace plm
+
+struct plm_handle {
+  plm_ctx* ctx = nullptr;
+  plm_model_desc m = {};
+  plm_round_desc rd = {};
+  int W = 0;                 // rows of a round: k + k^2
+  int R = 0;                 // activation row capacity
+  // weights (borrowed)
+  const void *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr, *aux_vocab = nullptr, *mask_aux = nullptr,
+             *cos_sin = nullptr;
+  std::vector<const void*> qkv, o, gate_up, down, in_norm, post_norm;
+  void* table = nullptr;
+  bool own_table = false;
+  std::vector<CUtensorMap> map_qkv, map_o, map_gate_up, map_down;
+  CUtensorMap map_lm;
+  std::map<std::pair<const void*, int>, CUtensorMap> row_maps;
+  // activations
+  void *x_norm = nullptr, *residual = nullptr, *y = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr,
+       *gathered = nullptr;
+  int32_t* positions = nullptr;
+  int64_t* slots = nullptr;
+  float* verify_logits = nullptr;
+  float* best_val = nullptr;
+  int32_t* best_idx = nullptr;
+  int lm_tiles = 0;
+  int64_t* verify = nullptr;
+  int32_t* flags = nullptr;
+  // layouts
+  int64_t *st_relpos = nullptr, *st_relaux = nullptr, *r0_relpos = nullptr, *r0_relaux = nullptr;
+  int32_t *st_depth = nullptr, *st_own = nullptr, *r0_depth = nullptr, *r0_own = nullptr, *causal_depth = nullptr,
+          *causal_own = nullptr;
+  // paged KV
+  void* kv = nullptr;
+  size_t plane_elems = 0;
+  int32_t* block_table = nullptr;
+  // loop state
+  int64_t *out = nullptr, *base = nullptr, *offset = nullptr, *anchor = nullptr, *pending = nullptr,
+          *round_sequence = nullptr, *sequence_step = nullptr, *aux_buf = nullptr, *prompt = nullptr,
+          *chunk_offsets = nullptr;
+  int64_t prompt_len = 0;
+  int attn_splits_round = 1;
+};
+
+namespace plm {
+namespace {
+
+void* kv_plane(plm_handle* h, int layer, int which) {
+  return static_cast<__nv_bfloat16*>(h->kv) + (size_t(layer) * 2 + which) * h->plane_elems;
+}
+
+int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMap** out) {
+  const int ntok = gemm_token_tile(rows);
+  if (ntok < 0) return fail(PLM_ERR_UNSUPPORTED, "row map: %d rows", rows);
+  auto key = std::make_pair(buffer, ntok);
+  auto it = h->row_maps.find(key);
+  if (it == h->row_maps.end()) {
+    plm_gemm_desc d = {};
+    d.dtype = h->m.dtype;
+    d.x = buffer;
+    d.k = k;
+    d.rows = rows;
+    d.x_rows = buffer == h->gathered ? 16 : h->R;
+    CUtensorMap map;
+    int st = gemm_row_map(&map, d);
+    if (st != PLM_OK) return st;
+    it = h->row_maps.emplace(key, map).first;
+  }
+  *out = &it->second;
+  return PLM_OK;
+}
+
+int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, const void* x, int rows,
+         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s) {
+  plm_gemm_desc d = {};
+  d.dtype = h->m.dtype;
+  d.w = w;
+  d.n_out = n_out;
+  d.k = k;
+  d.x = x;
+  d.x_rows = x == h->gathered ? 16 : h->R;
+  d.rows = rows;
+  d.out = out;
+  d.ldo = ldo;
+  d.epi = epi;
+  const CUtensorMap* mx = nullptr;
+  int st = row_map(h, x, k, rows, &mx);
+  if (st != PLM_OK) return st;
+  return gemm_launch(h->ctx, d, mw, mx, s, true);
+}
+
+// The Llama forward of `rows` rows whose logical KV indices start at *offset_ptr (vLLM llama.py:253-314):
+// prologue (+ layer-0 input norm), then per layer qkv(+RoPE, KV scatter) -> attention -> o -> add+norm ->
+// gate_up(+SiLU) -> down -> add+norm (the next layer's input norm, or the final norm).
+int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const int64_t* relpos, const int64_t* relaux,
+            const int32_t* depth, const int32_t* own, int attn_splits, int gather_row, cudaStream_t s) {
+  const plm_model_desc& m = h->m;
+  const int hidden = m.hidden, hd = m.head_dim;
+  const int q_size = m.num_heads * hd, kv_size = m.num_kv_heads * hd;
+  PrologueArgs p = {};
+  p.mode = mode;
+  p.k = h->rd.k;
+  p.vocab = m.vocab;
+  p.aux = m.aux_vocab;
+  p.num_aux_tokens = m.num_aux_tokens;
+  p.hidden = hidden;
+  p.eps = m.rms_eps;
+  p.offset = offset_ptr;
+  p.base = h->base;
+  p.anchor = h->anchor;
+  p.pending = h->pending;
+  p.rel_positions = relpos;
+  p.rel_aux = relaux;
+  p.aux_buf = h->aux_buf;
+  p.aux_len = h->rd.aux_len;
+  p.prompt = h->prompt;
+  p.prompt_cap = int64_t(h->rd.max_pages) * h->rd.page_size;
+  p.embed = h->embed;
+  p.aux_vocab = h->aux_vocab;
+  p.mask_aux = h->mask_aux;
+  p.norm_weight = h->in_norm[0];
+  p.block_table = h->block_table;
+  p.max_pages = h->rd.max_pages;
+  p.num_pages = h->rd.num_pages;
+  p.page_size = h->rd.page_size;
+  p.max_pos = m.max_pos;
+  p.residual = h->residual;
+  p.normed = h->x_norm;
+  p.positions = h->positions;
+  p.slots = h->slots;
+  p.err = h->ctx->err;
+  int st = prologue_launch(p, rows, s, true);
+  if (st != PLM_OK) return st;
+
+  for (int l = 0; l < m.num_layers; ++l) {
+    plm_gemm_epilogue e = {};
+    e.kind = PLM_EPI_QKV_ROPE;
+    e.q_out = h->q;
+    e.k_cache = kv_plane(h, l, 0);
+    e.v_cache = kv_plane(h, l, 1);
+    e.positions = h->positions;
+    e.slots = h->slots;
+    e.cos_sin = h->cos_sin;
+    e.num_heads = m.num_heads;
+    e.num_kv_heads = m.num_kv_heads;
+    e.head_dim = hd;
+    e.page_size = h->rd.page_size;
+    e.num_slots = int64_t(h->rd.num_pages) * h->rd.page_size;
+    e.max_pos = m.max_pos;
+    st = gemm(h, h->qkv[l], &h->map_qkv[l], q_size + 2 * kv_size, hidden, h->x_norm, rows, e, nullptr, 0, s);
+    if (st != PLM_OK) return st;
+
+    AttnArgs a = {};
+    a.q = h->q;
+    a.k_cache = kv_plane(h, l, 0);
+    a.v_cache = kv_plane(h, l, 1);
+    a.block_table = h->block_table;
+    a.max_pages = h->rd.max_pages;
+    a.num_pages = h->rd.num_pages;
+    a.page_size = h->rd.page_size;
+    a.offset = offset_ptr;
+    a.rows = rows;
+    a.depth = depth;
+    a.own_start = own;
+    a.num_heads = m.num_heads;
+    a.num_kv_heads = m.num_kv_heads;
+    a.head_dim = hd;
+    a.scale_log2 = float(1.4426950408889634 / sqrt(double(hd)));
+    a.out = h->attn;
+    a.splits = attn_splits;
+    st = attention_launch(h->ctx, a, s, true);
+    if (st != PLM_OK) return st;
+
+    plm_gemm_epilogue store = {};
+    store.kind = PLM_EPI_STORE;
+    st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, store, h->y, hidden, s);
+    if (st != PLM_OK) return st;
+    AddNormArgs n1 = {h->y, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr};
+    st = add_norm_launch(n1, rows, s, true);
+    if (st != PLM_OK) return st;
+
+    plm_gemm_epilogue silu = {};
+    silu.kind = PLM_EPI_SILU_MUL;
+    silu.gate_offset = m.intermediate;
+    st = gemm(h, h->gate_up[l], &h->map_gate_up[l], 2 * m.intermediate, hidden, h->x_norm, rows, silu, h->act,
+              m.intermediate, s);
+    if (st != PLM_OK) return st;
+    st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, store, h->y, hidden, s);
+    if (st != PLM_OK) return st;
+    const bool last = l + 1 == m.num_layers;
+    AddNormArgs n2 = {h->y, h->residual, h->x_norm, last ? h->final_norm : h->in_norm[l + 1], hidden, m.rms_eps,
+                      last ? gather_row : -1, last ? h->gathered : nullptr};
+    st = add_norm_launch(n2, rows, s, true);
+    if (st != PLM_OK) return st;
+  }
+  return PLM_OK;
+}
+
+int lm_head(plm_handle* h, const void* x, int rows, int n_verify, cudaStream_t s) {
+  plm_gemm_epilogue e = {};
+  e.kind = PLM_EPI_LOGITS;
+  e.verify_logits = h->verify_logits;
+  e.best_val = h->best_val;
+  e.best_idx = h->best_idx;
+  e.n_verify = n_verify;
+  e.vocab = h->m.vocab;
+  return gemm(h, h->lm_head, &h->map_lm, h->m.vocab, h->m.hidden, x, rows, e, nullptr, 0, s);
+}
+
+int verify(plm_handle* h, int n_rows, int mode, const int64_t* aux_base, cudaStream_t s) {
+  VerifyArgs a = {};
+  a.logits = h->verify_logits;
+  a.vocab = h->m.vocab;
+  a.logits_stride = h->m.vocab;
+  a.table = h->table;
+  a.aux = h->m.aux_vocab;
+  a.aux_buf = h->aux_buf;
+  a.aux_len = h->rd.aux_len;
+  a.aux_base = aux_base;
+  a.aux_row_offset = 0;
+  a.pending = h->pending;
+  a.n_accept = mode == kBookSteady ? h->rd.k - 1 : 0;
+  a.rule = h->rd.rule;
+  a.threshold = h->rd.threshold;
+  a.top_m = h->m.top_m;
+  a.shortlist = h->m.shortlist;
+  a.rounds = h->m.rounds;
+  a.sweeps = h->m.sweeps;
+  for (int r = 0; r < 4; ++r) {
+    const double eps = r == 0 ? h->m.epsilon : h->m.epsilon * h->m.refocus;
+    a.eps[r] = float(eps);
+    a.anneal[r] = float(pow(h->m.endpoint / eps, 1.0 / double(h->m.sweeps > 1 ? h->m.sweeps : 1)));
+  }
+  a.verify = h->verify;
+  a.flags = h->flags;
+  a.book.mode = mode;
+  a.book.k = h->rd.k;
+  a.book.best_val = h->best_val;
+  a.book.best_idx = h->best_idx;
+  a.book.n_tiles = h->lm_tiles;
+  a.book.rows = h->W;
+  a.book.out = h->out;
+  a.book.out_cap = h->rd.out_capacity;
+  a.book.base = h->base;
+  a.book.offset = h->offset;
+  a.book.anchor = h->anchor;
+  a.book.pending = h->pending;
+  a.book.round_sequence = h->round_sequence;
+  a.book.seq_cap = h->rd.seq_capacity;
+  a.book.sequence_step = h->sequence_step;
+  a.book.prompt_len = h->prompt_len;
+  a.counter = h->ctx->counters + (h->ctx->n_counters - 1);
+  a.err = h->ctx->err;
+  int st = verify_validate(a, n_rows);
+  if (st != PLM_OK) return st;
+  return verify_launch(a, h->m.dtype, n_rows, s, true);
+}
+
+int upload_layout(const std::vector<int64_t>& v, int64_t* dst) {
+  return check_cuda(cudaMemcpy(dst, v.data(), v.size() * sizeof(int64_t), cudaMemcpyHostToDevice), "layout upload");
+}
+int upload_layout32(const std::vector<int32_t>& v, int32_t* dst) {
+  return check_cuda(cudaMemcpy(dst, v.data(), v.size() * sizeof(int32_t), cudaMemcpyHostToDevice), "layout upload");
+}
+
+// plm/mask.py:42-65 for block sizes `blocks`.
+void round_layout(const std::vector<int>& blocks, std::vector<int64_t>& relpos, std::vector<int64_t>& relaux,
+                  std::vector<int32_t>& depth, std::vector<int32_t>& own) {
+  const int n = int(blocks.size());
+  relpos.clear();
+  relaux.clear();
+  depth.clear();
+  own.clear();
+  for (int d = 0; d < n; ++d) {
+    relpos.push_back(d);
+    relaux.push_back(-1);
+    depth.push_back(d);
+    own.push_back(kUnreachable);
+  }
+  int start = n;
+  for (int d = 0; d < n; ++d) {
+    for (int j = 0; j < blocks[d]; ++j) {
+      relpos.push_back(d + j);
+      relaux.push_back(d + j);
+      depth.push_back(d);
+      own.push_back(start);
+    }
+    start += blocks[d];
+  }
+}
+
+int validate_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_round_desc* r) {
+  if (m->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_create: only bf16 models are built");
+  if (m->num_layers < 1 || m->hidden % 64 != 0 || m->intermediate % 64 != 0 || m->head_dim % 64 != 0)
+    return fail(PLM_ERR_INVALID, "plm_create: hidden / intermediate / head_dim must be multiples of 64");
+  if ((m->num_heads * m->head_dim) % 64 != 0 || m->num_heads % m->num_kv_heads != 0)
+    return fail(PLM_ERR_INVALID, "plm_create: heads %d / kv heads %d", m->num_heads, m->num_kv_heads);
+  if (m->vocab < m->top_m || m->aux_vocab < 32) return fail(PLM_ERR_INVALID, "plm_create: vocab / aux vocabulary");
+  if (r->k < 1 || r->k + r->k * r->k > 256 || r->k > 32)
+    return fail(PLM_ERR_UNSUPPORTED, "plm_create: k=%d (round width must be <= 256)", r->k);
+  if (r->page_size < 1 || r->num_pages < 1 || r->max_pages < 1)
+    return fail(PLM_ERR_INVALID, "plm_create: paging");
+  if (r->max_prefill < 1 || r->max_prefill > kMaxPrefillRows)
+    return fail(PLM_ERR_INVALID, "plm_create: max_prefill %d (1..%d)", r->max_prefill, kMaxPrefillRows);
+  if (!w->embed || !w->lm_head || !w->final_norm || !w->aux_vocab || !w->mask_aux || !w->cos_sin || !w->qkv ||
+      !w->o || !w->gate_up || !w->down || !w->input_norm || !w->post_norm)
+    return fail(PLM_ERR_INVALID, "plm_create: missing weight pointer");
+  return PLM_OK;
+}
+
+}  // namespace
+}  // namespace plm
+
+using namespace plm;
+
+extern "C" {
+
+int plm_destroy(plm_handle* h) {
+  if (h == nullptr) return PLM_OK;
+  void* bufs[] = {h->x_norm, h->residual, h->y, h->q, h->attn, h->act, h->gathered, h->positions, h->slots,
+                  h->verify_logits, h->best_val, h->best_idx, h->verify, h->flags, h->st_relpos, h->st_relaux,
+                  h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
+                  h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
+                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets};
+  for (void* b : bufs) cudaFree(b);
+  if (h->own_table) cudaFree(h->table);
+  plm_ctx_destroy(h->ctx);
+  delete h;
+  return PLM_OK;
+}
+
+int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_round_desc* rd, plm_handle** out) {
+  if (!m || !w || !rd || !out) return fail(PLM_ERR_INVALID, "plm_create: null argument");
+  *out = nullptr;
+  int st = validate_create(m, w, rd);
+  if (st != PLM_OK) return st;
+  plm_handle* h = new plm_handle();
+  h->m = *m;
+  h->rd = *rd;
+  if (h->rd.seq_capacity < 1) h->rd.seq_capacity = 1 << 17;  // plm/decoder.py:86
+  if (h->rd.aux_len < 1) h->rd.aux_len = 8192;               // plm/decoder.py:28
+  const int K = rd->k;
+  h->W = K + K * K;
+  h->R = kMaxPrefillRows;
+  st = plm_ctx_create(&h->ctx);
+  auto guard = [&](int s) {
+    if (s != PLM_OK) plm_destroy(h);
+    return s;
+  };
+  if (st != PLM_OK) return guard(st);
+  h->embed = w->embed;
+  h->lm_head = w->lm_head;
+  h->final_norm = w->final_norm;
+  h->aux_vocab = w->aux_vocab;
+  h->mask_aux = w->mask_aux;
+  h->cos_sin = w->cos_sin;
+  const int L = m->num_layers;
+  h->qkv.assign(w->qkv, w->qkv + L);
+  h->o.assign(w->o, w->o + L);
+  h->gate_up.assign(w->gate_up, w->gate_up + L);
+  h->down.assign(w->down, w->down + L);
+  h->in_norm.assign(w->input_norm, w->input_norm + L);
+  h->post_norm.assign(w->post_norm, w->post_norm + L);
+
+  const int hidden = m->hidden, hd = m->head_dim, I = m->intermediate;
+  const int q_size = m->num_heads * hd, kv_size = m->num_kv_heads * hd;
+  // weight descriptors, once
+  h->map_qkv.resize(L);
+  h->map_o.resize(L);
+  h->map_gate_up.resize(L);
+  h->map_down.resize(L);
+  for (int l = 0; l < L && st == PLM_OK; ++l) {
+    plm_gemm_desc d = {};
+    d.dtype = m->dtype;
+    d.w = h->qkv[l], d.n_out = q_size + 2 * kv_size, d.k = hidden, d.epi.kind = PLM_EPI_QKV_ROPE;
+    st = gemm_weight_map(&h->map_qkv[l], d);
+    d.w = h->o[l], d.n_out = hidden, d.k = q_size, d.epi.kind = PLM_EPI_STORE;
+    if (st == PLM_OK) st = gemm_weight_map(&h->map_o[l], d);
+    d.w = h->gate_up[l], d.n_out = 2 * I, d.k = hidden, d.epi.kind = PLM_EPI_SILU_MUL;
+    if (st == PLM_OK) st = gemm_weight_map(&h->map_gate_up[l], d);
+    d.w = h->down[l], d.n_out = hidden, d.k = I, d.epi.kind = PLM_EPI_STORE;
+    if (st == PLM_OK) st = gemm_weight_map(&h->map_down[l], d);
+  }
+  if (st == PLM_OK) {
+    plm_gemm_desc d = {};
+    d.dtype = m->dtype;
+    d.w = h->lm_head, d.n_out = m->vocab, d.k = hidden, d.epi.kind = PLM_EPI_LOGITS;
+    st = gemm_weight_map(&h->map_lm, d);
+  }
+  if (st != PLM_OK) return guard(st);
+
+  const size_t R = size_t(h->R);
+  const size_t widest = size_t(std::max(std::max(hidden, q_size), I));
+  (void)widest;
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->x_norm), R * hidden, "x_norm");
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->residual), R * hidden, "residual");
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->y), R * hidden, "y");
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->q), R * q_size, "q");
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->attn), R * q_size, "attn");
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->act), R * I, "act");
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->gathered), size_t(16) * hidden, "gathered");
+  if (st == PLM_OK) st = dev_alloc(&h->positions, R, "positions");
+  if (st == PLM_OK) st = dev_alloc(&h->slots, R, "slots");
+  h->lm_tiles = (m->vocab + 127) / 128;
+  if (st == PLM_OK) st = dev_alloc(&h->verify_logits, size_t(K) * m->vocab, "verify logits");
+  if (st == PLM_OK) st = dev_alloc(&h->best_val, size_t(h->lm_tiles) * h->W, "argmax partials");
+  if (st == PLM_OK) st = dev_alloc(&h->best_idx, size_t(h->lm_tiles) * h->W, "argmax partials");
+  if (st == PLM_OK) st = dev_alloc(&h->verify, 32, "verify");
+  if (st == PLM_OK) st = dev_alloc(&h->flags, 32, "flags");
+  if (st != PLM_OK) return guard(st);
+  // zero the activations once: rows past `rows` are read by TMA boxes but never stored
+  for (void* b : {h->x_norm, h->residual, h->y, h->q, h->attn, h->act}) (void)b;
+  cudaMemset(h->x_norm, 0, R * hidden * 2);
+  cudaMemset(h->residual, 0, R * hidden * 2);
+  cudaMemset(h->y, 0, R * hidden * 2);
+  cudaMemset(h->q, 0, R * q_size * 2);
+  cudaMemset(h->attn, 0, R * q_size * 2);
+  cudaMemset(h->act, 0, R * I * 2);
+  cudaMemset(h->gathered, 0, size_t(16) * hidden * 2);
+
+  // layouts: steady round [k] * k, round 0 [W - 1] (plm/decoder.py:145-146), causal chunk rows
+  std::vector<int64_t> relpos, relaux;
+  std::vector<int32_t> depth, own;
+  round_layout(std::vector<int>(K, K), relpos, relaux, depth, own);
+  st = dev_alloc(&h->st_relpos, h->W, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->st_relaux, h->W, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->st_depth, h->W, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->st_own, h->W, "layout");
+  if (st == PLM_OK) st = upload_layout(relpos, h->st_relpos);
+  if (st == PLM_OK) st = upload_layout(relaux, h->st_relaux);
+  if (st == PLM_OK) st = upload_layout32(depth, h->st_depth);
+  if (st == PLM_OK) st = upload_layout32(own, h->st_own);
+  round_layout(std::vector<int>(1, h->W - 1), relpos, relaux, depth, own);
+  if (st == PLM_OK) st = dev_alloc(&h->r0_relpos, h->W, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->r0_relaux, h->W, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->r0_depth, h->W, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->r0_own, h->W, "layout");
+  if (st == PLM_OK) st = upload_layout(relpos, h->r0_relpos);
+  if (st == PLM_OK) st = upload_layout(relaux, h->r0_relaux);
+  if (st == PLM_OK) st = upload_layout32(depth, h->r0_depth);
+  if (st == PLM_OK) st = upload_layout32(own, h->r0_own);
+  std::vector<int32_t> causal(kMaxPrefillRows), unreachable(kMaxPrefillRows, kUnreachable);
+  for (int i = 0; i < kMaxPrefillRows; ++i) causal[i] = i;
+  if (st == PLM_OK) st = dev_alloc(&h->causal_depth, kMaxPrefillRows, "layout");
+  if (st == PLM_OK) st = dev_alloc(&h->causal_own, kMaxPrefillRows, "layout");
+  if (st == PLM_OK) st = upload_layout32(causal, h->causal_depth);
+  if (st == PLM_OK) st = upload_layout32(unreachable, h->causal_own);
+  if (st != PLM_OK) return guard(st);
+
+  // paged KV pool [layer][K|V][num_pages][kv_heads][page_size][head_dim] and an identity block table
+  h->plane_elems = size_t(rd->num_pages) * m->num_kv_heads * rd->page_size * hd;
+  st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->kv), size_t(L) * 2 * h->plane_elems, "KV pool");
+  if (st == PLM_OK) st = check_cuda(cudaMemset(h->kv, 0, size_t(L) * 2 * h->plane_elems * 2), "KV pool zero");
+  if (st == PLM_OK) st = dev_alloc(&h->block_table, rd->max_pages, "block table");
+  if (st == PLM_OK) {
+    std::vector<int32_t> ident(rd->max_pages);
+    for (int i = 0; i < rd->max_pages; ++i) ident[i] = i < rd->num_pages ? i : -1;
+    st = upload_layout32(ident, h->block_table);
+  }
+  // loop state
+  if (st == PLM_OK) st = dev_alloc(&h->out, size_t(h->rd.out_capacity), "out");
+  if (st == PLM_OK) st = dev_alloc(&h->base, 1, "state");
+  if (st == PLM_OK) st = dev_alloc(&h->offset, 1, "state");
+  if (st == PLM_OK) st = dev_alloc(&h->anchor, 1, "state");
+  if (st == PLM_OK) st = dev_alloc(&h->pending, 32, "state");
+  if (st == PLM_OK) st = dev_alloc(&h->round_sequence, size_t(h->rd.seq_capacity), "round sequence");
+  if (st == PLM_OK) st = dev_alloc(&h->sequence_step, 1, "state");
+  if (st == PLM_OK) st = dev_alloc(&h->aux_buf, size_t(h->rd.aux_len), "aux stream");
+  if (st == PLM_OK) st = dev_alloc(&h->prompt, size_t(rd->max_pages) * rd->page_size, "prompt");
+  if (st == PLM_OK) st = dev_alloc(&h->chunk_offsets, 4096, "chunk offsets");
+  if (st != PLM_OK) return guard(st);
+  cudaMemset(h->out, 0xff, size_t(h->rd.out_capacity) * 8);
+  cudaMemset(h->base, 0, 8);
+  cudaMemset(h->offset, 0, 8);
+  cudaMemset(h->anchor, 0, 8);
+  cudaMemset(h->pending, 0, 32 * 8);
+  cudaMemset(h->round_sequence, 0, size_t(h->rd.seq_capacity) * 8);
+  cudaMemset(h->sequence_step, 0, 8);
+  cudaMemset(h->aux_buf, 0, size_t(h->rd.aux_len) * 8);
+  cudaMemset(h->prompt, 0, size_t(rd->max_pages) * rd->page_size * 8);
+  h->attn_splits_round = attention_splits(m->num_heads, (h->W + 63) / 64, h->ctx->num_sms,
+                                          int64_t(rd->max_pages) * rd->page_size);
+
+  // the Voronoi cost table -(aux_vocab . lm_head^T)^T, [vocab][A] (plm/auxiliary.py:56-65)
+  if (w->table != nullptr) {
+    h->table = const_cast<void*>(w->table);
+  } else {
+    st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->table), size_t(m->vocab) * m->aux_vocab, "Voronoi table");
+    if (st != PLM_OK) return guard(st);
+    h->own_table = true;
+    for (int a0 = 0; a0 < m->aux_vocab && st == PLM_OK; a0 += 256) {
+      plm_gemm_desc d = {};
+      d.dtype = m->dtype;
+      d.w = h->lm_head;
+      d.n_out = m->vocab;
+      d.k = hidden;
+      d.x = static_cast<const __nv_bfloat16*>(h->aux_vocab) + size_t(a0) * hidden;
+      d.rows = std::min(256, m->aux_vocab - a0);
+      d.x_rows = d.rows;
+      d.epi.kind = PLM_EPI_TABLE;
+      d.epi.table = h->table;
+      d.epi.aux = m->aux_vocab;
+      d.epi.a0 = a0;
+      CUtensorMap mx;
+      st = gemm_row_map(&mx, d);
+      if (st == PLM_OK) st = gemm_launch(h->ctx, d, &h->map_lm, &mx, nullptr, false);
+    }
+  }
+  if (st == PLM_OK) st = check_cuda(cudaDeviceSynchronize(), "plm_create");
+  if (st != PLM_OK) return guard(st);
+  *out = h;
+  return PLM_OK;
+}
+
+int plm_set_block_table(plm_handle* h, const int32_t* table, int32_t n) {
+  if (!h || !table || n < 1 || n > h->rd.max_pages) return fail(PLM_ERR_INVALID, "plm_set_block_table: %d entries", n);
+  for (int i = 0; i < n; ++i)
+    if (table[i] < 0 || table[i] >= h->rd.num_pages)
+      return fail(PLM_ERR_INVALID, "plm_set_block_table: entry %d = %d outside the pool", i, table[i]);
+  return check_cuda(cudaMemcpy(h->block_table, table, size_t(n) * 4, cudaMemcpyHostToDevice), "block table");
+}
+
+int plm_set_aux_stream(plm_handle* h, const int64_t* cells, int64_t n, void* stream) {
+  if (!h || !cells || n < 1 || n > h->rd.aux_len) return fail(PLM_ERR_INVALID, "plm_set_aux_stream: n=%lld", (long long)n);
+  return check_cuda(cudaMemcpyAsync(h->aux_buf, cells, size_t(n) * 8, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
+                    "aux stream copy");
+}
+
+int plm_load_prompt(plm_handle* h, const int64_t* ids, int64_t n, void* stream) {
+  const int64_t cap = int64_t(h ? h->rd.max_pages : 0) * (h ? h->rd.page_size : 0);
+  if (!h || !ids || n < 1 || n > cap) return fail(PLM_ERR_INVALID, "plm_load_prompt: %lld tokens", (long long)n);
+  h->prompt_len = n;
+  return check_cuda(cudaMemcpyAsync(h->prompt, ids, size_t(n) * 8, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
+                    "prompt copy");
+}
+
+int plm_prefill(plm_handle* h, void* stream) {
+  if (!h || h->prompt_len < 1) return fail(PLM_ERR_INVALID, "plm_prefill: no prompt loaded");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int width = h->rd.max_prefill;
+  const int64_t n = h->prompt_len;
+  const int chunks = int((n + width - 1) / width);
+  if (chunks > 4096) return fail(PLM_ERR_INVALID, "plm_prefill: prompt too long");
+  if (n + 2 * h->W > int64_t(h->rd.max_pages) * h->rd.page_size)
+    return fail(PLM_ERR_INVALID, "plm_prefill: prompt of %lld leaves no room for a round", (long long)n);
+  std::vector<int64_t> offs(chunks);
+  for (int c = 0; c < chunks; ++c) offs[c] = int64_t(c) * width;
+  int st = check_cuda(cudaMemcpyAsync(h->chunk_offsets, offs.data(), chunks * 8, cudaMemcpyHostToDevice, s),
+                      "chunk offsets");
+  if (st != PLM_OK) return st;
+  for (int c = 0; c < chunks && st == PLM_OK; ++c) {
+    const int rows = int(std::min<int64_t>(width, n - offs[c]));
+    const bool last = c + 1 == chunks;
+    const int splits = attention_splits(h->m.num_heads, (rows + 63) / 64, h->ctx->num_sms, offs[c] + rows);
+    st = forward(h, kProloguePrefill, rows, h->chunk_offsets + c, nullptr, h->st_relaux, h->causal_depth,
+                 h->causal_own, splits, last ? int(n - 1 - offs[c]) : -1, s);
+  }
+  if (st == PLM_OK) st = lm_head(h, h->gathered, 1, 1, s);
+  if (st == PLM_OK) st = verify(h, 1, kBookFirstToken, nullptr, s);
+  return st;
+}
+
+int plm_round0(plm_handle* h, void* stream) {
+  if (!h) return fail(PLM_ERR_INVALID, "plm_round0: null handle");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = forward(h, kPrologueRound0, h->W, h->offset, h->r0_relpos, h->r0_relaux, h->r0_depth, h->r0_own,
+                   h->attn_splits_round, -1, s);
+  if (st == PLM_OK) st = lm_head(h, h->x_norm, h->W, 1, s);
+  if (st == PLM_OK) st = verify(h, 1, kBookRound0, h->base, s);
+  return st;
+}
+
+int plm_round(plm_handle* h, void* stream) {
+  if (!h) return fail(PLM_ERR_INVALID, "plm_round: null handle");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = forward(h, kPrologueSteady, h->W, h->offset, h->st_relpos, h->st_relaux, h->st_depth, h->st_own,
+                   h->attn_splits_round, -1, s);
+  if (st == PLM_OK) st = lm_head(h, h->x_norm, h->W, h->rd.k, s);
+  if (st == PLM_OK) st = verify(h, h->rd.k, kBookSteady, h->base, s);
+  return st;
+}
+
+int plm_state(plm_handle* h, plm_state_ptrs* p) {
+  if (!h || !p) return fail(PLM_ERR_INVALID, "plm_state: null argument");
+  p->out = h->out;
+  p->base = h->base;
+  p->offset = h->offset;
+  p->anchor = h->anchor;
+  p->pending = h->pending;
+  p->round_sequence = h->round_sequence;
+  p->sequence_step = h->sequence_step;
+  p->aux_buf = h->aux_buf;
+  p->block_table = h->block_table;
+  p->verify_logits = h->verify_logits;
+  p->best_val = h->best_val;
+  p->best_idx = h->best_idx;
+  p->verify = h->verify;
+  p->flags = h->flags;
+  p->hidden_normed = h->x_norm;
+  p->kv_cache = h->kv;
+  p->table = h->table;
+  p->out_capacity = h->rd.out_capacity;
+  p->seq_capacity = h->rd.seq_capacity;
+  p->aux_len = h->rd.aux_len;
+  p->plane_elems = int64_t(h->plane_elems);
+  p->width = h->W;
+  p->lm_tiles = h->lm_tiles;
+  p->row_capacity = h->R;
+  return PLM_OK;
+}
+
+int plm_check(plm_handle* h, int32_t* device_error) {
+  if (!h) return fail(PLM_ERR_INVALID, "plm_check: null handle");
+  return plm_ctx_check(h->ctx, device_error);
+}
+
+}  // extern "C"

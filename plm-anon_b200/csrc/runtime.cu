@@ -67,25 +67,15 @@ int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner,
   return PLM_OK;
 }
 
-void plan_splits(int tiles, int total_kb, int num_sms, int ctas_per_sm, int* splits, int* kb_per_split) {
-  const int slots = num_sms * ctas_per_sm;
-  int max_s = total_kb / 2;
-  if (max_s < 1) max_s = 1;
-  if (max_s > 32) max_s = 32;
-  int best = 1;
-  double best_eff = 0.0;
-  for (int s = 1; s <= max_s; ++s) {
-    const long ctas = long(tiles) * s;
-    const long waves = (ctas + slots - 1) / slots;
-    const double eff = double(ctas) / double(waves * slots);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
-      best = s;
-    }
+int gemm_cluster_splits(int tiles, int total_kb, int num_sms) {
+  int s = 1;
+  while (s < 8 && tiles * s < num_sms) {
+    const int next = 2 * s;
+    const int per = (total_kb + next - 1) / next;
+    if (next > total_kb || per * (next - 1) >= total_kb) break;  // every split needs at least one k-block
+    s = next;
   }
-  int per = (total_kb + best - 1) / best;
-  *kb_per_split = per;
-  *splits = (total_kb + per - 1) / per;
+  return s;
 }
 
 }  // namespace plm

@@ -35,25 +35,44 @@ int check_cuda(cudaError_t e, const char* what);
 int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
-// Split count for a weight-streaming launch of `tiles` output tiles over `total_kb` k-blocks, so that the grid
-// fills whole waves of `ctas_per_sm` resident CTAs per SM. Every split gets at least one k-block.
-void plan_splits(int tiles, int total_kb, int num_sms, int ctas_per_sm, int* splits, int* kb_per_split);
 
+// Launch with optional programmatic dependent launch and an optional cluster of `cluster_y` CTAs along y.
 template <typename... KArgs, typename... Args>
-cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                   Args&&... args) {
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      int cluster_y, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = unsigned(cluster_y);
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args&&... args) {
+  return launch_ex(kernel, grid, block, smem, stream, pdl, 1, std::forward<Args>(args)...);
+}
+
+// Cluster size for the k-split of a weight-streaming GEMM: the smallest power of two (<= 8, <= the k-blocks)
+// whose grid covers every SM once.
+int gemm_cluster_splits(int tiles, int total_kb, int num_sms);
 
 // Internal GEMM launch used by plm_gemm and by the round engine (`map_w` encoded once per weight).
 int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,

@@ -52,6 +52,7 @@ struct VerifyArgs {
   float* dbg_bias;           // [n_rows][top_m]
   float* dbg_stats;          // [n_rows][4] max, sum of exp, normaliser, unit
   int32_t* dbg_sigma;        // [n_rows] shortlist index of the decoded token
+  int64_t* dbg_phase_ns;     // [n_rows][8] %globaltimer at the end of each phase (nullable)
   Bookkeeping book;
   int* counter;              // arrival counter (zero between launches)
   int* err;

@@ -121,6 +121,10 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
 
   grid_dependency_wait();
   allow_dependents();
+  const uint64_t t_start = global_timer_ns();
+  auto phase = [&](int k) {
+    if (a.dbg_phase_ns != nullptr && tid == 0) a.dbg_phase_ns[r * 8 + k] = int64_t(global_timer_ns() - t_start);
+  };
 
   // ---------------- 1. softmax statistics and the acceptance rule ----------------
   const float* grow = a.logits + size_t(r) * a.logits_stride;
@@ -137,6 +141,7 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
   for (int i = tid; i < V; i += kVThreads) acc = acc + plm_expf(row[i] - mx);
   const float total = block_sum_f(acc, s->red_f);
   const float normaliser = mx + plm_logf(total);
+  phase(0);
 
   int flag = 0;
   if (r < a.n_accept && (a.rule == kRuleFloor || a.threshold > 0.0f)) {
@@ -162,6 +167,7 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
     }
   }
 
+  phase(1);
   // ---------------- 2a. exact top-M by radix select ----------------
   uint32_t prefix = 0, pmask = 0;
   int need = M;
@@ -169,9 +175,14 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
     const int shift = 24 - 8 * pass;
     for (int i = tid; i < 256; i += kVThreads) s->hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < V; i += kVThreads) {
-      const uint32_t u = orderable_key(row[i]);
-      if ((u & pmask) == prefix) atomicAdd(&s->hist[(u >> shift) & 255u], 1u);
+    // warp-aggregated: one shared-memory atomic per distinct digit per warp (most keys share the leading byte)
+    for (int base = 0; base < V; base += kVThreads) {
+      const int i = base + tid;
+      const uint32_t u = i < V ? orderable_key(row[i]) : 0u;
+      const bool match = i < V && (u & pmask) == prefix;
+      const uint32_t digit = match ? (u >> shift) & 255u : 256u;
+      const unsigned grp = __match_any_sync(0xffffffffu, digit);
+      if (match && lane == __ffs(grp) - 1) atomicAdd(&s->hist[digit], uint32_t(__popc(grp)));
     }
     __syncthreads();
     if (warp == 0) {
@@ -270,6 +281,7 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
   }
   __syncthreads();
 
+  phase(2);
   // ---------------- 2b. quota, spread, prior ----------------
   if (tid < M) s->prob[tid] = plm_expf(s->val[tid] - normaliser);
   __syncthreads();
@@ -330,6 +342,7 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
   }
   __syncthreads();
 
+  phase(3);
   // ---------------- 3. condense + annealed fit, `rounds` times ----------------
   const int threads_used = A < kVThreads ? A : kVThreads;
   const int ipt = A / threads_used;
@@ -362,6 +375,7 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
         }
       }
     }
+    if (rd == 0) phase(4);
     if (tid < M) {
       s->share[tid] = plm_logf(fmaxf(float(s->counts[tid]), 1e-9f));
       s->corr[tid] = 0.0f;
@@ -422,7 +436,9 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
     }
     if (tid < M) s->bias[tid] = s->offset[tid] + s->corr[tid];
     __syncthreads();
+    if (rd == 0) phase(5);
   }
+  phase(6);
 
   // ---------------- 4. the row's auxiliary cell ----------------
   if (warp == 0) {
@@ -461,6 +477,7 @@ __global__ void __launch_bounds__(kVThreads, 1) verify_decode_kernel(const Verif
       a.verify[r] = s->tok[bm];
       if (a.flags != nullptr) a.flags[r] = flag;
       if (a.dbg_sigma != nullptr) a.dbg_sigma[r] = bm;
+      if (a.dbg_phase_ns != nullptr) a.dbg_phase_ns[r * 8 + 7] = int64_t(global_timer_ns() - t_start);
       if (a.dbg_stats != nullptr) {
         a.dbg_stats[r * 4 + 0] = mx;
         a.dbg_stats[r * 4 + 1] = total;
@@ -668,6 +685,7 @@ extern "C" int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* d, void* s
   a.dbg_bias = d->dbg_bias;
   a.dbg_stats = d->dbg_stats;
   a.dbg_sigma = d->dbg_sigma;
+  a.dbg_phase_ns = d->dbg_phase_ns;
   const plm_bookkeeping& b = d->book;
   a.book = Bookkeeping{b.mode,       b.k,     b.best_val, b.best_idx,       b.n_tiles, b.rows,
                        b.out,        b.out_cap, b.base,   b.offset,         b.anchor,  b.pending,

@@ -64,7 +64,60 @@ class VerifyDesc(ctypes.Structure):
                 ("top_m", c_int32), ("shortlist", c_int32), ("rounds", c_int32), ("sweeps", c_int32),
                 ("epsilon", ctypes.c_double), ("refocus", ctypes.c_double), ("endpoint", ctypes.c_double),
                 ("verify", c_void_p), ("flags", c_void_p), ("dbg_tokens", c_void_p), ("dbg_counts", c_void_p),
-                ("dbg_bias", c_void_p), ("dbg_stats", c_void_p), ("dbg_sigma", c_void_p), ("book", Bookkeeping)]
+                ("dbg_bias", c_void_p), ("dbg_stats", c_void_p), ("dbg_sigma", c_void_p), ("dbg_phase_ns", c_void_p),
+                ("book", Bookkeeping)]
+
+
+class AttentionDesc(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("q", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+                ("block_table", c_void_p), ("max_pages", c_int32), ("num_pages", c_int32), ("page_size", c_int32),
+                ("offset", c_void_p), ("rows", c_int32), ("depth", c_void_p), ("own_start", c_void_p),
+                ("num_heads", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32), ("out", c_void_p),
+                ("splits", c_int32), ("max_keys", c_int64)]
+
+
+class KvAppendDesc(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("k", c_void_p), ("v", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+                ("block_table", c_void_p), ("max_pages", c_int32), ("num_pages", c_int32), ("page_size", c_int32),
+                ("offset", c_void_p), ("rows", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32)]
+
+
+class AddRmsNormDesc(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("x", c_void_p), ("residual", c_void_p), ("normed", c_void_p),
+                ("weight", c_void_p), ("rows", c_int32), ("hidden", c_int32), ("eps", ctypes.c_float),
+                ("gather_row", c_int32), ("gathered", c_void_p)]
+
+
+class ModelDesc(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("num_layers", c_int32), ("hidden", c_int32), ("num_heads", c_int32),
+                ("num_kv_heads", c_int32), ("head_dim", c_int32), ("intermediate", c_int32), ("vocab", c_int32),
+                ("aux_vocab", c_int32), ("num_aux_tokens", c_int32), ("rms_eps", ctypes.c_float),
+                ("max_pos", c_int32), ("top_m", c_int32), ("shortlist", c_int32), ("rounds", c_int32),
+                ("sweeps", c_int32), ("epsilon", ctypes.c_double), ("refocus", ctypes.c_double),
+                ("endpoint", ctypes.c_double)]
+
+
+class WeightPtrs(ctypes.Structure):
+    _fields_ = [("embed", c_void_p), ("lm_head", c_void_p), ("final_norm", c_void_p), ("aux_vocab", c_void_p),
+                ("mask_aux", c_void_p), ("cos_sin", c_void_p), ("qkv", POINTER(c_void_p)), ("o", POINTER(c_void_p)),
+                ("gate_up", POINTER(c_void_p)), ("down", POINTER(c_void_p)), ("input_norm", POINTER(c_void_p)),
+                ("post_norm", POINTER(c_void_p)), ("table", c_void_p)]
+
+
+class RoundDesc(ctypes.Structure):
+    _fields_ = [("k", c_int32), ("rule", c_int32), ("threshold", ctypes.c_float), ("page_size", c_int32),
+                ("num_pages", c_int32), ("max_pages", c_int32), ("out_capacity", c_int64),
+                ("seq_capacity", c_int64), ("aux_len", c_int64), ("max_prefill", c_int32)]
+
+
+class StatePtrs(ctypes.Structure):
+    _fields_ = [("out", c_void_p), ("base", c_void_p), ("offset", c_void_p), ("anchor", c_void_p),
+                ("pending", c_void_p), ("round_sequence", c_void_p), ("sequence_step", c_void_p),
+                ("aux_buf", c_void_p), ("block_table", c_void_p), ("verify_logits", c_void_p),
+                ("best_val", c_void_p), ("best_idx", c_void_p), ("verify", c_void_p), ("flags", c_void_p),
+                ("hidden_normed", c_void_p), ("kv_cache", c_void_p), ("table", c_void_p),
+                ("out_capacity", c_int64), ("seq_capacity", c_int64), ("aux_len", c_int64), ("plane_elems", c_int64),
+                ("width", c_int32), ("lm_tiles", c_int32), ("row_capacity", c_int32)]
 
 
 _lib: ctypes.CDLL | None = None
@@ -79,6 +132,19 @@ _SIGNATURES: dict[str, list] = {
     "plm_gemm_tiles": [c_int32, c_int32, c_int32, POINTER(c_int32)],
     "plm_gemm": [c_void_p, POINTER(GemmDesc), c_void_p],
     "plm_verify_decode": [c_void_p, POINTER(VerifyDesc), c_void_p],
+    "plm_attention": [c_void_p, POINTER(AttentionDesc), c_void_p],
+    "plm_kv_append": [c_void_p, POINTER(KvAppendDesc), c_void_p],
+    "plm_add_rmsnorm": [c_void_p, POINTER(AddRmsNormDesc), c_void_p],
+    "plm_create": [POINTER(ModelDesc), POINTER(WeightPtrs), POINTER(RoundDesc), POINTER(c_void_p)],
+    "plm_destroy": [c_void_p],
+    "plm_set_block_table": [c_void_p, POINTER(c_int32), c_int32],
+    "plm_set_aux_stream": [c_void_p, c_void_p, c_int64, c_void_p],
+    "plm_load_prompt": [c_void_p, c_void_p, c_int64, c_void_p],
+    "plm_prefill": [c_void_p, c_void_p],
+    "plm_round0": [c_void_p, c_void_p],
+    "plm_round": [c_void_p, c_void_p],
+    "plm_state": [c_void_p, POINTER(StatePtrs)],
+    "plm_check": [c_void_p, POINTER(c_int32)],
 }
 
 
@@ -173,3 +239,89 @@ def gemm(ctx: Context, w, x, rows: int, *, out=None, epi: GemmEpilogue | None = 
 def verify_decode(ctx: Context, desc: VerifyDesc, stream=None) -> None:
     """Enqueue plm_verify_decode (one CTA per row)."""
     check(library().plm_verify_decode(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_verify_decode")
+
+
+def attention(ctx: Context, desc: AttentionDesc, stream=None) -> None:
+    check(library().plm_attention(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_attention")
+
+
+def kv_append(ctx: Context, desc: KvAppendDesc, stream=None) -> None:
+    check(library().plm_kv_append(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_kv_append")
+
+
+def add_rmsnorm(ctx: Context, desc: AddRmsNormDesc, stream=None) -> None:
+    check(library().plm_add_rmsnorm(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_add_rmsnorm")
+
+
+class _DeviceArray:
+    """A zero-copy torch view of device memory owned by a handle (``__cuda_array_interface__``)."""
+
+    def __init__(self, address: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (address, False), "version": 3,
+                                         "strides": None}
+
+
+def device_view(address: int, shape: tuple, dtype):
+    """torch tensor aliasing ``shape`` elements of ``dtype`` at a device address (no copy, not owned)."""
+    import torch
+
+    typestr = {torch.int64: "<i8", torch.int32: "<i4", torch.float32: "<f4", torch.bfloat16: "<V2"}[dtype]
+    if dtype == torch.bfloat16:
+        raw = torch.as_tensor(_DeviceArray(address, shape, "<i2"), device="cuda")
+        return raw.view(torch.bfloat16)
+    return torch.as_tensor(_DeviceArray(address, shape, typestr), device="cuda")
+
+
+class Handle:
+    """A plm_handle: the round engine of one request stream on the current GPU."""
+
+    def __init__(self, model: ModelDesc, weights: WeightPtrs, round_desc: RoundDesc, keepalive=()) -> None:
+        handle = c_void_p()
+        self._keepalive = keepalive  # weight pointer arrays and tensors the handle borrows
+        check(library().plm_create(ctypes.byref(model), ctypes.byref(weights), ctypes.byref(round_desc),
+                                   ctypes.byref(handle)), "plm_create")
+        self.handle = handle
+        self.model, self.round_desc = model, round_desc
+
+    def state(self) -> StatePtrs:
+        p = StatePtrs()
+        check(library().plm_state(self.handle, ctypes.byref(p)), "plm_state")
+        return p
+
+    def set_block_table(self, table) -> None:
+        arr = (c_int32 * len(table))(*[int(v) for v in table])
+        check(library().plm_set_block_table(self.handle, arr, len(table)), "plm_set_block_table")
+
+    def set_aux_stream(self, cells, stream=None) -> None:
+        check(library().plm_set_aux_stream(self.handle, cells.data_ptr(), cells.numel(), stream_handle(stream)),
+              "plm_set_aux_stream")
+
+    def load_prompt(self, ids, stream=None) -> None:
+        check(library().plm_load_prompt(self.handle, ids.data_ptr(), ids.numel(), stream_handle(stream)),
+              "plm_load_prompt")
+
+    def prefill(self, stream=None) -> None:
+        check(library().plm_prefill(self.handle, stream_handle(stream)), "plm_prefill")
+
+    def round0(self, stream=None) -> None:
+        check(library().plm_round0(self.handle, stream_handle(stream)), "plm_round0")
+
+    def round(self, stream=None) -> None:
+        check(library().plm_round(self.handle, stream_handle(stream)), "plm_round")
+
+    def check(self) -> None:
+        code = c_int32(0)
+        check(library().plm_check(self.handle, ctypes.byref(code)), "plm_check")
+        if code.value:
+            raise NativeError(f"device error {code.value}: {DEVICE_ERRORS.get(code.value, 'unknown')}")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            library().plm_destroy(self.handle)
+            self.handle = c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,302 @@
+"""Generates the golden fixtures of tests/golden/ from the reference itself (run in the build container only).
+
+    python tests/golden/make_golden.py --reference /path/to/PLM-anon [--out tests/golden]
+
+The reference (justuswill/PLM-anon) has no CPU round path and no test fixtures of its own, so the fixtures come from
+running its own functions on the CPU:
+  layout.json       plm.mask.round_layout and RoundMaskView for several round shapes;
+  quota.npz         plm.iterate.quota on random weights;
+  accept.npz        plm.decoder.nucleus_acceptance / floor_acceptance on seeded logits;
+  epilogue.npz      RoundDecoder._epilogue (steady round bookkeeping) and _prologue (ids, aux cells, embeddings,
+                    positions, slots), called unbound on CPU tensors with a stand-in ``self``;
+  voronoi.npz       Voronoi.assign through LogitVoronoiAuxiliary (plm/iterate.py, plm/auxiliary.py) with the Triton
+                    kernels run by the Triton interpreter (TRITON_INTERPRET=1; autotuning bypassed with fixed launch
+                    meta GROUP=8, BLOCK=32; the compiled argmin replaced by its eager implementation);
+  llama.npz         the Llama forward of Hugging Face transformers (LlamaForCausalLM, eager attention, fp32) over a
+                    prompt plus one round under the round mask, pinning the oracle's paged forward.
+Inputs that are large (logits rows, cost tables, model weights) are regenerated from the stored seeds by torch's CPU
+generator, which is deterministic across machines; fixtures store their checksums so tests can confirm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import types
+from pathlib import Path
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+
+
+# ---------------------------------------------------------------- shared input recipes (also used by the tests)
+def voronoi_inputs(seed: int, n_rows: int, vocab: int, aux: int, kind: str):
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(n_rows, vocab, generator=g) * 2.0
+    if kind == "bf16":
+        logits = logits.bfloat16().float()
+    table = (torch.randn(vocab, aux, generator=g) * 0.3).bfloat16()
+    return logits, table
+
+
+def epilogue_logits(case: int, width: int, vocab: int):
+    g = torch.Generator().manual_seed(4000 + case)
+    return (torch.randn(width, vocab, generator=g) * 2).bfloat16().float()
+
+
+def accept_inputs(seed: int, n_rows: int, vocab: int):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(n_rows, vocab, generator=g) * 2.0).bfloat16().float()
+
+
+def llama_weights(seed: int, layers: int, hidden: int, heads: int, kv_heads: int, head_dim: int, inter: int,
+                  vocab: int):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g) * 0.02  # noqa: E731
+    q_size, kv_size = heads * head_dim, kv_heads * head_dim
+    w = {"embed": r(vocab + 1, hidden), "lm_head": r(vocab, hidden), "final_norm": 1 + r(hidden),
+         "aux_vocab": r(64, hidden), "mask_aux": r(hidden), "qkv": [], "o": [], "gate_up": [], "down": [],
+         "input_norm": [], "post_norm": []}
+    for _ in range(layers):
+        w["qkv"].append(r(q_size + 2 * kv_size, hidden))
+        w["o"].append(r(hidden, q_size))
+        w["gate_up"].append(r(2 * inter, hidden))
+        w["down"].append(r(hidden, inter))
+        w["input_norm"].append(1 + r(hidden))
+        w["post_norm"].append(1 + r(hidden))
+    return w
+
+
+LLAMA = dict(seed=11, layers=2, hidden=256, heads=2, kv_heads=1, head_dim=128, inter=512, vocab=512)
+VORONOI_CASES = [  # seed, rows, vocab, aux, kind
+    (100, 2, 50257, 1024, "fp32"), (101, 2, 50257, 1024, "bf16"), (102, 3, 3000, 256, "fp32"),
+    (103, 2, 8000, 512, "bf16"),
+]
+ACCEPT_CASES = [(200, 6, 50257), (201, 6, 4096)]
+
+
+def checksum(t: torch.Tensor) -> float:
+    return float(t.double().abs().sum())
+
+
+# ---------------------------------------------------------------- generators
+def gen_layout(ref, out: Path):
+    from plm.mask import RoundMask, round_layout
+
+    cases = {}
+    for blocks in ([4] * 4, [6] * 6, [7] * 7, [8] * 8, [10] * 10, [55], [41], [1, 2, 3]):
+        rel_positions, rel_aux, depth, own = round_layout(blocks, torch.device("cpu"))
+        w = depth.numel()
+        mask = RoundMask(w, torch.device("cpu"))
+        mask.depth[:w].copy_(depth)
+        mask.own_start[:w].copy_(own)
+        offset = 37
+        mask.offset.fill_(offset)
+        q = torch.arange(offset, offset + w)[:, None]
+        kv = torch.arange(0, offset + w)[None, :]
+        visible = mask.view(torch.zeros(1), torch.zeros(1), q, kv)
+        cases[",".join(map(str, blocks))] = {
+            "rel_positions": rel_positions.tolist(), "rel_aux": rel_aux.tolist(), "depth": depth.tolist(),
+            "own_start": own.tolist(), "offset": offset,
+            "visible_rows": ["".join("1" if v else "0" for v in row) for row in visible.tolist()]}
+    (out / "layout.json").write_text(json.dumps(cases))
+
+
+def gen_quota(ref, out: Path):
+    from plm.iterate import quota
+
+    g = torch.Generator().manual_seed(300)
+    weights = torch.rand(16, 128, generator=g) ** 4
+    weights = weights / weights.sum(-1, keepdim=True)
+    totals = [1024, 256, 4096, 7]
+    counts = np.stack([quota(weights, t).numpy() for t in totals])
+    np.savez_compressed(out / "quota.npz", weights=weights.numpy(), totals=np.asarray(totals), counts=counts)
+
+
+def gen_accept(ref, out: Path):
+    from plm.decoder import floor_acceptance, nucleus_acceptance
+
+    rows = {}
+    for seed, n, vocab in ACCEPT_CASES:
+        logits = accept_inputs(seed, n, vocab)
+        order = torch.argsort(logits, dim=-1, descending=True)
+        ranks = torch.tensor([0, 1, 4, 30, 300, 3000])[:n]
+        pending = order[torch.arange(n), ranks]
+        res = {}
+        for name, fn, thr in (("nucleus_0.94", nucleus_acceptance, 0.94), ("nucleus_0.5", nucleus_acceptance, 0.5),
+                              ("exact", nucleus_acceptance, -1.0), ("floor_2e-3", floor_acceptance, 2e-3),
+                              ("floor_1e-4", floor_acceptance, 1e-4)):
+            res[name] = fn(logits, pending, torch.tensor(thr, dtype=torch.float32)).numpy()
+        rows[f"{seed}"] = {"pending": pending.numpy(), "checksum": checksum(logits), **res}
+    flat = {f"{seed}/{key}": np.asarray(value) for seed, d in rows.items() for key, value in d.items()}
+    np.savez_compressed(out / "accept.npz", **flat)
+
+
+def gen_epilogue(ref, out: Path):
+    """RoundDecoder._prologue / _epilogue of plm/decoder.py, unbound, on CPU tensors."""
+    from plm.auxiliary import LogitVoronoiAuxiliary
+    from plm.decoder import RoundDecoder
+    from plm.mask import round_layout
+
+    records = {}
+    g = torch.Generator().manual_seed(400)
+    k, vocab, hidden, aux, bs = 7, 50257, 64, 1024, 16
+    width = k + k * k
+    scheme = LogitVoronoiAuxiliary(aux, hidden, vocab)
+    scheme.auxiliary_vocabulary.copy_(torch.randn(aux, hidden, generator=g))
+    scheme.mask_auxiliary.data.copy_(torch.randn(hidden, generator=g))
+    embed_weight = torch.randn(vocab + 1, hidden, generator=g)
+    for case, (nc_target, rule, thr) in enumerate([(0, "nucleus", -1.0), (3, "nucleus", -1.0), (6, "nucleus", -1.0),
+                                                   (2, "nucleus", 0.94), (1, "floor", 2e-3)]):
+        fake = types.SimpleNamespace(k=k, width=width, block_size=bs, vocab=vocab, sentinel=aux, num_aux_tokens=1,
+                                     scheme=scheme, accept_rule=rule, sequence_capacity=64)
+        logits = epilogue_logits(case, width, vocab)
+        verify = torch.randint(0, vocab, (k,), generator=g)
+        pending = torch.where(torch.arange(k - 1) < nc_target, verify[: k - 1], (verify[: k - 1] + 1) % vocab)
+        anchor = torch.tensor([123])
+        out_t = torch.full((512,), -1, dtype=torch.long)
+        out_t[:40] = torch.arange(40)
+        base_t = torch.tensor(40)
+        offset_t = torch.tensor(300)
+        round_sequence = torch.zeros(64, dtype=torch.long)
+        sequence_step = torch.tensor([5])
+        aux_buf = torch.randint(0, aux, (8192,), generator=g)
+        rel_positions, rel_aux, _, _ = round_layout([k] * k, torch.device("cpu"))
+        ids = torch.empty(width, dtype=torch.long)
+        seq_lens, decode_offset = torch.zeros(1, dtype=torch.int32), torch.zeros(1, dtype=torch.int32)
+        slot_mapping, kv_num_blocks = torch.zeros(width, dtype=torch.long), torch.zeros(1, dtype=torch.int32)
+        mask_offset = torch.zeros((), dtype=torch.long)
+        embeds, positions = RoundDecoder._prologue(
+            fake, offset_t, base_t, anchor, pending.clone(), aux_buf, rel_positions, rel_aux, ids, mask_offset,
+            seq_lens, decode_offset, slot_mapping, kv_num_blocks, torch.arange(width), embed_weight)
+        pre = {"ids": ids.clone(), "positions": positions, "slot_mapping": slot_mapping.clone(),
+               "embeds_checksum": torch.tensor(checksum(embeds)), "seq_lens": seq_lens.clone(),
+               "kv_num_blocks": kv_num_blocks.clone()}
+        pend = pending.clone()
+        RoundDecoder._epilogue(fake, logits, verify, pend, anchor, out_t, base_t, offset_t, torch.arange(k),
+                               torch.tensor(thr, dtype=torch.float32), torch.ones(1, dtype=torch.long), round_sequence,
+                               sequence_step)
+        post = {"out": out_t, "base": base_t, "offset": offset_t, "anchor": anchor, "pending": pend,
+                "round_sequence": round_sequence, "sequence_step": sequence_step}
+        inputs = {"logits_checksum": torch.tensor(checksum(logits)), "verify": verify, "pending_in": pending,
+                  "aux_buf": aux_buf, "rule": torch.tensor(0 if rule == "nucleus" else 1),
+                  "threshold": torch.tensor(thr)}
+        for key, value in {**pre, **post, **inputs}.items():
+            records[f"{case}/{key}"] = value.numpy() if isinstance(value, torch.Tensor) else np.asarray(value)
+    records["embed_weight_checksum"] = np.asarray(checksum(embed_weight))
+    np.savez_compressed(out / "epilogue.npz", **records)
+
+
+def gen_voronoi(ref, out: Path):
+    import plm.iterate as it
+    from plm.auxiliary import LogitVoronoiAuxiliary
+
+    class Fixed:
+        def __init__(self, fn, **meta):
+            self.fn, self.meta = fn, meta
+
+        def __getitem__(self, grid):
+            return lambda *a, **kw: self.fn[grid](*a, **{**self.meta, **kw})
+
+    it._scan_kernel = Fixed(it._scan_kernel.fn, GROUP=8, num_warps=4)
+    it._condense_kernel = Fixed(it._condense_kernel.fn, BLOCK=32, num_warps=4)
+    it._fused_argmin = it._argmin_impl
+    records = {}
+    for seed, n, vocab, aux, kind in VORONOI_CASES:
+        logits, table = voronoi_inputs(seed, n, vocab, aux, kind)
+        engine = it.Voronoi.from_table(table)
+        a = engine.assign(logits, n_targets=128, k=8, rounds=2, iterations=12)
+        cells = torch.randint(0, aux, (n,), generator=torch.Generator().manual_seed(seed + 1))
+        scheme = LogitVoronoiAuxiliary(aux, 8, vocab)
+        scheme._engine, scheme._cached_key = engine, None
+        decoded = a.tokens.gather(1, a.sigma.gather(1, cells[:, None])).squeeze(1)
+        key = f"{seed}"
+        records.update({f"{key}/tokens": a.tokens.numpy(), f"{key}/counts": a.counts.numpy(),
+                        f"{key}/sigma": a.sigma.numpy().astype(np.int16), f"{key}/bias": a.bias.numpy(),
+                        f"{key}/cells": cells.numpy(), f"{key}/decoded": decoded.numpy(),
+                        f"{key}/logits_checksum": np.asarray(checksum(logits)),
+                        f"{key}/table_checksum": np.asarray(checksum(table.float()))})
+        print(f"voronoi case {seed}: done", flush=True)
+    np.savez_compressed(out / "voronoi.npz", **records)
+
+
+def gen_llama(ref, out: Path):
+    """HF LlamaForCausalLM (fp32, eager attention) on [prompt + one round] under the round mask."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from plm.mask import RoundMask, round_layout
+
+    c = LLAMA
+    w = llama_weights(c["seed"], c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                      c["vocab"])
+    cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["inter"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"],
+                      head_dim=c["head_dim"], rms_norm_eps=1e-5, max_position_embeddings=4096,
+                      tie_word_embeddings=False, attention_bias=False, mlp_bias=False)
+    cfg._attn_implementation = "eager"
+    model = LlamaForCausalLM(cfg).eval()
+    q_size, kv_size = c["heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+    with torch.no_grad():
+        model.model.embed_tokens.weight.copy_(w["embed"][: c["vocab"]])
+        model.lm_head.weight.copy_(w["lm_head"])
+        model.model.norm.weight.copy_(w["final_norm"])
+        for i, layer in enumerate(model.model.layers):
+            q, k, v = w["qkv"][i].split([q_size, kv_size, kv_size])
+            layer.self_attn.q_proj.weight.copy_(q)
+            layer.self_attn.k_proj.weight.copy_(k)
+            layer.self_attn.v_proj.weight.copy_(v)
+            layer.self_attn.o_proj.weight.copy_(w["o"][i])
+            gate, up = w["gate_up"][i].split([c["inter"], c["inter"]])
+            layer.mlp.gate_proj.weight.copy_(gate)
+            layer.mlp.up_proj.weight.copy_(up)
+            layer.mlp.down_proj.weight.copy_(w["down"][i])
+            layer.input_layernorm.weight.copy_(w["input_norm"][i])
+            layer.post_attention_layernorm.weight.copy_(w["post_norm"][i])
+    k_round, prompt_len = 4, 24
+    rel_positions, _, depth, own = (t.numpy() for t in round_layout([k_round] * k_round, torch.device("cpu")))
+    width = rel_positions.size
+    round_mask = RoundMask(width, torch.device("cpu"))
+    round_mask.depth[:width].copy_(torch.as_tensor(depth))
+    round_mask.own_start[:width].copy_(torch.as_tensor(own))
+    round_mask.offset.fill_(prompt_len)
+    g = torch.Generator().manual_seed(c["seed"] + 1)
+    embeds = torch.randn(prompt_len + width, c["hidden"], generator=g) * 0.02
+    total = prompt_len + width
+    allowed = np.zeros((total, total), dtype=bool)
+    allowed[:prompt_len, :prompt_len] = np.tril(np.ones((prompt_len, prompt_len), dtype=bool))
+    q_idx = torch.arange(prompt_len, total)[:, None]
+    kv_idx = torch.arange(total)[None, :]
+    allowed[prompt_len:, :] = round_mask.view(None, None, q_idx, kv_idx).numpy()
+    mask = torch.where(torch.as_tensor(allowed), 0.0, torch.finfo(torch.float32).min)[None, None]
+    positions = torch.as_tensor(np.concatenate([np.arange(prompt_len), prompt_len + rel_positions]))[None]
+    with torch.no_grad():
+        logits = model(inputs_embeds=embeds[None], attention_mask=mask, position_ids=positions).logits[0]
+    np.savez_compressed(out / "llama.npz", logits=logits.numpy(), embeds=embeds.numpy(), k=k_round,
+                        prompt_len=prompt_len, **{f"cfg_{key}": value for key, value in c.items()})
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--reference", required=True, help="checkout of justuswill/PLM-anon")
+    parser.add_argument("--out", default=str(HERE))
+    parser.add_argument("--only", nargs="*", default=None)
+    args = parser.parse_args()
+    sys.path.insert(0, args.reference)
+    out = Path(args.out)
+    out.mkdir(parents=True, exist_ok=True)
+    gens = {"layout": gen_layout, "quota": gen_quota, "accept": gen_accept, "epilogue": gen_epilogue,
+            "voronoi": gen_voronoi, "llama": gen_llama}
+    for name, fn in gens.items():
+        if args.only is None or name in args.only:
+            fn(args.reference, out)
+            print(f"{name}: written", flush=True)
+
+
+if __name__ == "__main__":
+    main()

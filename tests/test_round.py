@@ -1,0 +1,180 @@
+"""The whole round on the GPU (RoundDecoder over libplm_native.so) against the CPU oracle.
+
+Teacher-forced parity, stage by stage (prefill, round 0, steady rounds): both sides run the forward on the same
+state; the GPU's logits must match the oracle's within bf16 tolerance (max abs error <= 2e-2), the final-norm hidden
+rows within 2e-2 + 2 bf16 ulps (2^-6 relative: those values reach |x| >= 4, where one bf16 ulp is 0.031), and
+the GPU's verify decode, acceptance and bookkeeping must equal the oracle's run on the GPU's own fp32 logits, bit
+for bit (output tokens, base, offset, anchor, pending, accepted-count record).
+A free-running comparison reports the end-to-end token agreement rate.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as omodel
+from oracle import rounds as orounds
+from oracle import voronoi as ov
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+HREL = 2.0 ** -6
+
+
+def _argmax_partials(decoder, rows: int) -> np.ndarray:
+    return np.asarray(decoder.proposal_argmax(rows), dtype=np.int64)
+
+
+def _pair(shape: str, k: int, page: int, seed: int, rule="nucleus", threshold=None, max_model_len=1024, **over):
+    from plm.decoder import RoundDecoder
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config(shape, **over)
+    weights = PLMWeights.random(cfg, seed=seed)
+    probe_pages = -(-(max_model_len + 2 * (k + k * k) + page) // page)
+    rng = np.random.default_rng(seed)
+    num_pages = probe_pages + 8
+    table = rng.permutation(num_pages)[:probe_pages].astype(np.int32)
+    page_bytes = cfg.num_layers * 2 * cfg.num_kv_heads * page * cfg.head_dim * 2
+    decoder = RoundDecoder(weights, k, rule, threshold, block_size=page, kv_cache_bytes=num_pages * page_bytes,
+                           max_model_len=max_model_len, block_table=table.tolist())
+    assert decoder.num_pages == num_pages and decoder.max_pages == probe_pages
+    shape_o = omodel.ModelShape(cfg.num_layers, cfg.hidden, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                                cfg.intermediate, cfg.vocab, cfg.aux_vocab, cfg.num_aux_tokens, cfg.rms_eps,
+                                cfg.rope_theta, decoder.cos_sin.shape[0])
+    named = {key: ([t.cpu() for t in v] if isinstance(v, list) else v.cpu()) for key, v in weights.named().items()}
+    oracle_model = omodel.OracleModel(shape_o, named, "bfloat16", page, num_pages, table, cos_sin=decoder.cos_sin.cpu())
+    decoder._fill_aux(seed)
+    aux = decoder.aux_buf.cpu().numpy().copy()
+    table_np = decoder.table.float().cpu().numpy()
+    oracle = omodel.RoundOracle(oracle_model, table_np, k, rule, threshold,
+                                ov.VoronoiConfig(cfg.top_m, cfg.shortlist, cfg.rounds, cfg.sweeps),
+                                capacity=decoder.out.numel(), aux_stream=aux)
+    return decoder, oracle, cfg
+
+
+def _gpu_state(decoder):
+    return {"out": decoder.out.cpu().numpy(), "base": int(decoder.base_t), "offset": int(decoder.offset_t),
+            "anchor": int(decoder.anchor[0]), "pending": decoder.pending.cpu().numpy()}
+
+
+def _assert_state(decoder, state: orounds.RoundState):
+    g = _gpu_state(decoder)
+    np.testing.assert_array_equal(g["out"], state.out)
+    assert (g["base"], g["offset"], g["anchor"]) == (state.base, state.offset, state.anchor)
+    np.testing.assert_array_equal(g["pending"], state.pending)
+
+
+def _close(name, gpu, ref, report, rel=0.0):
+    gpu, ref = np.asarray(gpu, dtype=np.float64), np.asarray(ref, dtype=np.float64)
+    diff = np.abs(gpu - ref)
+    err = float(diff.max())
+    report.setdefault(name, []).append(err)
+    bound = TOL + rel * np.abs(ref)
+    worst = int(np.argmax(diff - bound))
+    assert (diff <= bound).all(), f"{name}: error {diff.flat[worst]:.4g} > {bound.flat[worst]:.4g} (max abs {err:.4g})"
+
+
+@pytest.mark.parametrize("shape,k,page,rule,threshold,overrides", [
+    ("plm-tiny", 7, 16, "nucleus", None, {}),
+    ("plm-tiny", 6, 32, "floor", 2e-3, {"vocab": 8192, "aux_vocab": 256}),
+    ("plm-tiny", 4, 16, "nucleus", 0.94, {"num_kv_heads": 1, "head_dim": 128, "aux_vocab": 512}),
+    ("plm-80m", 6, 16, "nucleus", None, {"num_layers": 2}),
+    ("plm-1.3b", 7, 16, "nucleus", None, {}),
+])
+def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides):
+    decoder, oracle, cfg = _pair(shape, k, page, seed=3, rule=rule, threshold=threshold, **overrides)
+    report = {}
+    prompt = torch.randint(0, cfg.vocab, (64,), generator=torch.Generator().manual_seed(5))
+    W = decoder.width
+
+    # prefill + first token
+    decoder.handle.load_prompt(prompt.pin_memory())
+    decoder.handle.prefill()
+    decoder.check()
+    hidden_o, logits_o = oracle.prefill_forward(prompt.numpy())
+    gpu_logits = decoder.verify_logits[0].cpu().numpy()
+    _close("prefill logits", gpu_logits, logits_o[0], report)
+    _close("prefill hidden", decoder.hidden_normed[63].float().cpu().numpy(), hidden_o[0].numpy(), report, HREL)
+    oracle.commit_first(gpu_logits, 64)
+    _assert_state(decoder, oracle.state)
+
+    # round 0
+    decoder.handle.round0()
+    decoder.check()
+    hidden_o, logits_o = oracle.round0_forward()
+    gpu_logits = decoder.verify_logits[0].cpu().numpy()
+    _close("round0 logits", gpu_logits, logits_o[0], report)
+    _close("round0 hidden", decoder.hidden_normed[:W].float().cpu().numpy(), hidden_o.numpy(), report, HREL)
+    oracle.commit_round0(gpu_logits[None], _argmax_partials(decoder, W)[1:])
+    _assert_state(decoder, oracle.state)
+
+    # steady rounds
+    seq0 = int(decoder.sequence_step[0])
+    for _ in range(6 if cfg.num_layers <= 12 else 2):
+        decoder.handle.round()
+        decoder.check()
+        hidden_o, logits_o = oracle.round_forward()
+        gpu_logits = decoder.verify_logits.cpu().numpy()
+        _close("round logits", gpu_logits, logits_o[:k], report)
+        _close("round hidden", decoder.hidden_normed[:W].float().cpu().numpy(), hidden_o.numpy(), report, HREL)
+        oracle.commit_round(gpu_logits, _argmax_partials(decoder, W)[k:])
+        _assert_state(decoder, oracle.state)
+    record = decoder.round_sequence[seq0:int(decoder.sequence_step[0])].cpu().numpy().tolist()
+    assert record == oracle.state.round_sequence
+    out_dir = os.environ.get("PLM_PARITY_REPORT")
+    if out_dir:
+        with open(os.path.join(out_dir, f"parity_{shape}_k{k}_{rule}.json"), "w") as f:
+            json.dump({key: max(v) for key, v in report.items()}, f)
+
+
+def test_round_token_agreement_free_running():
+    """Both sides decode on their own logits; the agreement rate of the output tokens is reported (the two forwards
+    round differently, so a rare flip of a near-tie decision makes the sequences diverge from there on)."""
+    decoder, oracle, cfg = _pair("plm-tiny", 7, 16, seed=9)
+    prompt = torch.randint(0, cfg.vocab, (64,), generator=torch.Generator().manual_seed(6))
+    decoder.handle.load_prompt(prompt.pin_memory())
+    decoder.handle.prefill()
+    decoder.handle.round0()
+    oracle.prefill(prompt.numpy())
+    oracle.round0()
+    for _ in range(12):
+        decoder.handle.round()
+        oracle.round()
+    decoder.check()
+    n = min(int(decoder.base_t), oracle.state.base)
+    gpu_tokens = decoder.out[:n].cpu().numpy()
+    agree = float((gpu_tokens == oracle.state.out[:n]).mean())
+    first_diff = int(np.argmax(gpu_tokens != oracle.state.out[:n])) if agree < 1 else n
+    print(f"token agreement {agree:.3f} over {n} tokens, first divergence at {first_diff}")
+    out_dir = os.environ.get("PLM_PARITY_REPORT")
+    if out_dir:
+        with open(os.path.join(out_dir, "agreement_plm-tiny.json"), "w") as f:
+            json.dump({"agreement": agree, "tokens": n, "first_divergence": first_diff}, f)
+    assert n >= 14
+
+
+def test_decoder_generate_end_to_end():
+    """RoundDecoder.generate through the captured graph: deterministic per seed, the documented record schema."""
+    from plm.decoder import RoundDecoder
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config("plm-tiny")
+    weights = PLMWeights.random(cfg, seed=1)
+    decoder = RoundDecoder(weights, 7, block_size=16, kv_cache_bytes=64 << 20, max_model_len=1024)
+    decoder.prepare()
+    prompt = list(range(100, 164))
+    a = decoder.generate(prompt, 40, seed=0, stop_at_eos=False)
+    b = decoder.generate(prompt, 40, seed=0, stop_at_eos=False)
+    c = decoder.generate(prompt, 40, seed=1, stop_at_eos=False)
+    decoder.check()
+    assert a.token_ids == b.token_ids and len(a.token_ids) == 40
+    assert all(0 <= t < cfg.vocab for t in a.token_ids)
+    assert a.token_ids != c.token_ids
+    assert a.steady_rounds >= 1 and a.steady_tokens >= a.steady_rounds
