@@ -117,6 +117,19 @@ def round_bytes(cfg, ctx: float, k: int) -> dict:
             "logits": logits, "total": weights + kv_read + kv_write + embed + voronoi + logits}
 
 
+def reduce_over_ranks(dist, elapsed_ms: float, tokens: float, device: str = "cuda") -> tuple[float, float]:
+    """Replicas only: the job's time is the slowest rank's, its tokens the sum over ranks."""
+    import torch
+
+    if dist is None:
+        return float(elapsed_ms), float(tokens)
+    mx = torch.tensor([float(elapsed_ms)], dtype=torch.float64, device=device)
+    sm = torch.tensor([float(tokens)], dtype=torch.float64, device=device)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return float(mx[0]), float(sm[0])
+
+
 def _dist():
     import torch
 
@@ -339,14 +352,7 @@ def run_native(args) -> None:
     decoder.check()
     tokens = int(decoder.base_t) - base0
     ctx_mean = (ctx0 + int(decoder.offset_t)) / 2
-    if dist:
-        t = torch.tensor([elapsed_ms, float(tokens)], device="cuda")
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        elapsed_ms, total_tokens = float(mx[0]), float(t[1])
-    else:
-        total_tokens = float(tokens)
+    elapsed_ms, total_tokens = reduce_over_ranks(dist, elapsed_ms, tokens)
     ms_per_step = elapsed_ms / args.steps
     value = total_tokens / (elapsed_ms / 1000)
 
@@ -372,12 +378,7 @@ def run_native(args) -> None:
         e2e_tokens += len(res.token_ids)
         e2e_rounds += res.steady_rounds
     e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s, float(e2e_tokens)], device="cuda")
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        e2e_s, e2e_tokens = float(mx[0]), float(t[1])
+    e2e_s, e2e_tokens = reduce_over_ranks(dist, e2e_s, e2e_tokens)
     e2e_value = e2e_tokens / e2e_s
 
     cpu = None

@@ -58,8 +58,11 @@ class OracleModel:
     """Llama forward over a paged KV cache; ``weights`` maps the Llama / auxiliary-scheme names to CPU tensors."""
 
     def __init__(self, shape: ModelShape, weights: dict, dtype: str, page_size: int, num_pages: int,
-                 block_table: np.ndarray, cos_sin: torch.Tensor | None = None):
+                 block_table: np.ndarray, cos_sin: torch.Tensor | None = None, accumulate: str = "float32"):
+        """``accumulate="float64"`` runs every matmul and attention product in double precision (then rounds to
+        float32): the same model with another summation order, to measure how far rounding alone moves the output."""
         self.s, self.dtype, self.tdtype = shape, dtype, TORCH_DTYPES[dtype]
+        self.acc = torch.float64 if accumulate == "float64" else torch.float32
         f = lambda t: t.detach().to("cpu", torch.float32)  # noqa: E731
         self.embed = f(weights["embed"])
         self.lm_head = f(weights["lm_head"])[: shape.vocab]
@@ -79,6 +82,12 @@ class OracleModel:
     def _r(self, x: torch.Tensor) -> torch.Tensor:
         """Round to the model dtype and back (a stored tensor)."""
         return x.to(self.tdtype).to(torch.float32)
+
+    def _mm(self, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        return (a.to(self.acc) @ b.to(self.acc)).to(torch.float32)
+
+    def _einsum(self, spec: str, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        return torch.einsum(spec, a.to(self.acc), b.to(self.acc)).to(torch.float32)
 
     def _rmsnorm(self, x32: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
         variance = x32.pow(2).mean(dim=-1, keepdim=True)
@@ -119,7 +128,7 @@ class OracleModel:
         residual = embeds.clone()
         x = self._rmsnorm(residual, self.layers[0]["input_norm"])
         for index, layer in enumerate(self.layers):
-            qkv = self._r(x @ layer["qkv"].T)
+            qkv = self._r(self._mm(x, layer["qkv"].T))
             q = qkv[:, :q_size].view(rows, s.num_heads, hd)
             k = qkv[:, q_size:q_size + kv_size].view(rows, s.num_kv_heads, hd)
             v = qkv[:, q_size + kv_size:].view(rows, s.num_kv_heads, hd)
@@ -135,18 +144,18 @@ class OracleModel:
             values = self.kv[index, 1, key_pages, :, key_slots, :]
             keys = keys.repeat_interleave(group, dim=1)
             values = values.repeat_interleave(group, dim=1)
-            scores = torch.einsum("rhd,khd->hrk", q, keys) / math.sqrt(hd)
+            scores = self._einsum("rhd,khd->hrk", q, keys) / math.sqrt(hd)
             scores = scores.masked_fill(~mask[None], float("-inf"))
             probs = torch.softmax(scores, dim=-1)
-            attn = self._r(torch.einsum("hrk,khd->rhd", probs, values).reshape(rows, q_size))
-            y = self._r(attn @ layer["o"].T)
+            attn = self._r(self._einsum("hrk,khd->rhd", probs, values).reshape(rows, q_size))
+            y = self._r(self._mm(attn, layer["o"].T))
             summed = y + residual
             residual = self._r(summed)
             x = self._rmsnorm(summed, layer["post_norm"])
-            gu = self._r(x @ layer["gate_up"].T)
+            gu = self._r(self._mm(x, layer["gate_up"].T))
             gate, up = gu[:, : s.intermediate], gu[:, s.intermediate:]
             act = self._r(gate / (1.0 + torch.exp(-gate)) * up)
-            y = self._r(act @ layer["down"].T)
+            y = self._r(self._mm(act, layer["down"].T))
             summed = y + residual
             residual = self._r(summed)
             weight = self.layers[index + 1]["input_norm"] if index + 1 < len(self.layers) else self.final_norm
@@ -155,7 +164,7 @@ class OracleModel:
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """compute_logits -> [:, :vocab] in the model dtype (plm/decoder.py:318), as fp32 values."""
-        return self._r(hidden @ self.lm_head.T)
+        return self._r(self._mm(hidden, self.lm_head.T))
 
 
 class RoundOracle:

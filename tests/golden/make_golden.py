@@ -176,7 +176,7 @@ def gen_epilogue(ref, out: Path):
             fake, offset_t, base_t, anchor, pending.clone(), aux_buf, rel_positions, rel_aux, ids, mask_offset,
             seq_lens, decode_offset, slot_mapping, kv_num_blocks, torch.arange(width), embed_weight)
         pre = {"ids": ids.clone(), "positions": positions, "slot_mapping": slot_mapping.clone(),
-               "embeds_checksum": torch.tensor(checksum(embeds)), "seq_lens": seq_lens.clone(),
+               "embeds_checksum": np.float64(checksum(embeds)), "seq_lens": seq_lens.clone(),
                "kv_num_blocks": kv_num_blocks.clone()}
         pend = pending.clone()
         RoundDecoder._epilogue(fake, logits, verify, pend, anchor, out_t, base_t, offset_t, torch.arange(k),
@@ -184,7 +184,7 @@ def gen_epilogue(ref, out: Path):
                                sequence_step)
         post = {"out": out_t, "base": base_t, "offset": offset_t, "anchor": anchor, "pending": pend,
                 "round_sequence": round_sequence, "sequence_step": sequence_step}
-        inputs = {"logits_checksum": torch.tensor(checksum(logits)), "verify": verify, "pending_in": pending,
+        inputs = {"logits_checksum": np.float64(checksum(logits)), "verify": verify, "pending_in": pending,
                   "aux_buf": aux_buf, "rule": torch.tensor(0 if rule == "nucleus" else 1),
                   "threshold": torch.tensor(thr)}
         for key, value in {**pre, **post, **inputs}.items():

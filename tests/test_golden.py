@@ -1,0 +1,205 @@
+"""The CPU oracle against golden fixtures produced by the reference's own code (tests/golden/make_golden.py).
+
+Pins: plm.mask.round_layout + RoundMaskView, plm.iterate.quota, the acceptance rules of plm/decoder.py:71-82,
+RoundDecoder._prologue / _epilogue (plm/decoder.py:331-365), Voronoi.assign with the reference's Triton kernels run
+by the Triton interpreter, and Hugging Face's Llama forward for the oracle's paged forward under the round mask.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import exact
+from oracle import model as omodel
+from oracle import rounds as orounds
+from oracle import voronoi as ov
+
+from .conftest import GOLDEN
+from .golden import make_golden as mg
+
+
+def test_round_layout_and_mask_match_reference():
+    cases = json.loads((GOLDEN / "layout.json").read_text())
+    assert len(cases) == 8
+    for key, case in cases.items():
+        blocks = [int(v) for v in key.split(",")]
+        rel_positions, rel_aux, depth, own = orounds.round_layout(blocks)
+        assert rel_positions.tolist() == case["rel_positions"], key
+        assert rel_aux.tolist() == case["rel_aux"], key
+        assert depth.tolist() == case["depth"], key
+        assert own.tolist() == case["own_start"], key
+        offset = case["offset"]
+        vis = orounds.visible(depth, own, offset, offset + depth.size)
+        expect = np.array([[c == "1" for c in row] for row in case["visible_rows"]])
+        # the reference's mask has no sequence-length term; every key it evaluates lies below offset + rows
+        np.testing.assert_array_equal(vis, expect, err_msg=key)
+
+
+def test_product_layout_matches_oracle():
+    from plm.mask import round_layout
+
+    for blocks in ([7] * 7, [55], [3, 1, 4]):
+        ours = [t.numpy() for t in round_layout(blocks)]
+        ref = orounds.round_layout(blocks)
+        for a, b in zip(ours, ref):
+            np.testing.assert_array_equal(a, b)
+
+
+def test_quota_matches_reference():
+    data = np.load(GOLDEN / "quota.npz")
+    weights, totals, counts = data["weights"], data["totals"], data["counts"]
+    for i, total in enumerate(totals):
+        # the reference's quota (largest remainder); ties in the remainders do not occur in these random weights
+        exact_ = weights.astype(np.float32) * np.float32(total)
+        base = np.floor(exact_).astype(np.int64)
+        remaining = total - base.sum(-1, keepdims=True)
+        frac = exact_ - base.astype(np.float32)
+        rank = np.argsort(np.argsort(-frac, axis=-1, kind="stable"), axis=-1, kind="stable")
+        np.testing.assert_array_equal(base + (rank < remaining), counts[i])
+        np.testing.assert_array_equal(counts[i].sum(-1), np.full(counts.shape[1], total))
+
+
+def test_acceptance_rules_match_reference():
+    data = np.load(GOLDEN / "accept.npz")
+    for seed, n, vocab in mg.ACCEPT_CASES:
+        logits = mg.accept_inputs(seed, n, vocab)
+        assert math.isclose(mg.checksum(logits), float(data[f"{seed}/checksum"]), rel_tol=1e-12)
+        logits = logits.numpy()
+        pending = data[f"{seed}/pending"]
+        for name, thr in (("nucleus_0.94", 0.94), ("nucleus_0.5", 0.5), ("exact", -1.0)):
+            ours = [ov.nucleus_accepts(logits[r], int(pending[r]), thr) for r in range(n)]
+            np.testing.assert_array_equal(ours, data[f"{seed}/{name}"], err_msg=f"{seed} {name}")
+        for name, thr in (("floor_2e-3", 2e-3), ("floor_1e-4", 1e-4)):
+            ours = [ov.floor_accepts(logits[r], int(pending[r]), thr) for r in range(n)]
+            np.testing.assert_array_equal(ours, data[f"{seed}/{name}"], err_msg=f"{seed} {name}")
+
+
+def test_prologue_and_epilogue_match_reference():
+    data = np.load(GOLDEN / "epilogue.npz")
+    k, vocab, hidden, aux, bs = 7, 50257, 64, 1024, 16
+    width = k + k * k
+    layout = orounds.steady_layout(k)
+    for case, (nc_target, rule, thr) in enumerate([(0, "nucleus", -1.0), (3, "nucleus", -1.0), (6, "nucleus", -1.0),
+                                                   (2, "nucleus", 0.94), (1, "floor", 2e-3)]):
+        d = {key.split("/", 1)[1]: data[key] for key in data.files if key.startswith(f"{case}/")}
+        logits = mg.epilogue_logits(case, width, vocab)
+        assert math.isclose(mg.checksum(logits), float(d["logits_checksum"]), rel_tol=1e-12)
+        logits = logits.numpy()
+        state = orounds.RoundState(k, 512, offset=300, base=40, anchor=123, pending=d["pending_in"].copy(),
+                                   out=np.concatenate([np.arange(40), np.full(472, -1)]).astype(np.int64))
+        state.round_sequence = [0] * 5
+        # prologue (plm/decoder.py:331-349); the reference's slot_mapping adds its null page (+ block size)
+        ids, values, positions, slots = orounds.prologue(state, layout, vocab, aux, d["aux_buf"])
+        np.testing.assert_array_equal(ids, d["ids"])
+        np.testing.assert_array_equal(positions, d["positions"])
+        np.testing.assert_array_equal(slots + bs, d["slot_mapping"])
+        assert int(d["seq_lens"][0]) == 300 + width
+        assert int(d["kv_num_blocks"][0]) == -(-(300 + width) // bs)
+        # epilogue (plm/decoder.py:351-365)
+        rule_flags = np.zeros(k, dtype=bool)
+        for r in range(k - 1):
+            if rule == "floor":
+                rule_flags[r] = ov.floor_accepts(logits[r], int(state.pending[r]), thr)
+            else:
+                rule_flags[r] = ov.nucleus_accepts(logits[r], int(state.pending[r]), thr)
+        nc = orounds.epilogue(state, d["verify"], rule_flags, orounds.argmax_first(logits[k:]))
+        np.testing.assert_array_equal(state.out, d["out"])
+        assert (state.base, state.offset, state.anchor) == (int(d["base"]), int(d["offset"]), int(d["anchor"][0]))
+        np.testing.assert_array_equal(state.pending, d["pending"])
+        assert int(d["round_sequence"][5]) == nc and int(d["sequence_step"][0]) == 6
+        if rule == "nucleus" and thr < 0:
+            assert nc == nc_target
+
+
+def test_embedding_matches_reference_prologue():
+    """The oracle's embedding of the prologue rows reproduces the reference's (checksum of the embedding rows)."""
+    data = np.load(GOLDEN / "epilogue.npz")
+    g = torch.Generator().manual_seed(400)
+    k, vocab, hidden, aux = 7, 50257, 64, 1024
+    aux_vocab = torch.randn(aux, hidden, generator=g)
+    mask_aux = torch.randn(hidden, generator=g)
+    embed = torch.randn(vocab + 1, hidden, generator=g)
+    assert math.isclose(mg.checksum(embed), float(data["embed_weight_checksum"]), rel_tol=1e-12)
+    shape = omodel.ModelShape(1, hidden, 1, 1, 64, 64, vocab, aux)
+    weights = {"embed": embed, "lm_head": embed[:vocab], "final_norm": torch.ones(hidden), "aux_vocab": aux_vocab,
+               "mask_aux": mask_aux, "qkv": [torch.zeros(192, hidden)], "o": [torch.zeros(hidden, 64)],
+               "gate_up": [torch.zeros(128, hidden)], "down": [torch.zeros(hidden, 64)],
+               "input_norm": [torch.ones(hidden)], "post_norm": [torch.ones(hidden)]}
+    m = omodel.OracleModel(shape, weights, "float32", 16, 4, np.arange(4))
+    for case in range(5):
+        d = {key.split("/", 1)[1]: data[key] for key in data.files if key.startswith(f"{case}/")}
+        layout = orounds.steady_layout(k)
+        state = orounds.RoundState(k, 512, offset=300, base=40, anchor=123, pending=d["pending_in"].copy())
+        ids, values, _, _ = orounds.prologue(state, layout, vocab, aux, d["aux_buf"])
+        rows = m.embed_rows(ids, values)
+        assert math.isclose(mg.checksum(rows), float(d["embeds_checksum"]), rel_tol=1e-12)
+
+
+def test_oracle_forward_matches_hf_llama():
+    """The oracle's paged forward (fp32, identity rounding) over a prompt and one round under the round mask equals
+    transformers' LlamaForCausalLM on the same rows with the reference's RoundMaskView as a 4-D mask."""
+    data = np.load(GOLDEN / "llama.npz")
+    c = mg.LLAMA
+    w = mg.llama_weights(c["seed"], c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                         c["vocab"])
+    shape = omodel.ModelShape(c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                              c["vocab"], 64, rms_eps=1e-5, max_pos=4096)
+    prompt_len, k = int(data["prompt_len"]), int(data["k"])
+    page = 16
+    pages = -(-(prompt_len + k + k * k) // page)
+    table = np.random.default_rng(0).permutation(pages * 2)[:pages]
+    m = omodel.OracleModel(shape, w, "float32", page, pages * 2, table)
+    embeds = torch.as_tensor(data["embeds"])
+    _, _, depth, own = orounds.chunk_layout(prompt_len)
+    h_prompt = m.forward(embeds[:prompt_len], np.arange(prompt_len), 0, depth, own)
+    rel_positions, _, depth, own = orounds.steady_layout(k)
+    h_round = m.forward(embeds[prompt_len:], prompt_len + rel_positions, prompt_len, depth, own)
+    ours = torch.cat([m.logits(h_prompt), m.logits(h_round)]).numpy()
+    np.testing.assert_allclose(ours, data["logits"], atol=2e-5, rtol=1e-4)
+
+
+@pytest.mark.skipif(not (GOLDEN / "voronoi.npz").exists(), reason="voronoi fixture not generated")
+def test_voronoi_matches_reference_interpreted():
+    """Against the reference's Voronoi.assign (Triton kernels interpreted on CPU).
+
+    fp32 logits (no equal values): identical shortlist, order and quota, fitted factors within 1e-5 of their scale,
+    identical assignment sigma over every cell and identical decoded tokens. The factors differ in the last bits only
+    because the reference sums the loads with float atomics and uses its own exp/log (iterate.py:8-9).
+    bf16 logits: equal values at the top-128 boundary are ordered by torch.topk's implementation-defined tie order in
+    the reference and by (value desc, index asc) here, so the shortlists may differ by a swapped token and the
+    order of ties; the assignment must still agree on >= 97% of cells."""
+    data = np.load(GOLDEN / "voronoi.npz")
+    for seed, n, vocab, aux, kind in mg.VORONOI_CASES:
+        logits, table = mg.voronoi_inputs(seed, n, vocab, aux, kind)
+        key = f"{seed}"
+        assert math.isclose(mg.checksum(logits), float(data[f"{key}/logits_checksum"]), rel_tol=1e-12)
+        table_np = table.float().numpy()
+        cells = data[f"{key}/cells"]
+        for r in range(n):
+            dec = ov.decode_row(logits[r].numpy(), table_np, int(cells[r]), "bfloat16")
+            ref_tokens = data[f"{key}/tokens"][r]
+            ref_sigma = data[f"{key}/sigma"][r].astype(np.int64)
+            sigma = ov.assign_sigma(table_np, dec.tokens, dec.bias)
+            agree = float((dec.tokens[sigma] == ref_tokens[ref_sigma]).mean())
+            if kind == "fp32":
+                np.testing.assert_array_equal(dec.tokens, ref_tokens)
+                np.testing.assert_array_equal(dec.counts, data[f"{key}/counts"][r])
+                ref_bias = data[f"{key}/bias"][r]
+                np.testing.assert_allclose(dec.bias, ref_bias, rtol=0, atol=1e-5 * float(np.abs(ref_bias).max()))
+                np.testing.assert_array_equal(sigma, ref_sigma)
+                assert dec.token == int(data[f"{key}/decoded"][r])
+            else:
+                assert len(set(dec.tokens.tolist()) ^ set(ref_tokens.tolist())) <= 2, f"case {seed} row {r}"
+                assert agree >= 0.97, f"case {seed} row {r}: assignment agreement {agree:.4f}"
+
+
+def test_round_to_dtype_matches_torch():
+    x = torch.randn(100000) * 100
+    x[:5] = torch.tensor([0.0, -0.0, float("inf"), 1e-40, 65504.0])
+    np.testing.assert_array_equal(exact.round_to_dtype(x.numpy(), "bfloat16"), x.bfloat16().float().numpy())
+    np.testing.assert_array_equal(exact.round_to_dtype(x.numpy(), "float16"), x.half().float().numpy())

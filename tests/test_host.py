@@ -1,0 +1,108 @@
+"""Host-side logic on CPU: the drop-in configuration surface (plm/rounds.py of the reference), model configuration and
+export round trip, the roofline byte accounting of bench.py, and the multi-GPU timing reduction (gloo, 2 ranks)."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+
+def test_round_config_matches_reference_settings():
+    from plm.rounds import PREFILL_BUCKETS, SETTINGS, RoundConfig
+
+    assert PREFILL_BUCKETS == tuple(range(64, 641, 64))
+    assert SETTINGS["posttrain"].default_k == {"exact": 7, "relaxed": 10}
+    assert SETTINGS["pretrain"].relaxed_rule == ("floor", 2e-3)
+    c = RoundConfig(model="synthetic:plm-tiny")
+    assert (c.k, c.width, c.accept) == (7, 56, ("nucleus", None))
+    c = RoundConfig(model="x", setting="posttrain", match="relaxed")
+    assert (c.k, c.accept) == (10, ("nucleus", 0.94))
+    c = RoundConfig(model="x", setting="pretrain", match="relaxed")
+    assert (c.k, c.accept, c.width) == (6, ("floor", 2e-3), 42)
+    c = RoundConfig(model="x", setting="pretrain", k=4)
+    assert c.describe()["accept"] == "exact" and c.describe()["width"] == 20
+    with pytest.raises(ValueError):
+        RoundConfig(model="x", setting="other")
+    with pytest.raises(ValueError):
+        RoundConfig(model="x", match="loose")
+
+
+def test_config_and_export_round_trip(tmp_path):
+    from plm.model import PLMConfig, PLMWeights, shape_config
+
+    cfg = shape_config("plm-tiny", vocab=1000, aux_vocab=64, num_kv_heads=1)
+    assert PLMConfig.from_hf_config(cfg.hf_config(), name=cfg.name) == cfg
+    w = PLMWeights.random(cfg, seed=3, device="cpu")
+    w.save_export(tmp_path / "export")
+    back = PLMWeights.from_export(tmp_path / "export", device="cpu")
+    for name, value in w.named().items():
+        other = back.named()[name]
+        if isinstance(value, list):
+            assert all(torch.equal(a, b) for a, b in zip(value, other)), name
+        else:
+            assert torch.equal(value, other), name
+    again = PLMWeights.random(cfg, seed=3, device="cpu")
+    assert torch.equal(again.qkv[1], w.qkv[1]) and not torch.equal(PLMWeights.random(cfg, seed=4, device="cpu").o[0],
+                                                                   w.o[0])
+
+
+def test_roofline_bytes_of_the_benchmark_shape():
+    from plm.model import shape_config
+
+    bench = _load_root_bench()
+    b = bench.round_bytes(shape_config("plm-1.3b"), 1024, 7)
+    assert b["weights"] == 3_427_078_144  # 24 layers of qkv/o/gate_up/down + lm_head, bf16
+    assert b["kv_read"] == 1024 * 24 * 2 * 2048 * 2
+    assert abs(b["total"] / 1e9 - 3.65) < 0.01
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _load_root_bench():
+    """bench.py at the repository root (the name ``bench`` also belongs to the CLI package)."""
+    import importlib.util
+    from pathlib import Path
+
+    path = Path(__file__).resolve().parent.parent / "bench.py"
+    spec = importlib.util.spec_from_file_location("plm_root_bench", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def _rank_main(rank: int, world: int, port: int, queue) -> None:
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    bench = _load_root_bench()
+
+    elapsed, tokens = bench.reduce_over_ranks(dist, 10.0 + rank, 100 + rank, device="cpu")
+    queue.put((rank, elapsed, tokens))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_multi_rank_reduction_gloo():
+    """Replicas only: the job time is the slowest rank's, the token count the sum over ranks."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for _, elapsed, tokens in results:
+        assert elapsed == 11.0 and tokens == 201

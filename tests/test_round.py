@@ -1,10 +1,14 @@
 """The whole round on the GPU (RoundDecoder over libplm_native.so) against the CPU oracle.
 
 Teacher-forced parity, stage by stage (prefill, round 0, steady rounds): both sides run the forward on the same
-state; the GPU's logits must match the oracle's within bf16 tolerance (max abs error <= 2e-2), the final-norm hidden
-rows within 2e-2 + 2 bf16 ulps (2^-6 relative: those values reach |x| >= 4, where one bf16 ulp is 0.031), and
-the GPU's verify decode, acceptance and bookkeeping must equal the oracle's run on the GPU's own fp32 logits, bit
-for bit (output tokens, base, offset, anchor, pending, accepted-count record).
+state, and the GPU's verify decode, acceptance and bookkeeping must equal the oracle's run on the GPU's own fp32
+logits, bit for bit (output tokens, base, offset, anchor, pending, accepted-count record).
+
+Logits must agree within bf16 tolerance: max abs error <= max(2e-2, 2 s), where s is the model's own sensitivity to
+rounding — the oracle's max abs change when it accumulates in float64 instead of float32, measured on the prefill
+(a 2-layer model has s < 1e-2; a random 24-layer bf16 stack amplifies any rounding-order difference to s ~ 0.13).
+The final-norm hidden rows use max(2e-2 + 2^-6 |ref|, 2 s_hidden): their elements reach |x| >= 4, where one bf16
+ulp is 0.031.
 A free-running comparison reports the end-to-end token agreement rate.
 """
 
@@ -56,6 +60,8 @@ def _pair(shape: str, k: int, page: int, seed: int, rule="nucleus", threshold=No
     oracle = omodel.RoundOracle(oracle_model, table_np, k, rule, threshold,
                                 ov.VoronoiConfig(cfg.top_m, cfg.shortlist, cfg.rounds, cfg.sweeps),
                                 capacity=decoder.out.numel(), aux_stream=aux)
+    oracle.sensitivity_model = omodel.OracleModel(shape_o, named, "bfloat16", page, num_pages, table,
+                                                  cos_sin=decoder.cos_sin.cpu(), accumulate="float64")
     return decoder, oracle, cfg
 
 
@@ -71,12 +77,12 @@ def _assert_state(decoder, state: orounds.RoundState):
     np.testing.assert_array_equal(g["pending"], state.pending)
 
 
-def _close(name, gpu, ref, report, rel=0.0):
+def _close(name, gpu, ref, report, rel=0.0, floor=0.0):
     gpu, ref = np.asarray(gpu, dtype=np.float64), np.asarray(ref, dtype=np.float64)
     diff = np.abs(gpu - ref)
     err = float(diff.max())
     report.setdefault(name, []).append(err)
-    bound = TOL + rel * np.abs(ref)
+    bound = np.maximum(TOL + rel * np.abs(ref), floor)
     worst = int(np.argmax(diff - bound))
     assert (diff <= bound).all(), f"{name}: error {diff.flat[worst]:.4g} > {bound.flat[worst]:.4g} (max abs {err:.4g})"
 
@@ -99,9 +105,16 @@ def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides)
     decoder.handle.prefill()
     decoder.check()
     hidden_o, logits_o = oracle.prefill_forward(prompt.numpy())
+    # the model's own rounding sensitivity: the same forward accumulated in float64
+    probe = omodel.RoundOracle(oracle.sensitivity_model, oracle.table, k)
+    hidden_s, logits_s = probe.prefill_forward(prompt.numpy())
+    sens_l = float(np.abs(logits_s - logits_o).max())
+    sens_h = float((hidden_s - hidden_o).abs().max())
+    report["sensitivity logits"], report["sensitivity hidden"] = [sens_l], [sens_h]
+    fl, fh = 2 * sens_l, 2 * sens_h
     gpu_logits = decoder.verify_logits[0].cpu().numpy()
-    _close("prefill logits", gpu_logits, logits_o[0], report)
-    _close("prefill hidden", decoder.hidden_normed[63].float().cpu().numpy(), hidden_o[0].numpy(), report, HREL)
+    _close("prefill logits", gpu_logits, logits_o[0], report, floor=fl)
+    _close("prefill hidden", decoder.hidden_normed[63].float().cpu().numpy(), hidden_o[0].numpy(), report, HREL, fh)
     oracle.commit_first(gpu_logits, 64)
     _assert_state(decoder, oracle.state)
 
@@ -110,8 +123,8 @@ def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides)
     decoder.check()
     hidden_o, logits_o = oracle.round0_forward()
     gpu_logits = decoder.verify_logits[0].cpu().numpy()
-    _close("round0 logits", gpu_logits, logits_o[0], report)
-    _close("round0 hidden", decoder.hidden_normed[:W].float().cpu().numpy(), hidden_o.numpy(), report, HREL)
+    _close("round0 logits", gpu_logits, logits_o[0], report, floor=fl)
+    _close("round0 hidden", decoder.hidden_normed[:W].float().cpu().numpy(), hidden_o.numpy(), report, HREL, fh)
     oracle.commit_round0(gpu_logits[None], _argmax_partials(decoder, W)[1:])
     _assert_state(decoder, oracle.state)
 
@@ -122,8 +135,8 @@ def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides)
         decoder.check()
         hidden_o, logits_o = oracle.round_forward()
         gpu_logits = decoder.verify_logits.cpu().numpy()
-        _close("round logits", gpu_logits, logits_o[:k], report)
-        _close("round hidden", decoder.hidden_normed[:W].float().cpu().numpy(), hidden_o.numpy(), report, HREL)
+        _close("round logits", gpu_logits, logits_o[:k], report, floor=fl)
+        _close("round hidden", decoder.hidden_normed[:W].float().cpu().numpy(), hidden_o.numpy(), report, HREL, fh)
         oracle.commit_round(gpu_logits, _argmax_partials(decoder, W)[k:])
         _assert_state(decoder, oracle.state)
     record = decoder.round_sequence[seq0:int(decoder.sequence_step[0])].cpu().numpy().tolist()
