@@ -157,7 +157,7 @@ typedef struct plm_verify_desc {
   float* dbg_bias;
   float* dbg_stats;
   int32_t* dbg_sigma;
-  int64_t* dbg_phase_ns; /* [n_rows][8] nanoseconds from kernel start to the end of each phase (diagnostic) */
+  int64_t* dbg_phase_ns; /* [n_rows][16] nanoseconds from kernel start to the end of each phase (diagnostic) */
   plm_bookkeeping book;
 } plm_verify_desc;
 

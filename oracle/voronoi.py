@@ -9,9 +9,11 @@ identical fp32 logits and cost table both produce the same bits:
   shortlist  the top ``top_m`` logits ordered by (value descending, index ascending); on the tile-max path of
              iterate.py:248-273 ties at the boundary are resolved by torch.topk, here by lower index;
   quota      largest remainder, equal remainders ranked by shortlist position (iterate.py:214-223);
-  sums       ``exact.block_sum`` for vocabulary-wide sums, ``exact.lane_sum`` for 128- and 64-element sums, the
-             shortlist softmax in k order, and the fit's per-target load by per-warp bins (module docstring of
-             voronoi.cu) instead of atomics.
+  sums       vocabulary-wide sums are partitioned like the GPU's cluster of CLUSTER ranks: each rank's contiguous
+             slice is summed with ``exact.block_sum`` over THREADS threads and the slice sums added in rank order;
+             ``exact.lane_sum`` for 128- and 64-element sums; the shortlist softmax in k order; the fit's
+             per-target load per rank as a ``lane_sum`` over the target's entries (owned items ascending), the
+             rank partials added in rank order — instead of float atomics.
 """
 
 from __future__ import annotations
@@ -20,8 +22,12 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .exact import (F, block_sum, condense_key, condensed_cost, exp32, f32, lane_sum, log32, orderable_key,
+from .exact import (F, _butterfly, block_sum, condense_key, condensed_cost, exp32, f32, lane_sum, log32, orderable_key,
                     round_to_dtype)
+
+# The GPU decodes a verify row with a cluster of CLUSTER CTAs of THREADS threads (csrc/verify.h).
+CLUSTER = 8
+THREADS = 256
 
 # plm/iterate.py:21-25 and the defaults of Voronoi.prior / fit / assign (iterate.py:286, 292-294, 322-324)
 STEP_LIMIT = 0.25
@@ -56,11 +62,24 @@ class Decoded:
     unit: np.float32
 
 
+def _slices(n: int):
+    length = -(-n // CLUSTER)
+    return [(min(n, q * length), min(n, (q + 1) * length)) for q in range(CLUSTER)]
+
+
+def partitioned_sum(values: np.ndarray) -> np.float32:
+    """Slice sums in the 256-thread block order, added in rank order (the GPU cluster's vocabulary-wide sums)."""
+    total = F(0.0)
+    for lo, hi in _slices(values.size):
+        total = F(total + block_sum(values[lo:hi], threads=THREADS))
+    return total
+
+
 def row_stats(row: np.ndarray):
     """Maximum, sum of exp(x - max) and normaliser max + log(sum) of one row (iterate.py:54-80 / 176-192)."""
     row = f32(row)
     m = F(row.max())
-    total = block_sum(exp32(row - m))
+    total = partitioned_sum(exp32(row - m))
     return m, total, F(m + log32(total))
 
 
@@ -104,6 +123,22 @@ def condense(table: np.ndarray, tokens: np.ndarray, offset: np.ndarray, k: int) 
     return np.sort(keys, axis=0)[:k]
 
 
+def _rank_loads(weights_by_target: np.ndarray, present: np.ndarray) -> np.ndarray:
+    """Per-target load of one rank: [M, owned] weights and whether the item holds the target (a held entry's weight
+    can underflow to 0). One warp per target sums the target's entries (owned items ascending) in ``lane_sum`` order;
+    the lanes past the last entry add nothing, which the zero padding reproduces exactly."""
+    n_targets = weights_by_target.shape[0]
+    pos = np.cumsum(present, axis=1) - 1
+    longest = int(present.sum(axis=1).max(initial=0))
+    packed = np.zeros((n_targets, max(32, -(-longest // 32) * 32)), dtype=np.float32)
+    rows, cols = np.nonzero(present)
+    packed[rows, pos[rows, cols]] = weights_by_target[rows, cols]
+    acc = np.zeros((n_targets, 32), dtype=np.float32)
+    for start in range(0, packed.shape[1], 32):
+        acc = acc + packed[:, start:start + 32]
+    return f32(_butterfly(acc))
+
+
 def fit(keys: np.ndarray, counts: np.ndarray, offset: np.ndarray, unit: np.float32, iterations: int,
         epsilon: float, relax: float = RELAX, endpoint: float = ENDPOINT, limit: float = STEP_LIMIT) -> np.ndarray:
     """The annealed Sinkhorn fit of iterate.py:110-159 / 292-312 on the condensed problem."""
@@ -116,9 +151,11 @@ def fit(keys: np.ndarray, counts: np.ndarray, offset: np.ndarray, unit: np.float
     correction = np.zeros(n_targets, dtype=np.float32)
     target = (keys & 0x7F).astype(np.int64)
     base_cost = condensed_cost(keys)
-    threads = min(1024, n_items)
-    passes, n_warps = n_items // threads, threads // 32
-    warp_rows = np.arange(n_warps)
+    owned = n_items // CLUSTER
+    columns = np.arange(n_items)
+    held = np.zeros((n_targets, n_items), dtype=bool)
+    for q in range(k):
+        held[target[q], columns] = True
     for _ in range(iterations):
         weight = (-(base_cost + correction[target])) / temperature
         e = exp32(weight - weight.max(axis=0))
@@ -126,19 +163,13 @@ def fit(keys: np.ndarray, counts: np.ndarray, offset: np.ndarray, unit: np.float
         for q in range(k):
             wsum = wsum + e[q]
         e = e / wsum
-        bins = np.zeros((n_warps, n_targets), dtype=np.float32)
-        for j in range(passes):
-            cols = slice(j * threads, (j + 1) * threads)
-            for q in range(k):
-                t = target[q, cols].reshape(n_warps, 32)
-                w = e[q, cols].reshape(n_warps, 32)
-                group = np.zeros((n_warps, n_targets), dtype=np.float32)
-                for lane in range(32):
-                    group[warp_rows, t[:, lane]] = group[warp_rows, t[:, lane]] + w[:, lane]
-                bins = bins + group
+        dense = np.zeros((n_targets, n_items), dtype=np.float32)
+        for q in range(k):
+            dense[target[q], columns] = e[q]
         load = np.zeros(n_targets, dtype=np.float32)
-        for w in range(n_warps):
-            load = load + bins[w]
+        for rank in range(CLUSTER):
+            cols = slice(rank * owned, (rank + 1) * owned)
+            load = load + _rank_loads(dense[:, cols], held[:, cols])
         step = temperature * (log32(np.maximum(load, F(LOAD_FLOOR))) - share)
         step = np.minimum(np.maximum(step, -bound), bound)
         corrected = correction + F(relax) * step
@@ -180,7 +211,7 @@ def nucleus_accepts(row: np.ndarray, pending: int, nucleus: float) -> bool:
     m, total, _ = row_stats(row)
     probs = exp32(row - m) / total
     own = probs[pending]
-    mass = block_sum(np.where(probs > own, probs, F(0.0)))
+    mass = partitioned_sum(np.where(probs > own, probs, F(0.0)))
     return bool((mass < nucleus) or (own >= probs.max()))
 
 

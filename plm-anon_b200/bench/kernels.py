@@ -117,12 +117,13 @@ def bench_verify(args, ctx):
                              aux_buf=aux_buf.data_ptr(), aux_len=8192, top_m=128, shortlist=8, rounds=2, sweeps=12,
                              epsilon=0.15, refocus=0.35, endpoint=0.0087, verify=verify.data_ptr(),
                              flags=flags.data_ptr(), threshold=-1.0, book=native.Bookkeeping(mode=0))
-    phases = torch.zeros(args.rows, 8, dtype=torch.int64, device="cuda")
+    phases = torch.zeros(args.rows, 16, dtype=torch.int64, device="cuda")
     desc.dbg_phase_ns = phases.data_ptr()
     fn = lambda: native.verify_decode(ctx, desc)  # noqa: E731
     us = _time(fn, args.iters, args.warmup, not args.no_graph)
     ctx.check()
-    names = ["stats", "rule", "select", "quota_spread_prior", "condense0", "fit0", "round1", "argmin"]
+    names = ["stats", "rule", "slice_select", "merge_copy", "merge_sort", "staging", "quota_spread_prior", "condense0",
+             "fit0", "condense1", "fit1", "final_sync", "argmin"]
     nbytes = args.rows * (args.vocab * 4 + 2 * 128 * args.aux * 2)
     return {"kernel": "verify_decode_kernel", "rows": args.rows, "vocab": args.vocab, "aux": args.aux, "us": us,
             "GB/s": nbytes / us / 1e3, "bytes": nbytes,

@@ -23,6 +23,7 @@ enum DeviceError : int {
   kErrBadIndex = 4,         // an index (page, slot, token, aux cell) out of range was skipped
   kErrTimeoutSplit = 5,     // split reduction saw an inconsistent arrival count
   kErrBadShape = 6,         // a kernel was launched with a shape it cannot handle
+  kErrTimeoutPeer = 7,      // a cluster peer's st.async data did not arrive
 };
 
 // One second: far above any legitimate wait in a round (a whole round takes about a millisecond).
@@ -86,6 +87,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       return false;
     }
   }
+}
+
+// The same bounded wait with cluster-scope acquire: for data that peers of the cluster deliver with st.async.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
+// 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned); `valid` false zero-fills.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src, bool valid = true) {
+  const int size = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src), "r"(size)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ----------------------------------------------------------------------------------------------------------------
@@ -195,17 +233,34 @@ __device__ __forceinline__ void cluster_sync() {
 // Shared-memory address of `local` (an address in this CTA's shared memory) in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank) {
   uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
   return out;
 }
+// Plain 16-byte store into a cluster peer's shared memory (`addr` from cluster_map).
+__device__ __forceinline__ void st_dsmem_f32x4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+// One arrival on a cluster peer's mbarrier (`remote_bar` from cluster_map) with release semantics at cluster scope:
+// this thread's earlier writes, and those ordered before it by a CTA barrier, are visible to the peer's waiters.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+// Distributed shared memory loads are plain (not volatile): they read peers' shared memory that a cluster_sync (a
+// compiler memory barrier) has published, so the compiler may batch independent loads.
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_dsmem_u32(uint32_t addr) {
+  uint32_t v;
+  asm("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ float2 ld_dsmem_f32x2(uint32_t addr) {
   float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  asm("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
   return v;
 }
 

@@ -36,10 +36,10 @@ int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
 
-// Launch with optional programmatic dependent launch and an optional cluster of `cluster_y` CTAs along y.
+// Launch with optional programmatic dependent launch and an optional cluster of cluster_x * cluster_y CTAs.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                      int cluster_y, Args&&... args) {
+cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           bool pdl, int cluster_x, int cluster_y, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -52,9 +52,9 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
     attr[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
   }
-  if (cluster_y > 1) {
+  if (cluster_x * cluster_y > 1) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.x = unsigned(cluster_x);
     attr[n].val.clusterDim.y = unsigned(cluster_y);
     attr[n].val.clusterDim.z = 1;
     ++n;
@@ -64,10 +64,17 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Cluster of `cluster_y` CTAs along y.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      int cluster_y, Args&&... args) {
+  return launch_cluster(kernel, grid, block, smem, stream, pdl, 1, cluster_y, std::forward<Args>(args)...);
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
                    Args&&... args) {
-  return launch_ex(kernel, grid, block, smem, stream, pdl, 1, std::forward<Args>(args)...);
+  return launch_cluster(kernel, grid, block, smem, stream, pdl, 1, 1, std::forward<Args>(args)...);
 }
 
 // Cluster size for the k-split of a weight-streaming GEMM: the smallest power of two (<= 8, <= the k-blocks)

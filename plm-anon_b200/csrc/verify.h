@@ -7,6 +7,14 @@
 namespace plm {
 
 enum AcceptRule : int { kRuleNucleus = 0, kRuleFloor = 1 };
+
+// Each verify row is decoded by a cluster of kVerifyCluster CTAs of kVerifyThreads threads (the oracle mirrors the
+// partition: oracle/voronoi.py CLUSTER and THREADS).
+constexpr int kVerifyCluster = 8;
+constexpr int kVerifyThreads = 256;
+// Diagnostic phase record per verify row: statistics, rule, slice select, merge copy, merge sort, table staging,
+// quota/spread/prior, condense and fit of rounds 0 and 1, final cluster barrier, argmin (slots 13..15 unused).
+constexpr int kPhaseSlots = 16;
 enum BookMode : int { kBookNone = 0, kBookSteady = 1, kBookRound0 = 2, kBookFirstToken = 3 };
 
 struct Bookkeeping {
@@ -52,7 +60,7 @@ struct VerifyArgs {
   float* dbg_bias;           // [n_rows][top_m]
   float* dbg_stats;          // [n_rows][4] max, sum of exp, normaliser, unit
   int32_t* dbg_sigma;        // [n_rows] shortlist index of the decoded token
-  int64_t* dbg_phase_ns;     // [n_rows][8] %globaltimer at the end of each phase (nullable)
+  int64_t* dbg_phase_ns;     // [n_rows][kPhaseSlots] ns from kernel start to the end of each phase (nullable)
   Bookkeeping book;
   int* counter;              // arrival counter (zero between launches)
   int* err;

@@ -20,7 +20,8 @@ PLM_BF16, PLM_F16 = 0, 1
 EPI_STORE, EPI_SILU_MUL, EPI_QKV_ROPE, EPI_LOGITS, EPI_TABLE = range(5)
 
 DEVICE_ERRORS = {1: "TMA stage wait timed out", 2: "free stage wait timed out", 3: "MMA completion wait timed out",
-                 4: "index out of range", 5: "split reduction arrival count inconsistent", 6: "unsupported shape"}
+                 4: "index out of range", 5: "split reduction arrival count inconsistent", 6: "unsupported shape",
+                 7: "cluster peer data wait timed out"}
 
 
 class NativeError(RuntimeError):
