@@ -288,6 +288,17 @@ int plm_gemm_tiles(int32_t kind, int32_t n_out, int32_t gate_offset, int32_t* ti
 int plm_gemm(plm_ctx* ctx, const plm_gemm_desc* desc, void* stream);
 /* Verify decode + acceptance + (optionally) the round bookkeeping, one CTA per row. */
 int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* desc, void* stream);
+/* plm_verify_decode without a context, allocating nothing. This entry point has no counterpart in the reference: it
+ * serves callers that cannot allocate device memory, such as a host runtime bound over a foreign-function
+ * interface whose device memory belongs to its own allocator, or a decode loop that must not stall (cudaMalloc and
+ * cudaFree synchronise the device). Its scratch is a file-scope device array of 1024 bytes: the bookkeeping
+ * arrival counter (zero at module load, reset to zero by every bookkeeping launch), the device error word used
+ * when device_error is NULL, and 32 row slots for the decoded tokens and verdicts used when desc->verify or
+ * desc->flags is NULL. More than 32 rows is rejected with PLM_ERR_INVALID. device_error, when given, is a device
+ * int32 the caller has zeroed; the first device-side error code is written there. The first call on a device
+ * (with that device current) resolves the scratch's address with cudaGetSymbolAddress, so make it before any stream
+ * capture. Calls on one device share the scratch: overlapping calls (other streams or threads) race. */
+int plm_verify_decode_static(const plm_verify_desc* desc, int32_t* device_error, void* stream);
 int plm_attention(plm_ctx* ctx, const plm_attention_desc* desc, void* stream);
 int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* desc, void* stream);
 int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* desc, void* stream);

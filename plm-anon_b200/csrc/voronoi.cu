@@ -22,6 +22,7 @@
 // from the lm_head's per-tile argmax partials, anchor, base and offset (the implicit KV commit).
 // Every floating-point step is a separate IEEE operation in a fixed order and exp/log come from plm_math.h; the numpy
 // oracle (oracle/voronoi.py) performs the same operations.
+#include <atomic>
 #include <climits>
 
 #include "common.cuh"
@@ -1132,6 +1133,101 @@ extern "C" int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* d, void* s
   a.counter = ctx->counters + (ctx->n_counters - 1);
   a.err = ctx->err;
   int st = verify_validate(a, d->n_rows);
+  if (st != PLM_OK) return st;
+  return verify_launch(a, d->dtype, d->n_rows, static_cast<cudaStream_t>(stream), true);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// plm_verify_decode_static: the same kernel with no context and no allocation. Its scratch (the bookkeeping arrival
+// counter, the device error word when the caller gives none, and the per-row decoded tokens and verdicts when the
+// caller gives no buffers for them) is this file-scope array of kStaticScratchBytes. Callers that cannot allocate
+// device memory use it: a host runtime bound over a foreign-function interface whose device memory belongs to its
+// own allocator, or a decode loop that must not stall, since cudaMalloc / cudaFree synchronise the device.
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kStaticScratchBytes = 1024;
+constexpr int kStaticRows = 32;          // per-row slots; the kernel decodes at most 32 rows per launch
+constexpr int kStaticTokensOffset = 256; // int64 tokens [kStaticRows]
+constexpr int kStaticFlagsOffset = 512;  // int32 verdicts [kStaticRows]
+static_assert(kStaticTokensOffset + 8 * kStaticRows <= kStaticFlagsOffset, "static scratch layout");
+static_assert(kStaticFlagsOffset + 4 * kStaticRows <= kStaticScratchBytes, "static scratch layout");
+
+// Word 0: arrival counter (zero at module load; the last cluster of every bookkeeping launch resets it to zero).
+// Word 1: device error word when the caller passes none (first error wins; never cleared, never read back).
+static __device__ __align__(256) unsigned char g_verify_static_scratch[kStaticScratchBytes];
+
+constexpr int kStaticMaxDevices = 64;
+std::atomic<unsigned char*> g_static_scratch_ptr[kStaticMaxDevices];
+
+// Device address of the scratch on the current device, resolved once per device by cudaGetSymbolAddress.
+int static_scratch(unsigned char** out) {
+  int dev = 0;
+  int st = check_cuda(cudaGetDevice(&dev), "plm_verify_decode_static: cudaGetDevice");
+  if (st != PLM_OK) return st;
+  if (dev < 0 || dev >= kStaticMaxDevices)
+    return fail(PLM_ERR_UNSUPPORTED, "plm_verify_decode_static: device %d beyond %d", dev, kStaticMaxDevices);
+  unsigned char* p = g_static_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    st = check_cuda(cudaGetSymbolAddress(&addr, g_verify_static_scratch),
+                    "plm_verify_decode_static: cudaGetSymbolAddress(scratch)");
+    if (st != PLM_OK) return st;
+    p = static_cast<unsigned char*>(addr);
+    g_static_scratch_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return PLM_OK;
+}
+
+}  // namespace
+
+extern "C" int plm_verify_decode_static(const plm_verify_desc* d, int32_t* device_error, void* stream) {
+  if (d == nullptr) return fail(PLM_ERR_INVALID, "plm_verify_decode_static: null descriptor");
+  if (d->n_rows > kStaticRows)
+    return fail(PLM_ERR_INVALID, "plm_verify_decode_static: %d rows exceed the static scratch's %d row slots (%d bytes)",
+                d->n_rows, kStaticRows, kStaticScratchBytes);
+  unsigned char* scratch = nullptr;
+  int st = static_scratch(&scratch);
+  if (st != PLM_OK) return st;
+  VerifyArgs a = {};
+  a.logits = d->logits;
+  a.vocab = d->vocab;
+  a.logits_stride = d->logits_stride > 0 ? d->logits_stride : d->vocab;
+  a.table = d->table;
+  a.aux = d->aux;
+  a.aux_buf = d->aux_buf;
+  a.aux_len = d->aux_len;
+  a.aux_base = d->aux_base;
+  a.aux_row_offset = d->aux_row_offset;
+  a.pending = d->pending;
+  a.n_accept = d->n_accept;
+  a.rule = d->rule;
+  a.threshold = d->threshold;
+  a.top_m = d->top_m;
+  a.shortlist = d->shortlist;
+  a.rounds = d->rounds;
+  a.sweeps = d->sweeps;
+  for (int r = 0; r < 4; ++r) {  // as plm_verify_decode (plm/iterate.py:333-336)
+    const double eps = r == 0 ? d->epsilon : d->epsilon * d->refocus;
+    a.eps[r] = float(eps);
+    a.anneal[r] = float(pow(d->endpoint / eps, 1.0 / double(d->sweeps > 1 ? d->sweeps : 1)));
+  }
+  a.verify = d->verify != nullptr ? d->verify : reinterpret_cast<int64_t*>(scratch + kStaticTokensOffset);
+  a.flags = d->flags != nullptr ? d->flags : reinterpret_cast<int32_t*>(scratch + kStaticFlagsOffset);
+  a.dbg_tokens = d->dbg_tokens;
+  a.dbg_counts = d->dbg_counts;
+  a.dbg_bias = d->dbg_bias;
+  a.dbg_stats = d->dbg_stats;
+  a.dbg_sigma = d->dbg_sigma;
+  a.dbg_phase_ns = d->dbg_phase_ns;
+  const plm_bookkeeping& b = d->book;
+  a.book = Bookkeeping{b.mode,       b.k,     b.best_val, b.best_idx,       b.n_tiles, b.rows,
+                       b.out,        b.out_cap, b.base,   b.offset,         b.anchor,  b.pending,
+                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len};
+  a.counter = reinterpret_cast<int*>(scratch);
+  a.err = device_error != nullptr ? device_error : reinterpret_cast<int*>(scratch) + 1;
+  st = verify_validate(a, d->n_rows);
   if (st != PLM_OK) return st;
   return verify_launch(a, d->dtype, d->n_rows, static_cast<cudaStream_t>(stream), true);
 }

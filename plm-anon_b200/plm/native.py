@@ -133,6 +133,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_gemm_tiles": [c_int32, c_int32, c_int32, POINTER(c_int32)],
     "plm_gemm": [c_void_p, POINTER(GemmDesc), c_void_p],
     "plm_verify_decode": [c_void_p, POINTER(VerifyDesc), c_void_p],
+    "plm_verify_decode_static": [POINTER(VerifyDesc), c_void_p, c_void_p],
     "plm_attention": [c_void_p, POINTER(AttentionDesc), c_void_p],
     "plm_kv_append": [c_void_p, POINTER(KvAppendDesc), c_void_p],
     "plm_add_rmsnorm": [c_void_p, POINTER(AddRmsNormDesc), c_void_p],
