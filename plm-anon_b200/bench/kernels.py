@@ -20,12 +20,22 @@ from pathlib import Path
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 
 
-def _time(fn, iters: int, warmup: int, graph: bool) -> float:
+def _time(fn, iters: int, warmup: int, graph: bool, flush: bool = False) -> float:
     import torch
 
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if flush:  # every launch timed alone after 256 MB of writes have evicted L2 (weights and KV come from HBM)
+        buf = torch.empty(64 * 2**20, dtype=torch.float32, device="cuda")
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for start, end in events:
+            buf.add_(1.0)
+            start.record()
+            fn()
+            end.record()
+        torch.cuda.synchronize()
+        return 1000 * sum(start.elapsed_time(end) for start, end in events) / iters
     if graph:
         g = torch.cuda.CUDAGraph()
         stream = torch.cuda.Stream()
@@ -62,7 +72,7 @@ def bench_gemm(args, ctx):
     kind = {"store": native.EPI_STORE, "silu": native.EPI_SILU_MUL}[args.epi]
     epi = native.GemmEpilogue(kind=kind, gate_offset=args.n_out // 2)
     fn = lambda: native.gemm(ctx, w, x, args.rows, out=out, epi=epi, splits=args.splits)  # noqa: E731
-    us = _time(fn, args.iters, args.warmup, not args.no_graph)
+    us = _time(fn, args.iters, args.warmup, not args.no_graph, args.flush)
     ctx.check()
     nbytes = args.n_out * args.k * 2 + args.rows * args.k * 2 + args.rows * args.n_out * 2
     return {"kernel": "skinny_gemm_kernel", "n_out": args.n_out, "k": args.k, "rows": args.rows, "epi": args.epi,
@@ -95,7 +105,7 @@ def bench_attention(args, ctx):
                                 own_start=o32.data_ptr(), num_heads=heads, num_kv_heads=heads, head_dim=hd,
                                 out=out.data_ptr(), splits=args.splits, max_keys=total)
     fn = lambda: native.attention(ctx, desc)  # noqa: E731
-    us = _time(fn, args.iters, args.warmup, not args.no_graph)
+    us = _time(fn, args.iters, args.warmup, not args.no_graph, args.flush)
     ctx.check()
     nbytes = total * heads * hd * 2 * 2 + 2 * rows * heads * hd * 2
     return {"kernel": "round_attention_kernel", "ctx": args.ctx, "rows": rows, "heads": heads, "head_dim": hd,
@@ -120,7 +130,7 @@ def bench_verify(args, ctx):
     phases = torch.zeros(args.rows, 16, dtype=torch.int64, device="cuda")
     desc.dbg_phase_ns = phases.data_ptr()
     fn = lambda: native.verify_decode(ctx, desc)  # noqa: E731
-    us = _time(fn, args.iters, args.warmup, not args.no_graph)
+    us = _time(fn, args.iters, args.warmup, not args.no_graph, args.flush)
     ctx.check()
     names = ["stats", "rule", "slice_select", "merge_copy", "merge_sort", "staging", "quota_spread_prior", "condense0",
              "fit0", "condense1", "fit1", "final_sync", "argmin"]
@@ -138,6 +148,7 @@ def main() -> None:
         p.add_argument("--iters", type=int, default=20)
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--no-graph", action="store_true")
+        p.add_argument("--flush", action="store_true", help="evict L2 before every timed launch")
         p.add_argument("--splits", type=int, default=0)
         if name == "gemm":
             p.add_argument("--n-out", type=int, default=16384)

@@ -21,9 +21,12 @@ int gemm_token_tile(int rows) {
 
 namespace {
 
-template <int NTOK>
+// Pipeline depth: a ring of about 72 KB, so that three CTAs share an SM and one CTA's prologue and epilogue overlap
+// the others' weight streaming (at least 2 stages).
+template <int NTOK, int EPI>
 constexpr int stages_for() {
-  return NTOK <= 16 ? 5 : NTOK <= 64 ? 4 : 3;
+  constexpr int by_budget = (72 * 1024) / GemmShape<NTOK>::STAGE_BYTES;
+  return by_budget < 2 ? 2 : by_budget;
 }
 
 int tiles_for(int kind, int n_out, int gate_offset) {
@@ -53,7 +56,7 @@ GemmArgs make_args(plm_ctx* ctx, const plm_gemm_desc& d, int tiles, int splits, 
 template <typename T, int NTOK, int EPI>
 int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,
                cudaStream_t stream, bool pdl) {
-  constexpr int STAGES = stages_for<NTOK>();
+  constexpr int STAGES = stages_for<NTOK, EPI>();
   constexpr int SMEM = gemm_smem_bytes<NTOK, STAGES>();
   auto kernel = skinny_gemm_kernel<T, NTOK, STAGES, EPI>;
   static bool attr_set = false;
@@ -65,9 +68,10 @@ int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, c
   }
   const int tiles = tiles_for(EPI, d.n_out, d.epi.gate_offset);
   const int total_kb = d.k / kGemmBK;
-  int splits = d.splits > 0 ? d.splits : gemm_cluster_splits(tiles, total_kb, ctx->num_sms);
-  if (splits > 8 || (splits & (splits - 1)) != 0 || splits > total_kb)
-    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits (a power of two <= 8 and <= k/64)", splits);
+  const int per_sm = ctx->smem_per_sm > 0 ? ctx->smem_per_sm / (SMEM + 1024) : 1;
+  int splits = d.splits > 0 ? d.splits : gemm_cluster_splits(tiles, total_kb, ctx->num_sms * (per_sm > 0 ? per_sm : 1));
+  if (splits > 8 || splits > total_kb)
+    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits (at most 8 and at most k/64)", splits);
   if (NTOK > 128) splits = 1;  // the staging area holds no reduced slice for the widest tiles
   const int kb_per = (total_kb + splits - 1) / splits;
   if (kb_per * (splits - 1) >= total_kb)

@@ -27,8 +27,7 @@ EncodeTiledFn encode_fn() {
 
 // Split-reduction scratch of a context: enough for the widest launch of the round (lm_head over 50k features
 // at 3 splits and 64 rows is 38.6 MB).
-constexpr size_t kPartialFloats = size_t(16) << 20;  // 64 MB
-constexpr int kCounters = 8192;
+constexpr int kCounters = 64;
 }  // namespace
 
 namespace plm {
@@ -67,15 +66,24 @@ int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner,
   return PLM_OK;
 }
 
-int gemm_cluster_splits(int tiles, int total_kb, int num_sms) {
-  int s = 1;
-  while (s < 8 && tiles * s < num_sms) {
-    const int next = 2 * s;
-    const int per = (total_kb + next - 1) / next;
-    if (next > total_kb || per * (next - 1) >= total_kb) break;  // every split needs at least one k-block
-    s = next;
+int gemm_cluster_splits(int tiles, int total_kb, int slots) {
+  // Splits of a tile run as one cluster (at most 8 CTAs). Estimated time in k-block units: waves over the
+  // `slots` resident CTAs times (k-blocks per split + a fixed cost of kGemmOverheadKb for pipeline fill and the
+  // epilogue). The cheapest split count wins; ties keep fewer splits (less reduction work).
+  constexpr int kGemmOverheadKb = 4;
+  int best = 1;
+  long best_cost = -1;
+  for (int s = 1; s <= 8 && s <= total_kb; ++s) {
+    const int per = (total_kb + s - 1) / s;
+    if (per * (s - 1) >= total_kb) continue;  // every split needs at least one k-block
+    const long waves = (long(tiles) * s + slots - 1) / slots;
+    const long cost = waves * (per + kGemmOverheadKb);
+    if (best_cost < 0 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
   }
-  return s;
+  return best;
 }
 
 }  // namespace plm
@@ -103,6 +111,9 @@ int plm_ctx_create(plm_ctx** out) {
   if (st == PLM_OK)
     st = check_cuda(cudaDeviceGetAttribute(&c->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device),
                     "cudaDeviceGetAttribute(smem)");
+  if (st == PLM_OK)
+    st = check_cuda(cudaDeviceGetAttribute(&c->smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, c->device),
+                    "cudaDeviceGetAttribute(smem per SM)");
   if (st == PLM_OK) {
     int major = 0, minor = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, c->device);
@@ -113,8 +124,6 @@ int plm_ctx_create(plm_ctx** out) {
   }
   if (st == PLM_OK) st = check_cuda(cudaMalloc(&c->err, sizeof(int)), "cudaMalloc(error word)");
   if (st == PLM_OK) st = check_cuda(cudaMemset(c->err, 0, sizeof(int)), "cudaMemset(error word)");
-  if (st == PLM_OK) st = check_cuda(cudaMalloc(&c->partial, kPartialFloats * sizeof(float)), "cudaMalloc(scratch)");
-  if (st == PLM_OK) c->partial_floats = kPartialFloats;
   if (st == PLM_OK) st = check_cuda(cudaMalloc(&c->counters, kCounters * sizeof(int)), "cudaMalloc(counters)");
   if (st == PLM_OK) st = check_cuda(cudaMemset(c->counters, 0, kCounters * sizeof(int)), "cudaMemset(counters)");
   if (st == PLM_OK) c->n_counters = kCounters;
@@ -130,7 +139,6 @@ int plm_ctx_create(plm_ctx** out) {
 int plm_ctx_destroy(plm_ctx* ctx) {
   if (ctx == nullptr) return PLM_OK;
   cudaFree(ctx->err);
-  cudaFree(ctx->partial);
   cudaFree(ctx->counters);
   delete ctx;
   return PLM_OK;

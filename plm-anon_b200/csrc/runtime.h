@@ -16,9 +16,8 @@ struct plm_ctx {
   int device = 0;
   int num_sms = 148;
   int max_smem_optin = 0;
+  int smem_per_sm = 0;
   int* err = nullptr;           // device error word
-  float* partial = nullptr;     // split-reduction scratch (fp32)
-  size_t partial_floats = 0;
   int* counters = nullptr;      // arrival counters, zero between launches
   int n_counters = 0;
 };
@@ -77,9 +76,8 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   return launch_cluster(kernel, grid, block, smem, stream, pdl, 1, 1, std::forward<Args>(args)...);
 }
 
-// Cluster size for the k-split of a weight-streaming GEMM: the smallest power of two (<= 8, <= the k-blocks)
-// whose grid covers every SM once.
-int gemm_cluster_splits(int tiles, int total_kb, int num_sms);
+// Cluster size (1..8) for the k-split of a weight-streaming GEMM over `slots` resident CTAs (SMs x CTAs per SM).
+int gemm_cluster_splits(int tiles, int total_kb, int slots);
 
 // Internal GEMM launch used by plm_gemm and by the round engine (`map_w` encoded once per weight).
 int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,

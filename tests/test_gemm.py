@@ -39,7 +39,7 @@ def test_store_matches_fp32(ctx, n_out, k, rows):
     _close(out, ref)
 
 
-@pytest.mark.parametrize("splits", [1, 2, 4, 8])
+@pytest.mark.parametrize("splits", [1, 2, 3, 4, 5, 8])
 def test_forced_splits_and_determinism(ctx, splits):
     from plm import native
 
