@@ -23,6 +23,22 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100a GPU and the built libplm_native.so")
 
 
+def cli_bench():
+    """The CLI package plm-anon_b200/bench as (generate, harness). The name ``bench`` also belongs to the benchmark
+    script at the repository root, which wins on sys.path when pytest runs from there."""
+    import importlib
+
+    cached = sys.modules.get("bench")
+    if cached is None or not hasattr(cached, "__path__"):
+        sys.modules.pop("bench", None)
+        sys.path.insert(0, str(PACKAGE))
+        try:
+            importlib.import_module("bench")
+        finally:
+            sys.path.remove(str(PACKAGE))
+    return importlib.import_module("bench.generate"), importlib.import_module("bench.harness")
+
+
 @pytest.fixture(scope="session")
 def ctx():
     import torch

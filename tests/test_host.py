@@ -106,3 +106,39 @@ def test_multi_rank_reduction_gloo():
         assert p.exitcode == 0
     for _, elapsed, tokens in results:
         assert elapsed == 11.0 and tokens == 201
+
+
+def test_generate_cli_surface(tmp_path):
+    """bench.generate / bench.harness: the reference's flags parse, datasets load (token-id lists and the random
+    spec), per-pass aggregates follow bench/harness.py:33-39, and the baselines outside the round path exit."""
+    import argparse
+    import json
+
+    from tests.conftest import cli_bench
+
+    generate, harness = cli_bench()
+
+    parser = argparse.ArgumentParser()
+    generate.add_arguments(parser)
+    harness.add_run_arguments(parser)
+    args = parser.parse_args(["--model", "synthetic:plm-tiny", "--match", "relaxed", "--setting", "pretrain",
+                              "--dataset", "random:3:16:5", "--tokens", "32", "--seeds", "0", "1"])
+    assert (args.match, args.setting, args.k, args.seeds, args.tokens) == ("relaxed", "pretrain", None, [0, 1], 32)
+    ds = harness.load_dataset(args.dataset, 2, vocab=1000)
+    assert len(ds) == 2 and all(len(p) == 16 and max(p) < 1000 for p in ds)
+    assert ds == harness.load_dataset("random:3:16:5", 2, vocab=1000)
+    path = tmp_path / "prompts.json"
+    path.write_text(json.dumps([[1, 2, 3], "text"]))
+    assert harness.load_dataset(str(path), None) == [[1, 2, 3], "text"]
+    path.write_text(json.dumps({"not": "a list"}))
+    with pytest.raises(SystemExit):
+        harness.load_dataset(str(path), None)
+    records = [harness.speed_record("p", "", [1, 2], 2, 10, 100.0, 40.0, 8),
+               harness.speed_record("q", "", [0], 1, 5, 50.0, 20.0, 3)]
+    agg = harness.aggregate(records)
+    assert agg["calls"] == 3 and agg["tokens"] == 15
+    assert abs(agg["tokens_per_second"] - 1000 * 15 / 60.0) < 1e-9
+    assert abs(agg["e2e_tokens_per_second"] - 1000 * 15 / 150.0) < 1e-9
+    args.ar = True
+    with pytest.raises(SystemExit):
+        generate.build_generator(args)

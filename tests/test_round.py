@@ -191,3 +191,25 @@ def test_decoder_generate_end_to_end():
     assert all(0 <= t < cfg.vocab for t in a.token_ids)
     assert a.token_ids != c.token_ids
     assert a.steady_rounds >= 1 and a.steady_tokens >= a.steady_rounds
+
+
+@pytest.mark.gpu
+def test_generate_cli_end_to_end(tmp_path):
+    """python -m bench.generate on a tiny synthetic model: the results file has one pass per seed, every request
+    produced its tokens, and a seed reproduces its tokens (the warm-up pass and the measured pass of seed 0)."""
+    import json
+
+    from tests.conftest import cli_bench
+
+    generate, _ = cli_bench()
+
+    out = tmp_path / "results.json"
+    result = generate.main(["--model", "synthetic:plm-tiny", "--k", "4", "--dataset", "random:2:24:1", "--tokens", "40",
+                            "--seeds", "0", "0", "--block-size", "16", "--out", str(out)])
+    saved = json.loads(out.read_text())
+    assert saved["config"]["k"] == 4 and len(saved["passes"]) == 2
+    for p in saved["passes"]:
+        assert p["aggregate"]["prompts"] == 2 and p["aggregate"]["tokens"] == 80
+        assert all(len(r["token_ids"]) == 40 for r in p["results"])
+    first, second = (p["results"] for p in result["passes"])
+    assert [r["token_ids"] for r in first] == [r["token_ids"] for r in second]
