@@ -65,10 +65,13 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.perf_counter() + 3.0  # the timed region starts once sampling runs
+            while not self.samples and time.perf_counter() < deadline:
+                time.sleep(0.01)
         except FileNotFoundError:
             self.proc = None
         return self
@@ -366,20 +369,21 @@ def run_native(args) -> None:
     del graph, keep
 
     # end to end through the public API (configs[2] per request)
-    e2e_reqs = max(1, min(3, args.steps // 10 or 1))
-    prompt = torch.randint(0, cfg.vocab, (PROMPT_E2E,), generator=torch.Generator().manual_seed(0)).pin_memory()
-    decoder.generate(prompt, TOKENS_E2E, seed=0, stop_at_eos=False)  # warm-up request
-    if dist:
-        dist.barrier()
-    t0 = time.perf_counter()
-    e2e_tokens, e2e_rounds = 0, 0
-    for i in range(e2e_reqs):
-        res = decoder.generate(prompt, TOKENS_E2E, seed=i, stop_at_eos=False)
-        e2e_tokens += len(res.token_ids)
-        e2e_rounds += res.steady_rounds
-    e2e_s = time.perf_counter() - t0
-    e2e_s, e2e_tokens = reduce_over_ranks(dist, e2e_s, e2e_tokens)
-    e2e_value = e2e_tokens / e2e_s
+    e2e_reqs = 0 if args.skip_e2e else max(1, min(3, args.steps // 10 or 1))
+    e2e_tokens, e2e_rounds, e2e_s = 0, 0, 0.0
+    if e2e_reqs:
+        prompt = torch.randint(0, cfg.vocab, (PROMPT_E2E,), generator=torch.Generator().manual_seed(0)).pin_memory()
+        decoder.generate(prompt, TOKENS_E2E, seed=0, stop_at_eos=False)  # warm-up request
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_reqs):
+            res = decoder.generate(prompt, TOKENS_E2E, seed=i, stop_at_eos=False)
+            e2e_tokens += len(res.token_ids)
+            e2e_rounds += res.steady_rounds
+        e2e_s = time.perf_counter() - t0
+        e2e_s, e2e_tokens = reduce_over_ranks(dist, e2e_s, e2e_tokens)
+    e2e_value = e2e_tokens / e2e_s if e2e_s else None
 
     cpu = None
     if rank == 0 and not args.skip_cpu:
@@ -406,7 +410,7 @@ def run_native(args) -> None:
             "round_roofline": {"bound": "hbm", "achieved": round_achieved, "peak": peak, "unit": "GB/s",
                                "frac": round_achieved / peak, "bytes_per_round": bytes_},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": PROMPT_E2E * 8,
-                    "d2h_bytes_per_step": int(e2e_rounds / e2e_reqs) * (8 + 8 * 1024) + TOKENS_E2E * 8,
+                    "d2h_bytes_per_step": int(e2e_rounds / max(e2e_reqs, 1)) * (8 + 8 * 1024) + TOKENS_E2E * 8,
                     "step": f"one request: {PROMPT_E2E}-token prompt, {TOKENS_E2E} new tokens", "requests": e2e_reqs},
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_round * args.steps,
@@ -422,10 +426,11 @@ def run_native(args) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", default="native", choices=("native", "reference"))
     parser.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
+    parser.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end requests (profiling runs)")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "native":
         args.warmup = 3

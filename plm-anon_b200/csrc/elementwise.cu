@@ -8,7 +8,23 @@ namespace plm {
 namespace {
 
 constexpr int kRowThreads = 256;
-constexpr int kMaxPerThread = 16;  // hidden <= 4096
+constexpr int kVec = 8;      // 16-byte vectors of bf16
+constexpr int kMaxVecs = 2;  // vectors per thread: hidden <= kRowThreads * kVec * kMaxVecs = 4096
+
+// The row's 16-byte vectors owned by this thread: vector j is elements [8 (tid + j 256), ... + 8).
+template <typename T>
+__device__ __forceinline__ void load_row(const T* __restrict__ src, int hidden, uint4 (&out)[kMaxVecs]) {
+#pragma unroll
+  for (int j = 0; j < kMaxVecs; ++j) {
+    const int c = threadIdx.x + j * kRowThreads;
+    out[j] = c * kVec < hidden ? reinterpret_cast<const uint4*>(src)[c] : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float elem(const uint4& v, int e) {
+  return to_f32<T>(reinterpret_cast<const T*>(&v)[e]);
+}
 
 __device__ __forceinline__ float block_sum_rows(float v, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -92,28 +108,34 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
     const int64_t tok = id < 0 ? 0 : (id > a.vocab - 1 ? a.vocab - 1 : id);
     src = reinterpret_cast<const T*>(a.embed) + size_t(tok) * a.hidden;
   }
-  T* res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
-  T* nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
-  const T* w = reinterpret_cast<const T*>(a.norm_weight);
-  float v[kMaxPerThread];
+  T* __restrict__ res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
+  T* __restrict__ nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
+  const T* __restrict__ w = reinterpret_cast<const T*>(a.norm_weight);
+  uint4 e[kMaxVecs], wv[kMaxVecs];
+  load_row<T>(src, a.hidden, e);
+  load_row<T>(w, a.hidden, wv);
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxPerThread; ++j) {
-    const int i = tid + j * kRowThreads;
-    v[j] = 0.f;
-    if (i < a.hidden) {
-      const T e = src[i];
-      res[i] = e;
-      v[j] = to_f32<T>(e);
-      ss += v[j] * v[j];
+  for (int j = 0; j < kMaxVecs; ++j) {
+    const int c = tid + j * kRowThreads;
+    if (c * kVec < a.hidden) {
+      reinterpret_cast<uint4*>(res)[c] = e[j];
+#pragma unroll
+      for (int q = 0; q < kVec; ++q) ss += elem<T>(e[j], q) * elem<T>(e[j], q);
     }
   }
   ss = block_sum_rows(ss, red);
   const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
 #pragma unroll
-  for (int j = 0; j < kMaxPerThread; ++j) {
-    const int i = tid + j * kRowThreads;
-    if (i < a.hidden) nrm[i] = from_f32<T>(round_to<T>(v[j] * rstd) * to_f32<T>(w[i]));
+  for (int j = 0; j < kMaxVecs; ++j) {
+    const int c = tid + j * kRowThreads;
+    if (c * kVec < a.hidden) {
+      uint4 o;
+      T* ov = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int q = 0; q < kVec; ++q) ov[q] = from_f32<T>(round_to<T>(elem<T>(e[j], q) * rstd) * elem<T>(wv[j], q));
+      reinterpret_cast<uint4*>(nrm)[c] = o;
+    }
   }
 }
 
@@ -126,32 +148,44 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs
   const int r = blockIdx.x, tid = threadIdx.x;
   grid_dependency_wait();
   allow_dependents();
-  const T* x = reinterpret_cast<const T*>(a.x) + size_t(r) * a.hidden;
-  T* res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
-  T* nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
-  const T* w = reinterpret_cast<const T*>(a.weight);
+  const T* __restrict__ x = reinterpret_cast<const T*>(a.x) + size_t(r) * a.hidden;
+  T* __restrict__ res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
+  T* __restrict__ nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
+  const T* __restrict__ w = reinterpret_cast<const T*>(a.weight);
   T* gathered = (r == a.gather_row && a.gathered != nullptr) ? reinterpret_cast<T*>(a.gathered) : nullptr;
-  float v[kMaxPerThread];
+  uint4 xv[kMaxVecs], rv[kMaxVecs], wv[kMaxVecs];  // every load of the row is issued before any store
+  load_row<T>(x, a.hidden, xv);
+  load_row<T>(res, a.hidden, rv);
+  load_row<T>(w, a.hidden, wv);
+  float v[kMaxVecs][kVec];
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxPerThread; ++j) {
-    const int i = tid + j * kRowThreads;
-    v[j] = 0.f;
-    if (i < a.hidden) {
-      v[j] = to_f32<T>(x[i]) + to_f32<T>(res[i]);
-      res[i] = from_f32<T>(v[j]);
-      ss += v[j] * v[j];
+  for (int j = 0; j < kMaxVecs; ++j) {
+    const int c = tid + j * kRowThreads;
+    if (c * kVec < a.hidden) {
+      uint4 o;
+      T* ov = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int q = 0; q < kVec; ++q) {
+        v[j][q] = elem<T>(xv[j], q) + elem<T>(rv[j], q);
+        ov[q] = from_f32<T>(v[j][q]);
+        ss += v[j][q] * v[j][q];
+      }
+      reinterpret_cast<uint4*>(res)[c] = o;
     }
   }
   ss = block_sum_rows(ss, red);
   const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
 #pragma unroll
-  for (int j = 0; j < kMaxPerThread; ++j) {
-    const int i = tid + j * kRowThreads;
-    if (i < a.hidden) {
-      const T out = from_f32<T>(round_to<T>(v[j] * rstd) * to_f32<T>(w[i]));
-      nrm[i] = out;
-      if (gathered != nullptr) gathered[i] = out;
+  for (int j = 0; j < kMaxVecs; ++j) {
+    const int c = tid + j * kRowThreads;
+    if (c * kVec < a.hidden) {
+      uint4 o;
+      T* ov = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int q = 0; q < kVec; ++q) ov[q] = from_f32<T>(round_to<T>(v[j][q] * rstd) * elem<T>(wv[j], q));
+      reinterpret_cast<uint4*>(nrm)[c] = o;
+      if (gathered != nullptr) reinterpret_cast<uint4*>(gathered)[c] = o;
     }
   }
 }
@@ -188,13 +222,15 @@ __global__ void kv_append_kernel(const KvAppendArgs a) {
 }  // namespace
 
 int prologue_launch(const PrologueArgs& a, int rows, cudaStream_t stream, bool pdl) {
-  if (a.hidden > kRowThreads * kMaxPerThread) return fail(PLM_ERR_UNSUPPORTED, "prologue: hidden %d", a.hidden);
+  if (a.hidden > kRowThreads * kVec * kMaxVecs || a.hidden % kVec != 0)
+    return fail(PLM_ERR_UNSUPPORTED, "prologue: hidden %d (a multiple of 8, at most 4096)", a.hidden);
   return check_cuda(launch(embed_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
                     "embed_norm_kernel");
 }
 
 int add_norm_launch(const AddNormArgs& a, int rows, cudaStream_t stream, bool pdl) {
-  if (a.hidden > kRowThreads * kMaxPerThread) return fail(PLM_ERR_UNSUPPORTED, "add_norm: hidden %d", a.hidden);
+  if (a.hidden > kRowThreads * kVec * kMaxVecs || a.hidden % kVec != 0)
+    return fail(PLM_ERR_UNSUPPORTED, "add_norm: hidden %d (a multiple of 8, at most 4096)", a.hidden);
   return check_cuda(launch(add_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
                     "add_norm_kernel");
 }
