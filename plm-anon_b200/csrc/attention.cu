@@ -21,6 +21,8 @@ namespace {
 constexpr int kKeysPerTile = 64;
 constexpr int kAttnThreads = 128;
 constexpr int kQRowsPerCta = 64;
+constexpr int kStages = 3;           // K/V tiles in flight per CTA (two CTAs still share an SM)
+constexpr int kMaxPageSlice = 1024;  // block-table entries staged per CTA (keys per CTA <= 1023 pages)
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -57,26 +59,80 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
   constexpr int NT = kKeysPerTile / 8;  // key n-tiles per tile
   constexpr int KS = HD / 16;           // k-steps over the head dim
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* kbuf[2] = {smem, smem + TILE_BYTES};
-  uint8_t* vbuf[2] = {smem + 2 * TILE_BYTES, smem + 3 * TILE_BYTES};
+  auto kbuf = [&](int slot) { return smem + (2 * slot) * TILE_BYTES; };  // ring slot: K tile, then V tile
+  auto vbuf = [&](int slot) { return smem + (2 * slot + 1) * TILE_BYTES; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
   const int head = blockIdx.x, split = blockIdx.y, qt = blockIdx.z;
   const int group = head / (a.num_heads / a.num_kv_heads);
 
-  grid_dependency_wait();
-  allow_dependents();
-
+  // Before the dependency wait: everything the previous kernel does not write. The offset comes from an earlier
+  // kernel (the last round's commit, or a copy before a prefill), the block table and the layout are static, and
+  // the context keys [0, offset) were written by earlier rounds; only the query rows and the round's own K/V come
+  // from the QKV projection this kernel follows.
   const int64_t offset = *a.offset;
   const int64_t seq_len = offset + a.rows;
   const int n_tiles = int((seq_len + kKeysPerTile - 1) / kKeysPerTile);
-  const int per = (n_tiles + a.splits - 1) / a.splits;
-  const int t0 = split * per;
-  const int t1 = min(n_tiles, t0 + per);
+  const int t0 = int(int64_t(split) * n_tiles / a.splits);  // tiles spread evenly over the splits
+  const int t1 = int(int64_t(split + 1) * n_tiles / a.splits);
+  const int n_local = t1 - t0;
+  int* pages = reinterpret_cast<int*>(smem + 2 * kStages * TILE_BYTES);
+  const int64_t lp0 = int64_t(t0) * kKeysPerTile / a.page_size;
+  const int n_pages = n_local > 0 ? int((int64_t(t1) * kKeysPerTile - 1) / a.page_size - lp0 + 1) : 0;
+  const bool staged_pages = n_pages <= kMaxPageSlice;
+  for (int i = tid; i < (staged_pages ? n_pages : 0); i += kAttnThreads) {
+    const int64_t lp = lp0 + i;
+    pages[i] = lp < a.max_pages ? a.block_table[lp] : -1;
+  }
+  const int r0 = qt * kQRowsPerCta + warp * 16 + gq, r1 = r0 + 8;
+  const int dep0 = r0 < a.rows ? a.depth[r0] : -1, own0 = r0 < a.rows ? a.own_start[r0] : (1 << 30);
+  const int dep1 = r1 < a.rows ? a.depth[r1] : -1, own1 = r1 < a.rows ? a.own_start[r1] : (1 << 30);
+  __syncthreads();
+
+  const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
+  const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache);
+  auto issue = [&](int t, int buf) {  // tile t (absolute) into ring slot buf; one commit group per call
+#pragma unroll
+    for (int i = 0; i < (kKeysPerTile * CH) / kAttnThreads; ++i) {
+      const int idx = tid + i * kAttnThreads;
+      const int row = idx / CH, chunk = idx % CH;
+      const int64_t kv = int64_t(t) * kKeysPerTile + row;
+      bool valid = kv < seq_len;
+      size_t src = 0;
+      if (valid) {
+        const int64_t lp = kv / a.page_size;
+        const int page = staged_pages ? pages[lp - lp0] : (lp < a.max_pages ? a.block_table[lp] : -1);
+        if (page < 0 || page >= a.num_pages) {
+          record_error(a.err, kErrBadIndex);
+          valid = false;
+        } else {
+          src = ((size_t(page) * a.num_kv_heads + group) * a.page_size + size_t(kv % a.page_size)) * HD + chunk * 8;
+        }
+      }
+      cp_async_16(kbuf(buf) + swz<HD>(row, chunk), kc + src, valid);
+      cp_async_16(vbuf(buf) + swz<HD>(row, chunk), vc + src, valid);
+    }
+  };
+  // Pipeline prologue: kStages - 1 commit groups. Tiles lying wholly in the context go out before the wait.
+  int64_t whole = offset / kKeysPerTile - t0;  // tiles of this CTA whose last key lies below offset
+  whole = whole < 0 ? 0 : (whole > n_local ? n_local : whole);
+  const int ctx_tiles = int(whole);
+  int issued = 0;
+  for (; issued < kStages - 1 && issued < ctx_tiles; ++issued) {
+    issue(t0 + issued, issued);
+    cp_async_commit();
+  }
+
+  grid_dependency_wait();
+  allow_dependents();
+
+  for (; issued < kStages - 1; ++issued) {
+    if (issued < n_local) issue(t0 + issued, issued);
+    cp_async_commit();
+  }
 
   // ---- query fragments (A operand, rows r0 and r0 + 8 of this warp) ----
-  const int r0 = qt * kQRowsPerCta + warp * 16 + gq, r1 = r0 + 8;
   const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
   const size_t q_stride = size_t(a.num_heads) * HD;
   uint32_t qf[KS][4];
@@ -92,34 +148,6 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
     qf[kk][2] = ld(r0, col + 8);
     qf[kk][3] = ld(r1, col + 8);
   }
-  const int dep0 = r0 < a.rows ? a.depth[r0] : -1, own0 = r0 < a.rows ? a.own_start[r0] : (1 << 30);
-  const int dep1 = r1 < a.rows ? a.depth[r1] : -1, own1 = r1 < a.rows ? a.own_start[r1] : (1 << 30);
-
-  const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
-  const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache);
-  auto issue = [&](int t, int buf) {
-#pragma unroll
-    for (int i = 0; i < (kKeysPerTile * CH) / kAttnThreads; ++i) {
-      const int idx = tid + i * kAttnThreads;
-      const int row = idx / CH, chunk = idx % CH;
-      const int64_t kv = int64_t(t) * kKeysPerTile + row;
-      bool valid = kv < seq_len;
-      size_t src = 0;
-      if (valid) {
-        const int64_t lp = kv / a.page_size;
-        const int page = lp < a.max_pages ? a.block_table[lp] : -1;
-        if (page < 0 || page >= a.num_pages) {
-          record_error(a.err, kErrBadIndex);
-          valid = false;
-        } else {
-          src = ((size_t(page) * a.num_kv_heads + group) * a.page_size + size_t(kv % a.page_size)) * HD + chunk * 8;
-        }
-      }
-      cp_async_16(kbuf[buf] + swz<HD>(row, chunk), kc + src, valid);
-      cp_async_16(vbuf[buf] + swz<HD>(row, chunk), vc + src, valid);
-    }
-    cp_async_commit();
-  };
 
   float o[HD / 8][4];
 #pragma unroll
@@ -127,18 +155,14 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float scale = a.scale_log2;
 
-  if (t0 < t1) issue(t0, 0);
-  for (int t = t0; t < t1; ++t) {
-    const int buf = (t - t0) & 1;
-    if (t + 1 < t1) {
-      issue(t + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint8_t* kb = kbuf[buf];
-    const uint8_t* vb = vbuf[buf];
+  for (int i = 0; i < n_local; ++i) {
+    const int t = t0 + i, buf = i % kStages;
+    cp_async_wait<kStages - 2>();  // tile i has landed (one group is committed per tile, empty ones included)
+    __syncthreads();               // ... for every thread, and slot (i - 1) % kStages is free again
+    if (i + kStages - 1 < n_local) issue(t + kStages - 1, (i + kStages - 1) % kStages);
+    cp_async_commit();
+    const uint8_t* kb = kbuf(buf);
+    const uint8_t* vb = vbuf(buf);
 
     float s[NT][4];
 #pragma unroll
@@ -228,8 +252,9 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
         mma_bf16(o[2 * nn + 1], pa, b[2], b[3]);
       }
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
+  __syncthreads();  // the ring is reused by the split combine below
 
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -328,7 +353,7 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
 
 template <int HD>
 int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool pdl) {
-  constexpr int SMEM = 4 * kKeysPerTile * HD * 2;
+  constexpr int SMEM = 2 * kStages * kKeysPerTile * HD * 2 + kMaxPageSlice * 4;
   auto kernel = round_attention_kernel<HD>;
   static bool attr = false;
   if (!attr) {
