@@ -263,6 +263,11 @@ __device__ __forceinline__ float2 ld_dsmem_f32x2(uint32_t addr) {
   asm("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
 
 // ----------------------------------------------------------------------------------------------------------------
 // Element helpers: the model's storage dtype is bf16 or f16; arithmetic is fp32.

@@ -79,7 +79,7 @@ struct GemmArgs {
 
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 128;
-constexpr int kStagePad = 129;  // fp32 staging row stride (odd: conflict-free both ways)
+constexpr int kStagePad = 132;  // fp32 staging row stride (16-byte rows for vector loads of a column's features)
 
 template <int NTOK>
 struct GemmShape {
@@ -275,17 +275,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t peer[8];
 #pragma unroll
     for (int s = 0; s < 8; ++s) peer[s] = s < S ? cluster_map(stage, uint32_t(s)) : 0u;
-    for (int idx = tid; idx < (c_end - c_begin) * 128; idx += kGemmThreads) {
-      const int c = c_begin + (idx >> 7), f = idx & 127;
-      const uint32_t off = uint32_t(c * kStagePad + f) * 4u;
-      float part[8];
+    // 16-byte remote loads: thread tid takes features [4 (tid % 32), +4) of local columns tid / 32, + 4, ...; the
+    // loads of kPullCols of its columns from every rank are issued before any is summed.
+    constexpr int kPullCols = 4;
+    const int ncols_red = c_end - c_begin;
+    const int fq = (tid & 31) * 4, cq = tid >> 5;
+    for (int i0 = cq; i0 < ncols_red; i0 += 4 * kPullCols) {
+      float4 part[kPullCols][8];
 #pragma unroll
-      for (int s = 0; s < 8; ++s) part[s] = s < S ? ld_dsmem_f32(peer[s] + off) : 0.f;
-      float acc = 0.f;
+      for (int i = 0; i < kPullCols; ++i) {
+        const int lc = i0 + 4 * i;
+        const uint32_t off = uint32_t((c_begin + lc) * kStagePad + fq) * 4u;
 #pragma unroll
-      for (int s = 0; s < 8; ++s)
-        if (s < S) acc += part[s];
-      red[(c - c_begin) * kStagePad + f] = acc;
+        for (int s = 0; s < 8; ++s)
+          part[i][s] = (s < S && lc < ncols_red) ? ld_dsmem_f32x4(peer[s] + off) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kPullCols; ++i) {
+        const int lc = i0 + 4 * i;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          if (s < S) {
+            acc.x += part[i][s].x;
+            acc.y += part[i][s].y;
+            acc.z += part[i][s].z;
+            acc.w += part[i][s].w;
+          }
+        }
+        if (lc < ncols_red) *reinterpret_cast<float4*>(red + lc * kStagePad + fq) = acc;
+      }
     }
     cluster_sync();
   } else {
