@@ -53,7 +53,7 @@ __device__ __forceinline__ int swz(int row, int chunk) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;
   constexpr int TILE_BYTES = kKeysPerTile * HD * 2;
   constexpr int NT = kKeysPerTile / 8;  // key n-tiles per tile
@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
   const int t1 = int(int64_t(split + 1) * n_tiles / a.splits);
   const int n_local = t1 - t0;
   int* pages = reinterpret_cast<int*>(smem + 2 * kStages * TILE_BYTES);
-  const int64_t lp0 = int64_t(t0) * kKeysPerTile / a.page_size;
-  const int n_pages = n_local > 0 ? int((int64_t(t1) * kKeysPerTile - 1) / a.page_size - lp0 + 1) : 0;
+  const int64_t lp0 = (int64_t(t0) * kKeysPerTile) >> a.page_shift;
+  const int n_pages = n_local > 0 ? int(((int64_t(t1) * kKeysPerTile - 1) >> a.page_shift) - lp0 + 1) : 0;
   const bool staged_pages = n_pages <= kMaxPageSlice;
   for (int i = tid; i < (staged_pages ? n_pages : 0); i += kAttnThreads) {
     const int64_t lp = lp0 + i;
@@ -101,13 +101,14 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
       bool valid = kv < seq_len;
       size_t src = 0;
       if (valid) {
-        const int64_t lp = kv / a.page_size;
+        const int64_t lp = kv >> a.page_shift;
         const int page = staged_pages ? pages[lp - lp0] : (lp < a.max_pages ? a.block_table[lp] : -1);
         if (page < 0 || page >= a.num_pages) {
           record_error(a.err, kErrBadIndex);
           valid = false;
         } else {
-          src = ((size_t(page) * a.num_kv_heads + group) * a.page_size + size_t(kv % a.page_size)) * HD + chunk * 8;
+          src = ((size_t(page) * a.num_kv_heads + group) * a.page_size + size_t(kv & (a.page_size - 1))) * HD +
+                chunk * 8;
         }
       }
       cp_async_16(kbuf(buf) + swz<HD>(row, chunk), kc + src, valid);
@@ -325,28 +326,44 @@ __global__ void __launch_bounds__(kAttnThreads) round_attention_kernel(const Att
     wts[tid * (S + 1) + S] = lsum > 0.f ? 1.f / lsum : 0.f;
   }
   __syncthreads();
-  for (int idx = tid; idx < rpc * (HD / 2); idx += kAttnThreads) {
-    const int lr = idx / (HD / 2), c = (idx % (HD / 2)) * 2;
-    const int row = row_begin + lr;
-    const uint32_t off = uint32_t(row * HD + c) * 4u;
-    float2 part[8];
+  // 16-byte remote loads, two of the thread's row chunks x every rank in flight at a time; rows past a.rows are
+  // skipped
+  constexpr int Q4 = HD / 4;  // float4 per row
+  const int live = max(0, min(rpc, a.rows - (qt * kQRowsPerCta + row_begin)));
+  for (int idx0 = tid; idx0 < live * Q4; idx0 += 2 * kAttnThreads) {
+    float4 part[2][8];
 #pragma unroll
-    for (int sp = 0; sp < 8; ++sp)
-      part[sp] = sp < S ? ld_dsmem_f32x2(cluster_map(po, uint32_t(sp)) + off) : make_float2(0.f, 0.f);
-    float acc0 = 0.f, acc1 = 0.f;
+    for (int u = 0; u < 2; ++u) {
+      const int idx = idx0 + u * kAttnThreads;
+      const int lr = idx / Q4, c = (idx % Q4) * 4;
+      const uint32_t off = uint32_t((row_begin + lr) * HD + c) * 4u;
 #pragma unroll
-    for (int sp = 0; sp < 8; ++sp) {
-      if (sp < S) {
-        const float w = wts[lr * (S + 1) + sp];
-        acc0 += w * part[sp].x;
-        acc1 += w * part[sp].y;
-      }
+      for (int sp = 0; sp < 8; ++sp)
+        part[u][sp] = (sp < S && idx < live * Q4) ? ld_dsmem_f32x4(cluster_map(po, uint32_t(sp)) + off)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const int grow = qt * kQRowsPerCta + row;
-    const float inv = wts[lr * (S + 1) + S];
-    if (grow < a.rows)
-      *reinterpret_cast<__nv_bfloat162*>(out + size_t(grow) * out_stride + head * HD + c) =
-          __floats2bfloat162_rn(acc0 * inv, acc1 * inv);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int idx = idx0 + u * kAttnThreads;
+      if (idx >= live * Q4) continue;
+      const int lr = idx / Q4, c = (idx % Q4) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        if (sp < S) {
+          const float w = wts[lr * (S + 1) + sp];
+          acc.x += w * part[u][sp].x;
+          acc.y += w * part[u][sp].y;
+          acc.z += w * part[u][sp].z;
+          acc.w += w * part[u][sp].w;
+        }
+      }
+      const int grow = qt * kQRowsPerCta + row_begin + lr;
+      const float inv = wts[lr * (S + 1) + S];
+      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + size_t(grow) * out_stride + head * HD + c);
+      dst[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+      dst[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    }
   }
   cluster_sync();
 }
@@ -382,6 +399,9 @@ int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
   if (a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads != 0)
     return fail(PLM_ERR_INVALID, "attention: %d heads over %d kv heads", a.num_heads, a.num_kv_heads);
   if (a.rows < 1 || a.rows > 1024) return fail(PLM_ERR_INVALID, "attention: rows %d", a.rows);
+  if (a.page_size < 1 || a.page_size > 4096 || (a.page_size & (a.page_size - 1)) != 0)
+    return fail(PLM_ERR_UNSUPPORTED, "attention: page size %d (a power of two <= 4096)", a.page_size);
+  a.page_shift = __builtin_ctz(unsigned(a.page_size));
   if (!a.q || !a.k_cache || !a.v_cache || !a.block_table || !a.offset || !a.depth || !a.own_start || !a.out)
     return fail(PLM_ERR_INVALID, "attention: null operand");
   const int q_tiles = (a.rows + kQRowsPerCta - 1) / kQRowsPerCta;

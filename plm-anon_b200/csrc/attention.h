@@ -16,6 +16,7 @@ struct AttnArgs {
   int max_pages;
   int num_pages;
   int page_size;
+  int page_shift;              // log2(page_size): page sizes are powers of two
   const int64_t* offset;       // device scalar: logical KV index of query row 0
   int rows;
   const int32_t* depth;        // [rows] relative to offset
