@@ -41,6 +41,12 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 2^x by the special-function unit (relative error ~2^-22; -inf gives +0): the softmax's exponentials.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -92,28 +98,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
 
   const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
   const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache);
+  // Thread tid always copies 16-byte chunk tid % CH of tile rows tid / CH + u * RSTEP: its page lookups are issued
+  // together, then 32-bit-cheap address arithmetic from per-thread constants; a bad page is recorded once per tile.
+  constexpr int ITER = (kKeysPerTile * CH) / kAttnThreads;
+  constexpr int RSTEP = kAttnThreads / CH;
+  const int my_chunk = tid % CH, my_row0 = tid / CH;
+  const size_t head_off = size_t(group) * a.page_size * HD + size_t(my_chunk) * 8;  // elements
+  const size_t page_stride = size_t(a.num_kv_heads) * a.page_size * HD;            // elements per page
   auto issue = [&](int t, int buf) {  // tile t (absolute) into ring slot buf; one commit group per call
+    const int64_t kv0 = int64_t(t) * kKeysPerTile + my_row0;
+    int pg[ITER];
 #pragma unroll
-    for (int i = 0; i < (kKeysPerTile * CH) / kAttnThreads; ++i) {
-      const int idx = tid + i * kAttnThreads;
-      const int row = idx / CH, chunk = idx % CH;
-      const int64_t kv = int64_t(t) * kKeysPerTile + row;
-      bool valid = kv < seq_len;
-      size_t src = 0;
-      if (valid) {
-        const int64_t lp = kv >> a.page_shift;
-        const int page = staged_pages ? pages[lp - lp0] : (lp < a.max_pages ? a.block_table[lp] : -1);
-        if (page < 0 || page >= a.num_pages) {
-          record_error(a.err, kErrBadIndex);
-          valid = false;
-        } else {
-          src = ((size_t(page) * a.num_kv_heads + group) * a.page_size + size_t(kv & (a.page_size - 1))) * HD +
-                chunk * 8;
-        }
-      }
-      cp_async_16(kbuf(buf) + swz<HD>(row, chunk), kc + src, valid);
-      cp_async_16(vbuf(buf) + swz<HD>(row, chunk), vc + src, valid);
+    for (int u = 0; u < ITER; ++u) {
+      const int64_t kv = kv0 + u * RSTEP;
+      const int64_t lp = kv >> a.page_shift;
+      pg[u] = kv >= seq_len ? -2 : staged_pages ? pages[lp - lp0] : (lp < a.max_pages ? a.block_table[lp] : -1);
     }
+    bool bad = false;
+#pragma unroll
+    for (int u = 0; u < ITER; ++u) {
+      const int row = my_row0 + u * RSTEP;
+      const bool valid = pg[u] >= 0 && pg[u] < a.num_pages;
+      bad |= pg[u] != -2 && !valid;
+      const size_t src =
+          valid ? size_t(pg[u]) * page_stride + head_off + size_t((kv0 + u * RSTEP) & (a.page_size - 1)) * HD : 0;
+      cp_async_16(kbuf(buf) + swz<HD>(row, my_chunk), kc + src, valid);
+      cp_async_16(vbuf(buf) + swz<HD>(row, my_chunk), vc + src, valid);
+    }
+    if (bad) record_error(a.err, kErrBadIndex);
   };
   // Pipeline prologue: kStages - 1 commit groups. Tiles lying wholly in the context go out before the wait.
   int64_t whole = offset / kKeysPerTile - t0;  // tiles of this CTA whose last key lies below offset
@@ -211,17 +223,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float c0 = n0 == -INFINITY ? 1.f : exp2f(m0 - n0);
-    const float c1 = n1 == -INFINITY ? 1.f : exp2f(m1 - n1);
+    const float c0 = n0 == -INFINITY ? 1.f : ex2(m0 - n0);
+    const float c1 = n1 == -INFINITY ? 1.f : ex2(m1 - n1);
     m0 = n0;
     m1 = n1;
     float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-      s[j][0] = n0 == -INFINITY ? 0.f : exp2f(s[j][0] - n0);
-      s[j][1] = n0 == -INFINITY ? 0.f : exp2f(s[j][1] - n0);
-      s[j][2] = n1 == -INFINITY ? 0.f : exp2f(s[j][2] - n1);
-      s[j][3] = n1 == -INFINITY ? 0.f : exp2f(s[j][3] - n1);
+      s[j][0] = n0 == -INFINITY ? 0.f : ex2(s[j][0] - n0);
+      s[j][1] = n0 == -INFINITY ? 0.f : ex2(s[j][1] - n0);
+      s[j][2] = n1 == -INFINITY ? 0.f : ex2(s[j][2] - n1);
+      s[j][3] = n1 == -INFINITY ? 0.f : ex2(s[j][3] - n1);
       ps0 += s[j][0] + s[j][1];
       ps1 += s[j][2] + s[j][3];
     }
