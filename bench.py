@@ -145,7 +145,7 @@ def _dist():
         torch.cuda.set_device(local)
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
         return rank, world, local, dist
     if torch.cuda.is_available():
         torch.cuda.set_device(0)
@@ -326,6 +326,12 @@ def run_reference(args) -> None:
     print(json.dumps(line))
 
 
+# DRAM bytes (read + write) of the weight GEMMs of one round of the benchmark shape, from one ncu capture of each
+# GEMM shape (profiles/skinny_gemm_plm-1.3b_rows56.md): 24 x (qkv 25.47 + o 8.69 + gate_up 68.12 + down 34.64) MB
+# + lm_head 209.7 MB.
+GEMM_DRAM_BYTES_PER_ROUND = 3.495e9
+
+
 def run_native(args) -> None:
     import torch
 
@@ -405,7 +411,8 @@ def run_native(args) -> None:
             "tokens_per_round": total_tokens / (args.steps * world),
             "roofline": {"bound": "hbm", "kernel": "skinny_gemm_kernel (all weight GEMMs of a round)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": peak_kind, "traffic": None, "bytes_per_round": bytes_["weights"],
+                         "peak_source": peak_kind, "traffic": GEMM_DRAM_BYTES_PER_ROUND,
+                         "bytes_per_round": bytes_["weights"],
                          "ms_per_round": gemm_ms, "launches_per_round": gemm_launches},
             "round_roofline": {"bound": "hbm", "achieved": round_achieved, "peak": peak, "unit": "GB/s",
                                "frac": round_achieved / peak, "bytes_per_round": bytes_},

@@ -3,6 +3,7 @@
     python plm-anon_b200/bench/kernels.py gemm --n-out 16384 --k 2048 --rows 56 --epi silu
     python plm-anon_b200/bench/kernels.py attention --ctx 1024 --k 7 --heads 16 --head-dim 128 --page 16
     python plm-anon_b200/bench/kernels.py verify --vocab 50257 --aux 1024 --rows 7
+    python plm-anon_b200/bench/kernels.py norm --rows 56 --hidden 2048
 
 Prints one JSON line per run: microseconds per launch and the algorithmic bytes per launch over that time. With
 ``--iters 1 --no-graph`` it issues exactly one launch after ``--warmup`` launches, the shape a profiler capture of one
@@ -112,6 +113,26 @@ def bench_attention(args, ctx):
             "page": page, "us": us, "GB/s": nbytes / us / 1e3, "bytes": nbytes}
 
 
+def bench_norm(args, ctx):
+    import torch
+
+    from plm import native
+
+    x = torch.randn(args.rows, args.hidden, device="cuda").bfloat16()
+    res = torch.randn(args.rows, args.hidden, device="cuda").bfloat16()
+    w = torch.ones(args.hidden, device="cuda").bfloat16()
+    normed = torch.empty_like(x)
+    desc = native.AddRmsNormDesc(dtype=native.PLM_BF16, x=x.data_ptr(), residual=res.data_ptr(),
+                                 normed=normed.data_ptr(), weight=w.data_ptr(), rows=args.rows, hidden=args.hidden,
+                                 eps=1e-5, gather_row=-1, gathered=None)
+    fn = lambda: native.add_rmsnorm(ctx, desc)  # noqa: E731
+    us = _time(fn, args.iters, args.warmup, not args.no_graph, args.flush)
+    ctx.check()
+    nbytes = args.rows * args.hidden * 2 * 4 + args.hidden * 2  # read x, residual; write residual, normed; weight
+    return {"kernel": "add_norm_kernel", "rows": args.rows, "hidden": args.hidden, "us": us, "GB/s": nbytes / us / 1e3,
+            "bytes": nbytes}
+
+
 def bench_verify(args, ctx):
     import torch
 
@@ -143,7 +164,7 @@ def bench_verify(args, ctx):
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     sub = parser.add_subparsers(dest="kernel", required=True)
-    for name in ("gemm", "attention", "verify"):
+    for name in ("gemm", "attention", "verify", "norm"):
         p = sub.add_parser(name)
         p.add_argument("--iters", type=int, default=20)
         p.add_argument("--warmup", type=int, default=3)
@@ -161,6 +182,9 @@ def main() -> None:
             p.add_argument("--heads", type=int, default=16)
             p.add_argument("--head-dim", type=int, default=128)
             p.add_argument("--page", type=int, default=16)
+        elif name == "norm":
+            p.add_argument("--rows", type=int, default=56)
+            p.add_argument("--hidden", type=int, default=2048)
         else:
             p.add_argument("--vocab", type=int, default=50257)
             p.add_argument("--aux", type=int, default=1024)
@@ -169,7 +193,7 @@ def main() -> None:
     from plm import native
 
     ctx = native.Context()
-    fn = {"gemm": bench_gemm, "attention": bench_attention, "verify": bench_verify}[args.kernel]
+    fn = {"gemm": bench_gemm, "attention": bench_attention, "verify": bench_verify, "norm": bench_norm}[args.kernel]
     print(json.dumps(fn(args, ctx)))
 
 
