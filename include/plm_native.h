@@ -8,7 +8,7 @@
  *   - Launch functions only enqueue work on `stream`; they never synchronise, so they can be captured into a
  *     CUDA graph. Device-side faults are not raised: a kernel that meets an index out of range or a wait that
  *     runs out of time records a code in the context's device error word (plm_ctx_check reads it).
- *   - A context (plm_ctx) owns the device error word and the split-reduction scratch. It is bound to the device
+ *   - A context (plm_ctx) owns the device error word and the kernels' arrival counters. It is bound to the device
  *     current at creation and must only be used from one host thread at a time.
  *
  * Reference interfaces replaced (paths inside justuswill/PLM-anon):
@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 1
+#define PLM_ABI_VERSION 2
 
 enum plm_status {
   PLM_OK = 0,
@@ -56,7 +56,9 @@ enum plm_epilogue {
   PLM_EPI_SILU_MUL = 1, /* out[r][j] = silu(Y[r][j]) * Y[r][gate_offset + j], j < gate_offset */
   PLM_EPI_QKV_ROPE = 2, /* neox RoPE on q,k; q -> q_out, k,v -> paged cache at slots[r] */
   PLM_EPI_LOGITS = 3,   /* rows < n_verify: fp32 logits; other rows: per-tile (max, first index) */
-  PLM_EPI_TABLE = 4     /* table[n][a0 + r] = -Y[r][n] (the Voronoi cost table) */
+  PLM_EPI_TABLE = 4,    /* table[n][a0 + r] = -Y[r][n] (the Voronoi cost table) */
+  PLM_EPI_PARTIAL = 5   /* fp32 k-split partials: ((float*)out)[(s * rows + r) * ldo + n] for split s < splits
+                           (splits must be given, <= 16); the consumer sums them in split order */
 };
 
 enum plm_accept_rule { PLM_RULE_NUCLEUS = 0, PLM_RULE_FLOOR = 1 };
@@ -104,7 +106,7 @@ typedef struct plm_gemm_desc {
   const void* x;  /* [x_rows][k] row-major activations, 16-byte aligned */
   int32_t x_rows; /* allocated rows of x (>= rows) */
   int32_t rows;   /* rows to compute, 1..256 */
-  void* out;      /* PLM_EPI_STORE / PLM_EPI_SILU_MUL output */
+  void* out;      /* PLM_EPI_STORE / PLM_EPI_SILU_MUL / PLM_EPI_PARTIAL output */
   int32_t ldo;    /* output row stride in elements */
   int32_t splits; /* 0 = choose automatically */
   plm_gemm_epilogue epi;
@@ -205,6 +207,11 @@ typedef struct plm_add_rmsnorm_desc {
   float eps;
   int32_t gather_row; /* -1: none; else also copy that normed row to `gathered` */
   void* gathered;
+  /* With partials != NULL, x is ignored and x[r] = bf16(sum over s < n_partials of partials[s * partial_stride +
+   * r * hidden + i]) summed in split order (the PLM_EPI_PARTIAL output of the GEMM before this norm). */
+  const float* partials;
+  int32_t n_partials;
+  int64_t partial_stride;
 } plm_add_rmsnorm_desc;
 
 /* ---- round engine (one handle = one request stream on one GPU, batch 1) ---- */

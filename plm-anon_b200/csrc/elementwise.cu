@@ -10,6 +10,7 @@ namespace {
 constexpr int kRowThreads = 256;
 constexpr int kVec = 8;      // 16-byte vectors of bf16
 constexpr int kMaxVecs = 2;  // vectors per thread: hidden <= kRowThreads * kVec * kMaxVecs = 4096
+constexpr int kMaxNormPartials = 16;  // k-split partials an add_norm may sum
 
 // The row's 16-byte vectors owned by this thread: vector j is elements [8 (tid + j 256), ... + 8).
 template <typename T>
@@ -154,9 +155,48 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs
   const T* __restrict__ w = reinterpret_cast<const T*>(a.weight);
   T* gathered = (r == a.gather_row && a.gathered != nullptr) ? reinterpret_cast<T*>(a.gathered) : nullptr;
   uint4 xv[kMaxVecs], rv[kMaxVecs], wv[kMaxVecs];  // every load of the row is issued before any store
-  load_row<T>(x, a.hidden, xv);
   load_row<T>(res, a.hidden, rv);
   load_row<T>(w, a.hidden, wv);
+  if (a.partials != nullptr) {
+    // The projection's k-split partials, summed in split order from 0 and rounded to the model dtype: the values the
+    // GEMM's own reduction and store would have produced.
+    // Per 8-element chunk, the loads of every split are issued before the in-order sum (one round trip).
+    const float* __restrict__ pp = a.partials + size_t(r) * a.hidden;
+#pragma unroll
+    for (int j = 0; j < kMaxVecs; ++j) {
+      const int c = tid + j * kRowThreads;
+      xv[j] = make_uint4(0, 0, 0, 0);
+      if (c * kVec >= a.hidden) continue;
+      float4 lo[kMaxNormPartials], hi[kMaxNormPartials];
+#pragma unroll
+      for (int sp = 0; sp < kMaxNormPartials; ++sp) {
+        if (sp < a.n_partials) {
+          const float4* ps = reinterpret_cast<const float4*>(pp + size_t(sp) * a.partial_stride);
+          lo[sp] = ps[2 * c];
+          hi[sp] = ps[2 * c + 1];
+        }
+      }
+      float acc[kVec] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int sp = 0; sp < kMaxNormPartials; ++sp) {
+        if (sp < a.n_partials) {
+          acc[0] += lo[sp].x;
+          acc[1] += lo[sp].y;
+          acc[2] += lo[sp].z;
+          acc[3] += lo[sp].w;
+          acc[4] += hi[sp].x;
+          acc[5] += hi[sp].y;
+          acc[6] += hi[sp].z;
+          acc[7] += hi[sp].w;
+        }
+      }
+      T* xo = reinterpret_cast<T*>(&xv[j]);
+#pragma unroll
+      for (int q = 0; q < kVec; ++q) xo[q] = from_f32<T>(acc[q]);
+    }
+  } else {
+    load_row<T>(x, a.hidden, xv);
+  }
   float v[kMaxVecs][kVec];
   float ss = 0.f;
 #pragma unroll
@@ -261,8 +301,15 @@ extern "C" int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* d, void* st
 extern "C" int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* d, void* stream) {
   if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null argument");
   if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_add_rmsnorm: only bf16 is built");
-  if (!d->x || !d->residual || !d->normed || !d->weight || d->rows < 1 || d->hidden < 1)
+  if (!d->residual || !d->normed || !d->weight || d->rows < 1 || d->hidden < 1)
     return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null operand");
-  AddNormArgs a = {d->x, d->residual, d->normed, d->weight, d->hidden, d->eps, d->gather_row, d->gathered};
+  if (d->partials == nullptr && d->x == nullptr) return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null operand");
+  if (d->partials != nullptr &&
+      (d->n_partials < 1 || d->n_partials > kMaxNormPartials || d->partial_stride < int64_t(d->rows) * d->hidden))
+    return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: %d partials with stride %lld", d->n_partials,
+                (long long)d->partial_stride);
+  AddNormArgs a = {d->x,      d->residual,   d->normed,       d->weight,       d->hidden,
+                   d->eps,    d->gather_row, d->gathered,     d->partials,     d->n_partials,
+                   d->partial_stride};
   return add_norm_launch(a, d->rows, static_cast<cudaStream_t>(stream), true);
 }

@@ -45,6 +45,9 @@ struct AddNormArgs {
   float eps;
   int gather_row;  // -1: none
   void* gathered;
+  const float* partials = nullptr;  // non-null: x = bf16(sum of n_partials fp32 slices, split order)
+  int n_partials = 0;
+  int64_t partial_stride = 0;       // floats between slices
 };
 
 struct KvAppendArgs {

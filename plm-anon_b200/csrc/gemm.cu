@@ -70,14 +70,18 @@ int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, c
   const int total_kb = d.k / kGemmBK;
   const int per_sm = ctx->smem_per_sm > 0 ? ctx->smem_per_sm / (SMEM + 1024) : 1;
   int splits = d.splits > 0 ? d.splits : gemm_cluster_splits(tiles, total_kb, ctx->num_sms * (per_sm > 0 ? per_sm : 1));
-  if (splits > 8 || splits > total_kb)
-    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits (at most 8 and at most k/64)", splits);
-  if (NTOK > 128) splits = 1;  // the staging area holds no reduced slice for the widest tiles
+  if (EPI == kEpiPartial) {  // splits written out, not reduced: no cluster, up to kMaxPartialSplits
+    if (splits < 1 || splits > kMaxPartialSplits || splits > total_kb)
+      return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d partial splits (1..%d, at most k/64)", splits, kMaxPartialSplits);
+  } else {
+    if (splits > 8 || splits > total_kb)
+      return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits (at most 8 and at most k/64)", splits);
+    if (NTOK > 128) splits = 1;  // the staging area holds no reduced slice for the widest tiles
+  }
   const int kb_per = (total_kb + splits - 1) / splits;
-  if (kb_per * (splits - 1) >= total_kb)
-    return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d splits leave an empty split of %d k-blocks", splits, total_kb);
   GemmArgs args = make_args(ctx, d, tiles, splits, kb_per);
-  return check_cuda(launch_ex(kernel, dim3(tiles, splits), dim3(kGemmThreads), SMEM, stream, pdl, splits, *map_w,
+  return check_cuda(launch_ex(kernel, dim3(tiles, splits), dim3(kGemmThreads), SMEM, stream, pdl,
+                              EPI == kEpiPartial ? 1 : splits, *map_w,
                               *map_x, args),
                     "skinny_gemm_kernel launch");
 }
@@ -91,6 +95,7 @@ int launch_epi(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* mw, cons
     case PLM_EPI_QKV_ROPE: return launch_one<T, NTOK, kEpiQkvRope>(ctx, d, mw, mx, s, pdl);
     case PLM_EPI_LOGITS: return launch_one<T, NTOK, kEpiLogits>(ctx, d, mw, mx, s, pdl);
     case PLM_EPI_TABLE: return launch_one<T, NTOK, kEpiTable>(ctx, d, mw, mx, s, pdl);
+    case PLM_EPI_PARTIAL: return launch_one<T, NTOK, kEpiPartial>(ctx, d, mw, mx, s, pdl);
   }
   return fail(PLM_ERR_INVALID, "plm_gemm: unknown epilogue %d", d.epi.kind);
 }
@@ -123,6 +128,10 @@ int validate(const plm_gemm_desc& d) {
   switch (e.kind) {
     case PLM_EPI_STORE:
       if (d.out == nullptr || d.ldo < d.n_out) return fail(PLM_ERR_INVALID, "plm_gemm: store needs out, ldo >= n_out");
+      break;
+    case PLM_EPI_PARTIAL:
+      if (d.out == nullptr || d.ldo < d.n_out) return fail(PLM_ERR_INVALID, "plm_gemm: partial needs out, ldo >= n_out");
+      if (d.splits < 1) return fail(PLM_ERR_INVALID, "plm_gemm: partial needs an explicit split count");
       break;
     case PLM_EPI_SILU_MUL:
       if (e.gate_offset <= 0 || e.gate_offset % 64 != 0 || d.n_out != 2 * e.gate_offset)
@@ -163,6 +172,42 @@ int gemm_row_map(CUtensorMap* map, const plm_gemm_desc& d) {
   const int ntok = gemm_token_tile(d.rows);
   if (ntok < 0) return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d rows", d.rows);
   return encode_map_2d(map, d.x, d.dtype, uint64_t(d.k), uint64_t(d.x_rows), uint64_t(d.k) * 2, 64, uint32_t(ntok));
+}
+
+template <int NTOK>
+int partial_splits_for(plm_ctx* ctx, int n_out, int k) {
+  constexpr int SMEM = gemm_smem_bytes<NTOK, stages_for<NTOK, kEpiPartial>()>();
+  const int per_sm = ctx->smem_per_sm > 0 ? ctx->smem_per_sm / (SMEM + 1024) : 1;
+  const int slots = ctx->num_sms * (per_sm > 0 ? per_sm : 1);
+  const int tiles = (n_out + 127) / 128, total_kb = k / kGemmBK;
+  // waves x (k-blocks per split + a fixed cost of 3) plus a quarter k-block per split for the consumer's extra reads
+  int best = 1;
+  double best_cost = -1;
+  for (int s = 1; s <= kMaxPartialSplits && s <= total_kb; ++s) {
+    const int per = (total_kb + s - 1) / s;
+    const double waves = double((tiles * s + slots - 1) / slots);
+    const double cost = waves * (per + 3) + 0.25 * s;
+    if (best_cost < 0 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+int gemm_partial_splits(plm_ctx* ctx, int n_out, int k, int rows) {
+  switch (gemm_token_tile(rows)) {
+    case 16: return partial_splits_for<16>(ctx, n_out, k);
+    case 32: return partial_splits_for<32>(ctx, n_out, k);
+    case 48: return partial_splits_for<48>(ctx, n_out, k);
+    case 64: return partial_splits_for<64>(ctx, n_out, k);
+    case 80: return partial_splits_for<80>(ctx, n_out, k);
+    case 96: return partial_splits_for<96>(ctx, n_out, k);
+    case 112: return partial_splits_for<112>(ctx, n_out, k);
+    case 128: return partial_splits_for<128>(ctx, n_out, k);
+    case 256: return partial_splits_for<256>(ctx, n_out, k);
+  }
+  return 1;
 }
 
 int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,

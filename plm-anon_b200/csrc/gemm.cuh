@@ -16,7 +16,9 @@
 //   kEpiSiluMul  the gate_up projection with SiLU(gate) * up fused (tile = 64 gate rows + the matching 64 up rows);
 //   kEpiQkvRope  the qkv projection with neox RoPE on q and k, q written out, k and v scattered into the paged cache;
 //   kEpiLogits   the lm_head: verify rows as fp32 logits, proposal rows reduced to a per-tile (max, first index);
-//   kEpiTable    the Voronoi cost table, table[v][a] = -(aux_vocab[a] . lm_head[v]).
+//   kEpiTable    the Voronoi cost table, table[v][a] = -(aux_vocab[a] . lm_head[v]);
+//   kEpiPartial  each k-split's fp32 partial straight to global memory, no cluster reduction (the next kernel sums
+//                the splits in order).
 // Weight loads are issued before griddepcontrol.wait, so under programmatic dependent launch they overlap the
 // tail of the previous kernel; everything that reads activations comes after it.
 #pragma once
@@ -27,12 +29,15 @@
 
 namespace plm {
 
+constexpr int kMaxPartialSplits = 16;  // k-splits a kEpiPartial launch may write out
+
 enum GemmEpilogueKind : int {
   kEpiStore = 0,
   kEpiSiluMul = 1,
   kEpiQkvRope = 2,
   kEpiLogits = 3,
   kEpiTable = 4,
+  kEpiPartial = 5,
 };
 
 struct QkvEpilogue {
@@ -123,8 +128,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
   const int total_kb = args.k / kGemmBK;
-  const int kb_begin = split * args.kb_per_split;
-  const int kb_end = (split == args.splits - 1) ? total_kb : kb_begin + args.kb_per_split;
+  const int kb_begin = split * total_kb / args.splits;  // k-blocks spread evenly: no split is empty
+  const int kb_end = (split + 1) * total_kb / args.splits;
   const int nk = kb_end - kb_begin;
 
   if (tid == 0) {
@@ -240,12 +245,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int row = warp * 32 + lane;  // feature lane inside the 128-wide tile
   const uint32_t t_warp = tmem + (uint32_t(warp * 32) << 16);
   const int rows = args.rows;
+  float* partial = EPI == kEpiPartial ? reinterpret_cast<float*>(args.out) + size_t(split) * rows * args.ldo : nullptr;
+  const int part_feats = min(128, args.n_out - tile * 128);
   for (int c0 = 0; c0 < rows; c0 += 32) {
     float v[32];
     tmem_ld_32cols(t_warp + c0, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (c0 + j < rows) stage[(c0 + j) * kStagePad + row] = v[j];
+    for (int j = 0; j < 32; ++j) {
+      if (c0 + j >= rows) continue;
+      if (EPI == kEpiPartial) {  // a warp's 32 lanes write 32 consecutive features of one row
+        if (row < part_feats) partial[size_t(c0 + j) * args.ldo + tile * 128 + row] = v[j];
+      } else {
+        stage[(c0 + j) * kStagePad + row] = v[j];
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -259,6 +272,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_dealloc(tmem, Shape::TMEM_COLS);
   }
   const bool ok = mma_ok && flags[0] == 0;
+  if (EPI == kEpiPartial) return;  // launched without a cluster: nothing left to reduce here
 
   // ---------------- split reduction over the cluster ----------------
   // The `splits` CTAs of a tile form one cluster. After the barrier, rank r sums the partial tiles of all ranks,

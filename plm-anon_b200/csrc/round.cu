@@ -24,6 +24,8 @@ namespace {
 constexpr int kUnreachable = 1 << 30;  // plm/mask.py:14
 constexpr int kMaxPrefillRows = 256;
 
+constexpr int kPartialSlices = 16;  // the most k-splits gemm_partial_splits chooses
+
 template <typename Tp>
 int dev_alloc(Tp** p, size_t count, const char* what) {
   return check_cuda(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(Tp)), what);
@@ -52,6 +54,7 @@ struct plm_handle {
        *gathered = nullptr;
   int32_t* positions = nullptr;
   int64_t* slots = nullptr;
+  float* partials = nullptr;  // [kPartialSlices][R][hidden] fp32 k-split partials of the o and down projections
   float* verify_logits = nullptr;
   float* best_val = nullptr;
   int32_t* best_idx = nullptr;
@@ -103,7 +106,7 @@ int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMa
 }
 
 int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, const void* x, int rows,
-         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s) {
+         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s, int splits = 0) {
   plm_gemm_desc d = {};
   d.dtype = h->m.dtype;
   d.w = w;
@@ -114,6 +117,7 @@ int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, 
   d.rows = rows;
   d.out = out;
   d.ldo = ldo;
+  d.splits = splits;
   d.epi = epi;
   const CUtensorMap* mx = nullptr;
   int st = row_map(h, x, k, rows, &mx);
@@ -203,11 +207,15 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     st = attention_launch(h->ctx, a, s, true);
     if (st != PLM_OK) return st;
 
-    plm_gemm_epilogue store = {};
-    store.kind = PLM_EPI_STORE;
-    st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, store, h->y, hidden, s);
+    // o and down write their k-split partials; the residual-add RMSNorm that follows sums them in split order
+    plm_gemm_epilogue part = {};
+    part.kind = PLM_EPI_PARTIAL;
+    const int64_t slice = int64_t(rows) * hidden;
+    const int s_o = gemm_partial_splits(h->ctx, hidden, q_size, rows);
+    st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, part, h->partials, hidden, s, s_o);
     if (st != PLM_OK) return st;
-    AddNormArgs n1 = {h->y, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr};
+    AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
+                      h->partials, s_o, slice};
     st = add_norm_launch(n1, rows, s, true);
     if (st != PLM_OK) return st;
 
@@ -217,11 +225,14 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     st = gemm(h, h->gate_up[l], &h->map_gate_up[l], 2 * m.intermediate, hidden, h->x_norm, rows, silu, h->act,
               m.intermediate, s);
     if (st != PLM_OK) return st;
-    st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, store, h->y, hidden, s);
+    const int s_d = gemm_partial_splits(h->ctx, hidden, m.intermediate, rows);
+    st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, part, h->partials, hidden, s,
+              s_d);
     if (st != PLM_OK) return st;
     const bool last = l + 1 == m.num_layers;
-    AddNormArgs n2 = {h->y, h->residual, h->x_norm, last ? h->final_norm : h->in_norm[l + 1], hidden, m.rms_eps,
-                      last ? gather_row : -1, last ? h->gathered : nullptr};
+    AddNormArgs n2 = {nullptr,  h->residual,           h->x_norm, last ? h->final_norm : h->in_norm[l + 1],
+                      hidden,   m.rms_eps,             last ? gather_row : -1, last ? h->gathered : nullptr,
+                      h->partials, s_d, slice};
     st = add_norm_launch(n2, rows, s, true);
     if (st != PLM_OK) return st;
   }
@@ -349,7 +360,8 @@ extern "C" {
 
 int plm_destroy(plm_handle* h) {
   if (h == nullptr) return PLM_OK;
-  void* bufs[] = {h->x_norm, h->residual, h->y, h->q, h->attn, h->act, h->gathered, h->positions, h->slots,
+  void* bufs[] = {h->x_norm, h->residual, h->y, h->q, h->attn, h->act, h->gathered, h->partials, h->positions,
+                  h->slots,
                   h->verify_logits, h->best_val, h->best_idx, h->verify, h->flags, h->st_relpos, h->st_relaux,
                   h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
@@ -431,6 +443,7 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->attn), R * q_size, "attn");
   if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->act), R * I, "act");
   if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->gathered), size_t(16) * hidden, "gathered");
+  if (st == PLM_OK) st = dev_alloc(&h->partials, size_t(kPartialSlices) * R * hidden, "projection partials");
   if (st == PLM_OK) st = dev_alloc(&h->positions, R, "positions");
   if (st == PLM_OK) st = dev_alloc(&h->slots, R, "slots");
   h->lm_tiles = (m->vocab + 127) / 128;

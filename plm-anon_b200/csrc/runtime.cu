@@ -74,8 +74,7 @@ int gemm_cluster_splits(int tiles, int total_kb, int slots) {
   int best = 1;
   long best_cost = -1;
   for (int s = 1; s <= 8 && s <= total_kb; ++s) {
-    const int per = (total_kb + s - 1) / s;
-    if (per * (s - 1) >= total_kb) continue;  // every split needs at least one k-block
+    const int per = (total_kb + s - 1) / s;  // the largest split (k-blocks are spread evenly)
     const long waves = (long(tiles) * s + slots - 1) / slots;
     const long cost = waves * (per + kGemmOverheadKb);
     if (best_cost < 0 || cost < best_cost) {

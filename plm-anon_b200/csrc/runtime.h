@@ -85,5 +85,7 @@ int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, 
 int gemm_weight_map(CUtensorMap* map, const plm_gemm_desc& d);
 int gemm_row_map(CUtensorMap* map, const plm_gemm_desc& d);
 int gemm_token_tile(int rows);
+// Split count for a PLM_EPI_PARTIAL launch of this shape (1..16): fills the resident CTA slots in one wave.
+int gemm_partial_splits(plm_ctx* ctx, int n_out, int k, int rows);
 
 }  // namespace plm

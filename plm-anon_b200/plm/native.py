@@ -17,7 +17,7 @@ STATUS_NAMES = {-1: "PLM_ERR_INVALID", -2: "PLM_ERR_CUDA", -3: "PLM_ERR_DEVICE",
                 -5: "PLM_ERR_NOMEM"}
 
 PLM_BF16, PLM_F16 = 0, 1
-EPI_STORE, EPI_SILU_MUL, EPI_QKV_ROPE, EPI_LOGITS, EPI_TABLE = range(5)
+EPI_STORE, EPI_SILU_MUL, EPI_QKV_ROPE, EPI_LOGITS, EPI_TABLE, EPI_PARTIAL = range(6)
 
 DEVICE_ERRORS = {1: "TMA stage wait timed out", 2: "free stage wait timed out", 3: "MMA completion wait timed out",
                  4: "index out of range", 5: "split reduction arrival count inconsistent", 6: "unsupported shape",
@@ -86,7 +86,8 @@ class KvAppendDesc(ctypes.Structure):
 class AddRmsNormDesc(ctypes.Structure):
     _fields_ = [("dtype", c_int32), ("x", c_void_p), ("residual", c_void_p), ("normed", c_void_p),
                 ("weight", c_void_p), ("rows", c_int32), ("hidden", c_int32), ("eps", ctypes.c_float),
-                ("gather_row", c_int32), ("gathered", c_void_p)]
+                ("gather_row", c_int32), ("gathered", c_void_p), ("partials", c_void_p), ("n_partials", c_int32),
+                ("partial_stride", ctypes.c_int64)]
 
 
 class ModelDesc(ctypes.Structure):

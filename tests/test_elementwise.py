@@ -50,3 +50,32 @@ def test_add_rmsnorm_rejects_unsupported_width(ctx):
                                  weight=x.data_ptr(), rows=2, hidden=100, eps=1e-5, gather_row=-1, gathered=None)
     with pytest.raises(native.NativeError):
         native.add_rmsnorm(ctx, desc)
+
+
+@pytest.mark.parametrize("rows,hidden,splits", [(56, 2048, 16), (7, 512, 3), (3, 2560, 1)])
+def test_add_rmsnorm_from_partials(ctx, rows, hidden, splits):
+    """x given as fp32 k-split partials: summed in split order and rounded to bf16 first, then the same fused
+    residual-add RMSNorm; equal bit for bit to the run with that bf16 x."""
+    from plm import native
+
+    g = torch.Generator(device="cuda").manual_seed(splits * hidden)
+    part = torch.randn(splits, rows, hidden, generator=g, device="cuda")
+    x = torch.zeros(rows, hidden, device="cuda")
+    for s in range(splits):
+        x = x + part[s]
+    x = x.bfloat16()
+    res = (2 * torch.randn(rows, hidden, generator=g, device="cuda")).bfloat16()
+    w = (1 + 0.1 * torch.randn(hidden, generator=g, device="cuda")).bfloat16()
+    outs = []
+    for use_partials in (False, True):
+        res_io, normed = res.clone(), torch.empty_like(x)
+        desc = native.AddRmsNormDesc(dtype=native.PLM_BF16, x=None if use_partials else x.data_ptr(),
+                                     residual=res_io.data_ptr(), normed=normed.data_ptr(), weight=w.data_ptr(),
+                                     rows=rows, hidden=hidden, eps=1e-5, gather_row=-1, gathered=None,
+                                     partials=part.data_ptr() if use_partials else None,
+                                     n_partials=splits if use_partials else 0,
+                                     partial_stride=rows * hidden if use_partials else 0)
+        native.add_rmsnorm(ctx, desc)
+        ctx.check()
+        outs.append((res_io, normed))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])

@@ -55,6 +55,41 @@ def test_forced_splits_and_determinism(ctx, splits):
     assert torch.equal(outs[0], outs[1]), "same split count must give bit-identical results"
 
 
+@pytest.mark.parametrize("n_out,k,rows,splits", [(2048, 2048, 56, 1), (2048, 2048, 56, 3), (2048, 8192, 56, 16),
+                                                  (1000, 1024, 42, 9), (640, 1024, 200, 4)])
+def test_partial_epilogue(ctx, n_out, k, rows, splits):
+    """PLM_EPI_PARTIAL writes each k-split's fp32 partial; summed in split order and rounded they equal the store
+    epilogue at the same split count bit for bit (the cluster reduction adds the ranks in the same order)."""
+    from plm import native
+
+    w = _rand(n_out, k, scale=0.02, seed=11)
+    x = _rand(rows, k, seed=12)
+    part = torch.full((splits * rows, n_out), float("nan"), dtype=torch.float32, device="cuda")
+    native.gemm(ctx, w, x, rows, out=part, epi=native.GemmEpilogue(kind=native.EPI_PARTIAL), splits=splits)
+    ctx.check()
+    slices = part.view(splits, rows, n_out)
+    total = torch.zeros(rows, n_out, dtype=torch.float32, device="cuda")
+    for s in range(splits):
+        total = total + slices[s]
+    _close(total, x.float() @ w.float().T)
+    if splits <= 8 and rows <= 128:
+        store = torch.zeros(rows, n_out, dtype=torch.bfloat16, device="cuda")
+        native.gemm(ctx, w, x, rows, out=store, splits=splits)
+        ctx.check()
+        assert torch.equal(total.bfloat16(), store)
+
+
+def test_partial_epilogue_needs_explicit_splits(ctx):
+    from plm import native
+
+    w, x = _rand(256, 256, seed=1), _rand(8, 256, seed=2)
+    part = torch.zeros(64, 256, dtype=torch.float32, device="cuda")
+    with pytest.raises(native.NativeError):
+        native.gemm(ctx, w, x, 8, out=part, epi=native.GemmEpilogue(kind=native.EPI_PARTIAL))
+    with pytest.raises(native.NativeError):
+        native.gemm(ctx, w, x, 8, out=part, epi=native.GemmEpilogue(kind=native.EPI_PARTIAL), splits=17)
+
+
 def test_padded_row_buffer(ctx):
     """Rows beyond `rows` in the operand buffer must not leak into the result (they are read by TMA, not stored)."""
     from plm import native
