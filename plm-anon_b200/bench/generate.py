@@ -8,8 +8,10 @@ One process runs the whole dataset ``1 + len(--seeds)`` times: a discarded warm-
 a cold clock, then one pass per seed. The seed drives the request's auxiliary cell stream. ``--model`` is an export
 directory (config.json + safetensors with the auxiliary scheme) or ``synthetic:<shape>[:seed=<n>]``.
 
-Only the parallel-round path is built here: the autoregressive baselines (``--ar``) and the EAGLE-3 / Fast-dLLM v2
-comparators (``--eagle3``, ``--fdv2``) run stock vLLM or third-party packages in the reference and exit with a message.
+``--ar --ar-sampler voronoi`` is the AR-Voronoi comparator (plm/voronoi_ar.py, bench/ar.py): one verify row per step,
+which is a round with k = 1 on the same engine, and decodes the same tokens as ``--match exact``. The other AR
+samplers and the EAGLE-3 / Fast-dLLM v2 comparators (``--eagle3``, ``--fdv2``) run stock vLLM or third-party packages
+in the reference and exit with a message.
 """
 
 from __future__ import annotations
@@ -36,7 +38,10 @@ def add_arguments(parser: argparse.ArgumentParser) -> None:
                         help="exact, or relaxed (the setting's looser accept rule)")
     parser.add_argument("--k", type=int, help="proposal length per round; default from --setting")
     parser.add_argument("--block-size", type=int, default=KV_BLOCK_SIZE, help="KV page size in tokens")
-    parser.add_argument("--ar", action="store_true", help="autoregressive decoding (not built on this engine)")
+    parser.add_argument("--ar", action="store_true", help="autoregressive decoding: one Voronoi-decoded row per step")
+    parser.add_argument("--ar-sampler", default="voronoi", choices=("voronoi", "icdf", "topk", "greedy"),
+                        help="voronoi: the PLM's own decode rule on the seeded cells, token-identical to --match exact "
+                             "(the only sampler built on this engine)")
     parser.add_argument("--eagle3", default="", help="EAGLE-3 head (not built on this engine)")
     parser.add_argument("--fdv2", action="store_true", help="Fast-dLLM v2 (not built on this engine)")
 
@@ -55,18 +60,29 @@ def run_plm(decoder, prompt, tokens: int, stop_at_eos: bool, seed: int) -> dict:
     return record
 
 
+def round_config(args: argparse.Namespace) -> RoundConfig:
+    """The RoundConfig the flags select (bench/generate.py:67-71). AR-Voronoi is exact matching with k = 1."""
+    if args.ar:
+        return RoundConfig(model=args.model, setting=args.setting, mode=args.mode, match="exact", k=1,
+                           max_model_len=args.max_model_len)
+    return RoundConfig(model=args.model, setting=args.setting, mode=args.mode, match=args.match, k=args.k,
+                       max_model_len=args.max_model_len)
+
+
 def plm_generator(args: argparse.Namespace) -> tuple[dict, Callable]:
-    """bench/generate.py:67-71."""
-    round_config = RoundConfig(model=args.model, setting=args.setting, mode=args.mode, match=args.match, k=args.k,
-                               max_model_len=args.max_model_len)
-    decoder = round_config.build(kv_cache_bytes=KV_CACHE_BYTES, block_size=args.block_size)
-    described = {"decoding": round_config.match, **round_config.describe()}
+    """bench/generate.py:67-71 (and the AR-Voronoi comparator of 55-64 as a k = 1 round)."""
+    round_config_ = round_config(args)
+    decoder = round_config_.build(kv_cache_bytes=KV_CACHE_BYTES, block_size=args.block_size)
+    decoding = "ar-voronoi" if args.ar else round_config_.match
+    described = {"decoding": decoding, **round_config_.describe()}
     return described, lambda prompt, seed: run_plm(decoder, prompt, args.tokens, args.stop_at_eos, seed)
 
 
 def build_generator(args: argparse.Namespace) -> tuple[dict, Callable]:
-    if args.ar or args.eagle3 or args.fdv2:
-        raise SystemExit("--ar, --eagle3 and --fdv2 are not built on this engine: it runs PLM parallel rounds only")
+    if args.eagle3 or args.fdv2:
+        raise SystemExit("--eagle3 and --fdv2 are not built on this engine: it runs PLM parallel rounds")
+    if args.ar and args.ar_sampler != "voronoi":
+        raise SystemExit(f"--ar-sampler {args.ar_sampler} is not built on this engine (voronoi is: a k = 1 round)")
     return plm_generator(args)
 
 

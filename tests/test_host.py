@@ -140,5 +140,11 @@ def test_generate_cli_surface(tmp_path):
     assert abs(agg["tokens_per_second"] - 1000 * 15 / 60.0) < 1e-9
     assert abs(agg["e2e_tokens_per_second"] - 1000 * 15 / 150.0) < 1e-9
     args.ar = True
+    rc = generate.round_config(args)  # AR-Voronoi: exact matching, one verify row per step
+    assert (rc.k, rc.match, rc.width) == (1, "exact", 2)
+    args.ar_sampler = "topk"
+    with pytest.raises(SystemExit):
+        generate.build_generator(args)
+    args.ar, args.fdv2 = False, True
     with pytest.raises(SystemExit):
         generate.build_generator(args)

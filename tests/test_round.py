@@ -93,6 +93,7 @@ def _close(name, gpu, ref, report, rel=0.0, floor=0.0):
     ("plm-tiny", 4, 16, "nucleus", 0.94, {"num_kv_heads": 1, "head_dim": 128, "aux_vocab": 512}),
     ("plm-80m", 6, 16, "nucleus", None, {"num_layers": 2}),
     ("plm-1.3b", 7, 16, "nucleus", None, {}),
+    ("plm-tiny", 1, 16, "nucleus", None, {}),  # k = 1: the AR-Voronoi comparator (plm/voronoi_ar.py)
 ])
 def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides):
     decoder, oracle, cfg = _pair(shape, k, page, seed=3, rule=rule, threshold=threshold, **overrides)
@@ -191,6 +192,30 @@ def test_decoder_generate_end_to_end():
     assert all(0 <= t < cfg.vocab for t in a.token_ids)
     assert a.token_ids != c.token_ids
     assert a.steady_rounds >= 1 and a.steady_tokens >= a.steady_rounds
+
+
+def test_ar_voronoi_matches_exact_plm():
+    """The AR-Voronoi comparator (k = 1: one verify row per step) and exact-match PLM rounds (k = 7) decode the same
+    tokens (README.md:83-85, plm/voronoi_ar.py:3-6): with exact matching a proposal is accepted only if it equals
+    the token the verify decode gives, and every output position p is decoded with auxiliary cell aux[p]. The
+    forwards differ in row composition, so near-ties may flip late tokens; the shared prefix must be long."""
+    from plm.decoder import RoundDecoder
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config("plm-tiny")
+    weights = PLMWeights.random(cfg, seed=2)
+    prompt = list(range(300, 340))
+    tokens = []
+    for k in (1, 7):
+        decoder = RoundDecoder(weights, k, block_size=16, kv_cache_bytes=64 << 20, max_model_len=1024)
+        decoder.prepare()
+        tokens.append(decoder.generate(prompt, 48, seed=5, stop_at_eos=False).token_ids)
+        decoder.check()
+        decoder.close()
+    same = 0
+    while same < 48 and tokens[0][same] == tokens[1][same]:
+        same += 1
+    assert same >= 24, f"AR-Voronoi and exact PLM agree on only {same} leading tokens"
 
 
 @pytest.mark.gpu
