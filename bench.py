@@ -152,7 +152,7 @@ def _dist():
     return 0, 1, 0, None
 
 
-def _setup_decoder(seed: int = 0):
+def _setup_decoder(seed: int = 0, separate_mlp: bool = False):
     """The configs[1] workload: weights, a decoder over a shuffled pool, a 1024-token N(0, 1) context."""
     import torch
 
@@ -168,7 +168,7 @@ def _setup_decoder(seed: int = 0):
     g = torch.Generator().manual_seed(seed)
     table = torch.randperm(num_pages, generator=g)[:max_pages].tolist()
     decoder = RoundDecoder(weights, K, "nucleus", None, block_size=PAGE, kv_cache_bytes=num_pages * page_bytes,
-                           max_model_len=max_model_len, block_table=table)
+                           max_model_len=max_model_len, block_table=table, separate_mlp=separate_mlp)
     decoder.prepare()
     return cfg, weights, decoder
 
@@ -336,7 +336,7 @@ def run_native(args) -> None:
     import torch
 
     rank, world, local, dist = _dist()
-    cfg, weights, decoder = _setup_decoder()
+    cfg, weights, decoder = _setup_decoder(separate_mlp=args.separate_mlp)
     _seed_context(decoder, cfg)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -438,6 +438,8 @@ def main() -> None:
     parser.add_argument("--impl", default="native", choices=("native", "reference"))
     parser.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     parser.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end requests (profiling runs)")
+    parser.add_argument("--separate-mlp", action="store_true",
+                        help="gate_up and down as two launches instead of the persistent MLP block launch")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "native":
         args.warmup = 3

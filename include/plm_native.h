@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 2
+#define PLM_ABI_VERSION 3
 
 enum plm_status {
   PLM_OK = 0,
@@ -258,6 +258,8 @@ typedef struct plm_round_desc {
   int64_t seq_capacity;   /* accepted-count record (0: 1 << 17) */
   int64_t aux_len;        /* auxiliary cell stream (0: 8192) */
   int32_t max_prefill;    /* rows per prefill chunk, 1..256 */
+  int32_t separate_mlp;   /* 0: gate_up, SiLU and down of a forward of at most 128 rows run as one persistent
+                             launch (default); 1: as two launches, like wider forwards */
 } plm_round_desc;
 
 /* Device addresses of a handle's state, for readers and for seeding synthetic workloads. */

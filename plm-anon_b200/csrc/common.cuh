@@ -24,6 +24,7 @@ enum DeviceError : int {
   kErrTimeoutSplit = 5,     // split reduction saw an inconsistent arrival count
   kErrBadShape = 6,         // a kernel was launched with a shape it cannot handle
   kErrTimeoutPeer = 7,      // a cluster peer's st.async data did not arrive
+  kErrTimeoutFlag = 8,      // an operand another CTA of the grid produces was not signalled in time
 };
 
 // One second: far above any legitimate wait in a round (a whole round takes about a millisecond).
@@ -114,6 +115,27 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// ----------------------------------------------------------------------------------------------------------------
+// Hand-off between CTAs of one grid through global counters. The writer stores its data, executes
+// __threadfence(), synchronises the CTA threads that stored, and one thread adds to the counter with release
+// semantics; the reader polls with acquire loads and, before reading the data with TMA (the async proxy), orders
+// that read after the acquire with fence.proxy.async.global.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Barrier over `count` threads (a multiple of 32) of the CTA; ids 1..15 (0 is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned); `valid` false zero-fills.
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src, bool valid = true) {
   const int size = valid ? 16 : 0;
@@ -148,6 +170,25 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
+}
+
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to shared memory,
+// completing on `bar` like the tiled loads (no multicast).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Row operands packed for bulk loads ("row tiles"): k-block kb (64 elements) of rows [0, ntok) is ntok x 128
+// contiguous bytes, row r's 16-byte chunk c stored at chunk c ^ (r % 8) of its 128-byte row (the 128-byte swizzle
+// the MMA descriptors expect); k-blocks follow each other, so any run of k-blocks is one contiguous copy.
+// Returns the index of that 16-byte chunk.
+__host__ __device__ __forceinline__ size_t row_tile_chunk(int kb, int r, int c, int ntok) {
+  return (size_t(kb) * ntok + r) * 8 + size_t(c ^ (r & 7));
 }
 
 // ----------------------------------------------------------------------------------------------------------------

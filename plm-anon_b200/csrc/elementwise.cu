@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
   const int r = blockIdx.x, tid = threadIdx.x;
   grid_dependency_wait();
   allow_dependents();
+  if (r == 0 && tid == 0 && a.epoch != nullptr) *a.epoch += a.epoch_step;  // one forward more
   const int64_t offset = *a.offset;
   if (tid == 0) {
     int64_t id = a.vocab, cell = a.aux;  // proposal placeholder; masked sentinel cell
@@ -226,6 +227,7 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs
       for (int q = 0; q < kVec; ++q) ov[q] = from_f32<T>(round_to<T>(v[j][q] * rstd) * elem<T>(wv[j], q));
       reinterpret_cast<uint4*>(nrm)[c] = o;
       if (gathered != nullptr) reinterpret_cast<uint4*>(gathered)[c] = o;
+      if (a.row_tiles != nullptr) reinterpret_cast<uint4*>(a.row_tiles)[row_tile_chunk(c >> 3, r, c & 7, a.tile_rows)] = o;
     }
   }
 }

@@ -33,6 +33,8 @@ struct PrologueArgs {
   void* normed;                // [rows][hidden]
   int32_t* positions;          // [rows]
   int64_t* slots;              // [rows]
+  int* epoch;                  // forward counter of the MLP block's tile flags (null: none)
+  int epoch_step;              // 1 when this forward runs the MLP block kernel, else 0
   int* err;
 };
 
@@ -48,6 +50,8 @@ struct AddNormArgs {
   const float* partials = nullptr;  // non-null: x = bf16(sum of n_partials fp32 slices, split order)
   int n_partials = 0;
   int64_t partial_stride = 0;       // floats between slices
+  void* row_tiles = nullptr;        // non-null: the normed rows also as row tiles of `tile_rows` rows (common.cuh)
+  int tile_rows = 0;
 };
 
 struct KvAppendArgs {

@@ -15,6 +15,7 @@
 
 #include "attention.h"
 #include "elementwise.h"
+#include "mlp.h"
 #include "runtime.h"
 #include "verify.h"
 
@@ -75,6 +76,13 @@ struct plm_handle {
           *chunk_offsets = nullptr;
   int64_t prompt_len = 0;
   int attn_splits_round = 1;
+  // MLP block kernel: schedule, per-layer gate_up counters and the forward counter they are compared with
+  plm::MlpSchedule mlp;
+  int* mlp_flags = nullptr;  // [layers] gate_up tiles stored, summed over the block forwards
+  void* mlp_tiles = nullptr;  // per layer: packed gate_up then packed down (pack.cu)
+  void *x_tiles = nullptr, *act_tiles = nullptr;  // the MLP block's row operands as row tiles (common.cuh)
+  size_t mlp_gate_up_bytes = 0, mlp_layer_bytes = 0;
+  int* epoch = nullptr;
 };
 
 namespace plm {
@@ -164,6 +172,9 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
   p.normed = h->x_norm;
   p.positions = h->positions;
   p.slots = h->slots;
+  const bool mlp_block = h->mlp.sched != nullptr && rows <= kMlpMaxRows;
+  p.epoch = h->epoch;
+  p.epoch_step = mlp_block ? 1 : 0;
   p.err = h->ctx->err;
   int st = prologue_launch(p, rows, s, true);
   if (st != PLM_OK) return st;
@@ -216,19 +227,43 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     if (st != PLM_OK) return st;
     AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
                       h->partials, s_o, slice};
+    if (mlp_block) {  // the MLP block reads its input as row tiles
+      n1.row_tiles = h->x_tiles;
+      n1.tile_rows = gemm_token_tile(rows);
+    }
     st = add_norm_launch(n1, rows, s, true);
     if (st != PLM_OK) return st;
 
-    plm_gemm_epilogue silu = {};
-    silu.kind = PLM_EPI_SILU_MUL;
-    silu.gate_offset = m.intermediate;
-    st = gemm(h, h->gate_up[l], &h->map_gate_up[l], 2 * m.intermediate, hidden, h->x_norm, rows, silu, h->act,
-              m.intermediate, s);
-    if (st != PLM_OK) return st;
-    const int s_d = gemm_partial_splits(h->ctx, hidden, m.intermediate, rows);
-    st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, part, h->partials, hidden, s,
-              s_d);
-    if (st != PLM_OK) return st;
+    int s_d = 0;
+    if (mlp_block) {
+      MlpBlockArgs b = {};
+      b.dtype = m.dtype;
+      b.gate_up_tiles = static_cast<const uint8_t*>(h->mlp_tiles) + size_t(l) * h->mlp_layer_bytes;
+      b.down_tiles = static_cast<const uint8_t*>(b.gate_up_tiles) + h->mlp_gate_up_bytes;
+      b.x_tiles = h->x_tiles;
+      b.act_tiles = h->act_tiles;
+      b.partials = h->partials;
+      b.rows = rows;
+      b.hidden = hidden;
+      b.intermediate = m.intermediate;
+      b.gate_done = h->mlp_flags + l;
+      b.epoch = h->epoch;
+      b.err = h->ctx->err;
+      st = mlp_block_launch(h->mlp, b, s, true);
+      if (st != PLM_OK) return st;
+      s_d = h->mlp.down_splits;
+    } else {
+      plm_gemm_epilogue silu = {};
+      silu.kind = PLM_EPI_SILU_MUL;
+      silu.gate_offset = m.intermediate;
+      st = gemm(h, h->gate_up[l], &h->map_gate_up[l], 2 * m.intermediate, hidden, h->x_norm, rows, silu, h->act,
+                m.intermediate, s);
+      if (st != PLM_OK) return st;
+      s_d = gemm_partial_splits(h->ctx, hidden, m.intermediate, rows);
+      st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, part, h->partials, hidden, s,
+                s_d);
+      if (st != PLM_OK) return st;
+    }
     const bool last = l + 1 == m.num_layers;
     AddNormArgs n2 = {nullptr,  h->residual,           h->x_norm, last ? h->final_norm : h->in_norm[l + 1],
                       hidden,   m.rms_eps,             last ? gather_row : -1, last ? h->gathered : nullptr,
@@ -365,8 +400,10 @@ int plm_destroy(plm_handle* h) {
                   h->verify_logits, h->best_val, h->best_idx, h->verify, h->flags, h->st_relpos, h->st_relaux,
                   h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
-                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets};
+                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->mlp_flags,
+                  h->epoch, h->mlp_tiles, h->x_tiles, h->act_tiles};
   for (void* b : bufs) cudaFree(b);
+  mlp_schedule_destroy(&h->mlp);
   if (h->own_table) cudaFree(h->table);
   plm_ctx_destroy(h->ctx);
   delete h;
@@ -452,6 +489,29 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   if (st == PLM_OK) st = dev_alloc(&h->best_idx, size_t(h->lm_tiles) * h->W, "argmax partials");
   if (st == PLM_OK) st = dev_alloc(&h->verify, 32, "verify");
   if (st == PLM_OK) st = dev_alloc(&h->flags, 32, "flags");
+  if (st == PLM_OK && rd->separate_mlp == 0 && hidden % 128 == 0 && I % 128 == 0) {
+    st = mlp_schedule_create(h->ctx->num_sms, hidden, I, &h->mlp);
+    // row tiles of up to kMlpMaxRows rows, zeroed once (rows past a forward's count are read but never stored)
+    if (st == PLM_OK) st = check_cuda(cudaMalloc(&h->x_tiles, size_t(kMlpMaxRows) * hidden * 2), "row tiles");
+    if (st == PLM_OK) st = check_cuda(cudaMalloc(&h->act_tiles, size_t(kMlpMaxRows) * I * 2), "row tiles");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->x_tiles, 0, size_t(kMlpMaxRows) * hidden * 2), "memset");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->act_tiles, 0, size_t(kMlpMaxRows) * I * 2), "memset");
+    if (st == PLM_OK) st = dev_alloc(&h->mlp_flags, size_t(L), "mlp gate_up counters");
+    if (st == PLM_OK) st = dev_alloc(&h->epoch, 1, "mlp epoch");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->mlp_flags, 0, size_t(L) * sizeof(int)), "memset");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->epoch, 0, sizeof(int)), "memset");
+    // the MLP weights are read once here into their packed layout
+    h->mlp_gate_up_bytes = packed_tiles_bytes(2 * I, hidden, I);
+    h->mlp_layer_bytes = h->mlp_gate_up_bytes + packed_tiles_bytes(hidden, I, 0);
+    if (st == PLM_OK)
+      st = check_cuda(cudaMalloc(&h->mlp_tiles, size_t(L) * h->mlp_layer_bytes), "packed MLP weights");
+    for (int l = 0; l < L && st == PLM_OK; ++l) {
+      uint8_t* dst = static_cast<uint8_t*>(h->mlp_tiles) + size_t(l) * h->mlp_layer_bytes;
+      st = pack_weight_tiles(h->gate_up[l], 2 * I, hidden, I, dst, nullptr);
+      if (st == PLM_OK) st = pack_weight_tiles(h->down[l], hidden, I, 0, dst + h->mlp_gate_up_bytes, nullptr);
+    }
+    if (st == PLM_OK) st = check_cuda(cudaDeviceSynchronize(), "packing the MLP weights");
+  }
   if (st != PLM_OK) return guard(st);
   // zero the activations once: rows past `rows` are read by TMA boxes but never stored
   for (void* b : {h->x_norm, h->residual, h->y, h->q, h->attn, h->act}) (void)b;

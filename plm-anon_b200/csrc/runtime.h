@@ -88,4 +88,8 @@ int gemm_token_tile(int rows);
 // Split count for a PLM_EPI_PARTIAL launch of this shape (1..16): fills the resident CTA slots in one wave.
 int gemm_partial_splits(plm_ctx* ctx, int n_out, int k, int rows);
 
+// Tiled weight copies (pack.cu): bytes of the packed copy, and the packing launch on `stream`.
+size_t packed_tiles_bytes(int n_out, int k, int gate_offset);
+int pack_weight_tiles(const void* w, int n_out, int k, int gate_offset, void* dst, cudaStream_t stream);
+
 }  // namespace plm

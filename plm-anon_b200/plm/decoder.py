@@ -41,14 +41,15 @@ class RoundDecoder:
 
     ``accept_rule`` is ``nucleus`` (``threshold`` None: exact match) or ``floor``. ``block_size`` is the KV page
     size; ``kv_cache_bytes`` sizes the page pool; ``block_table`` optionally maps logical to physical pages
-    (default identity)."""
+    (default identity). ``separate_mlp`` runs gate_up and down as two launches instead of the one persistent MLP
+    block launch (for comparison; forwards wider than 128 rows always use two)."""
 
     sequence_capacity = 1 << 17
 
     def __init__(self, weights: PLMWeights, k: int, accept_rule: str = "nucleus", threshold: float | None = None,
                  chunk_widths: tuple[int, ...] = (), *, block_size: int = 64, kv_cache_bytes: int = 1 << 30,
                  max_model_len: int = 4096, tokenizer=None, eos_token_id: int | None = None,
-                 block_table: list[int] | None = None, max_prefill: int = 256) -> None:
+                 block_table: list[int] | None = None, max_prefill: int = 256, separate_mlp: bool = False) -> None:
         if accept_rule not in ("nucleus", "floor"):
             raise ValueError(f"accept rule {accept_rule!r}: nucleus or floor")
         if not torch.cuda.is_available():
@@ -86,7 +87,8 @@ class RoundDecoder:
         round_desc = native.RoundDesc(
             k=k, rule=rule, threshold=-1.0 if threshold is None else float(threshold), page_size=block_size,
             num_pages=self.num_pages, max_pages=self.max_pages, out_capacity=self.max_seq,
-            seq_capacity=self.sequence_capacity, aux_len=AUX_STREAM_LENGTH, max_prefill=max_prefill)
+            seq_capacity=self.sequence_capacity, aux_len=AUX_STREAM_LENGTH, max_prefill=max_prefill,
+            separate_mlp=1 if separate_mlp else 0)
         self.handle = native.Handle(model, ptrs, round_desc, keepalive=(weights, self.cos_sin, self._layer_arrays))
         if block_table is not None:
             self.handle.set_block_table(block_table)

@@ -21,7 +21,7 @@ EPI_STORE, EPI_SILU_MUL, EPI_QKV_ROPE, EPI_LOGITS, EPI_TABLE, EPI_PARTIAL = rang
 
 DEVICE_ERRORS = {1: "TMA stage wait timed out", 2: "free stage wait timed out", 3: "MMA completion wait timed out",
                  4: "index out of range", 5: "split reduction arrival count inconsistent", 6: "unsupported shape",
-                 7: "cluster peer data wait timed out"}
+                 7: "cluster peer data wait timed out", 8: "cross-CTA operand wait timed out"}
 
 
 class NativeError(RuntimeError):
@@ -109,7 +109,8 @@ class WeightPtrs(ctypes.Structure):
 class RoundDesc(ctypes.Structure):
     _fields_ = [("k", c_int32), ("rule", c_int32), ("threshold", ctypes.c_float), ("page_size", c_int32),
                 ("num_pages", c_int32), ("max_pages", c_int32), ("out_capacity", c_int64),
-                ("seq_capacity", c_int64), ("aux_len", c_int64), ("max_prefill", c_int32)]
+                ("seq_capacity", c_int64), ("aux_len", c_int64), ("max_prefill", c_int32),
+                ("separate_mlp", c_int32)]
 
 
 class StatePtrs(ctypes.Structure):

@@ -35,7 +35,8 @@ def _argmax_partials(decoder, rows: int) -> np.ndarray:
     return np.asarray(decoder.proposal_argmax(rows), dtype=np.int64)
 
 
-def _pair(shape: str, k: int, page: int, seed: int, rule="nucleus", threshold=None, max_model_len=1024, **over):
+def _pair(shape: str, k: int, page: int, seed: int, rule="nucleus", threshold=None, max_model_len=1024,
+          separate_mlp=False, **over):
     from plm.decoder import RoundDecoder
     from plm.model import PLMWeights, shape_config
 
@@ -47,7 +48,7 @@ def _pair(shape: str, k: int, page: int, seed: int, rule="nucleus", threshold=No
     table = rng.permutation(num_pages)[:probe_pages].astype(np.int32)
     page_bytes = cfg.num_layers * 2 * cfg.num_kv_heads * page * cfg.head_dim * 2
     decoder = RoundDecoder(weights, k, rule, threshold, block_size=page, kv_cache_bytes=num_pages * page_bytes,
-                           max_model_len=max_model_len, block_table=table.tolist())
+                           max_model_len=max_model_len, block_table=table.tolist(), separate_mlp=separate_mlp)
     assert decoder.num_pages == num_pages and decoder.max_pages == probe_pages
     shape_o = omodel.ModelShape(cfg.num_layers, cfg.hidden, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                                 cfg.intermediate, cfg.vocab, cfg.aux_vocab, cfg.num_aux_tokens, cfg.rms_eps,
@@ -94,6 +95,7 @@ def _close(name, gpu, ref, report, rel=0.0, floor=0.0):
     ("plm-80m", 6, 16, "nucleus", None, {"num_layers": 2}),
     ("plm-1.3b", 7, 16, "nucleus", None, {}),
     ("plm-tiny", 1, 16, "nucleus", None, {}),  # k = 1: the AR-Voronoi comparator (plm/voronoi_ar.py)
+    ("plm-80m", 7, 16, "nucleus", None, {"num_layers": 2, "separate_mlp": True}),  # gate_up and down as two launches
 ])
 def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides):
     decoder, oracle, cfg = _pair(shape, k, page, seed=3, rule=rule, threshold=threshold, **overrides)
