@@ -276,17 +276,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
 
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
   const size_t out_stride = size_t(a.num_heads) * HD;
+  // Element (row, col) of the output: row-major, or inside the row tiles (the 16-byte chunk of its k-block, then
+  // the position within the chunk; writers store at most one chunk's worth at a time).
+  uint8_t* tiles = static_cast<uint8_t*>(a.row_tiles);
+  auto out_at = [&](int row, int col) -> __nv_bfloat16* {
+    if (tiles != nullptr)
+      return reinterpret_cast<__nv_bfloat16*>(tiles + row_tile_chunk(col >> 6, row, (col >> 3) & 7, a.tile_rows) * 16) +
+             (col & 7);
+    return out + size_t(row) * out_stride + col;
+  };
   if (a.splits == 1) {
     const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
     for (int j = 0; j < HD / 8; ++j) {
       const int col = head * HD + j * 8 + 2 * tq;
       if (r0 < a.rows)
-        *reinterpret_cast<__nv_bfloat162*>(out + size_t(r0) * out_stride + col) =
-            __floats2bfloat162_rn(o[j][0] * inv0, o[j][1] * inv0);
+        *reinterpret_cast<__nv_bfloat162*>(out_at(r0, col)) = __floats2bfloat162_rn(o[j][0] * inv0, o[j][1] * inv0);
       if (r1 < a.rows)
-        *reinterpret_cast<__nv_bfloat162*>(out + size_t(r1) * out_stride + col) =
-            __floats2bfloat162_rn(o[j][2] * inv1, o[j][3] * inv1);
+        *reinterpret_cast<__nv_bfloat162*>(out_at(r1, col)) = __floats2bfloat162_rn(o[j][2] * inv1, o[j][3] * inv1);
     }
     return;
   }
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
       }
       const int grow = qt * kQRowsPerCta + row_begin + lr;
       const float inv = wts[lr * (S + 1) + S];
-      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + size_t(grow) * out_stride + head * HD + c);
+      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out_at(grow, head * HD + c));
       dst[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
       dst[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
     }
@@ -414,7 +421,8 @@ int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
   if (a.page_size < 1 || a.page_size > 4096 || (a.page_size & (a.page_size - 1)) != 0)
     return fail(PLM_ERR_UNSUPPORTED, "attention: page size %d (a power of two <= 4096)", a.page_size);
   a.page_shift = __builtin_ctz(unsigned(a.page_size));
-  if (!a.q || !a.k_cache || !a.v_cache || !a.block_table || !a.offset || !a.depth || !a.own_start || !a.out)
+  if (!a.q || !a.k_cache || !a.v_cache || !a.block_table || !a.offset || !a.depth || !a.own_start ||
+      (!a.out && !a.row_tiles) || (a.row_tiles && (a.tile_rows < a.rows || a.tile_rows % 16 != 0)))
     return fail(PLM_ERR_INVALID, "attention: null operand");
   const int q_tiles = (a.rows + kQRowsPerCta - 1) / kQRowsPerCta;
   if (a.splits < 1) a.splits = 1;

@@ -23,7 +23,9 @@ struct AttnArgs {
   const int32_t* own_start;    // [rows]
   int num_heads, num_kv_heads, head_dim;
   float scale_log2;            // head_dim^-1/2 * log2(e)
-  void* out;                   // [rows][num_heads * head_dim]
+  void* out;                   // [rows][num_heads * head_dim]; may be null when row_tiles is set
+  void* row_tiles;             // non-null: the output written as row tiles of tile_rows rows instead (common.cuh)
+  int tile_rows;
   int splits;                  // KV splits = cluster size, a power of two <= 8
   int* err;
 };

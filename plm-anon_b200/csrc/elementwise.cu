@@ -50,7 +50,8 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
   const int r = blockIdx.x, tid = threadIdx.x;
   grid_dependency_wait();
   allow_dependents();
-  if (r == 0 && tid == 0 && a.epoch != nullptr) *a.epoch += a.epoch_step;  // one forward more
+  if (r == 0 && a.counters != nullptr)
+    for (int i = tid; i < a.n_counters; i += kRowThreads) a.counters[i] = 0;
   const int64_t offset = *a.offset;
   if (tid == 0) {
     int64_t id = a.vocab, cell = a.aux;  // proposal placeholder; masked sentinel cell

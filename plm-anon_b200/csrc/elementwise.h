@@ -33,8 +33,8 @@ struct PrologueArgs {
   void* normed;                // [rows][hidden]
   int32_t* positions;          // [rows]
   int64_t* slots;              // [rows]
-  int* epoch;                  // forward counter of the MLP block's tile flags (null: none)
-  int epoch_step;              // 1 when this forward runs the MLP block kernel, else 0
+  int* counters;               // zeroed at the start of the forward (the layer blocks' phase counters; may be null)
+  int n_counters;
   int* err;
 };
 

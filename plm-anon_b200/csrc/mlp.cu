@@ -1,32 +1,37 @@
-// The Llama MLP block of one forward as ONE persistent launch:
-//   act = SiLU(x . Wg^T) * (x . Wu^T)            (vLLM LlamaMLP: gate_up_proj -> SiluAndMul)
-//   partials[s] = act[:, K_s] . Wd[:, K_s]^T      (down_proj, fp32 k-split partials)
-// The products are the ones the two skinny_gemm_kernel launches it replaces compute (gemm.cuh, epilogues
-// kEpiSiluMul and kEpiPartial); a gate_up tile is accumulated by one CTA over the whole k range instead of a
-// cluster of k-splits, so fp32 sums are formed in another order.
+// Everything between attention and the next layer's input norm as ONE persistent launch per layer:
+//   o partials[s] = attn[:, K_s] . Wo[:, K_s]^T          (o_proj, fp32 k-split partials)
+//   residual, x   = residual-add RMSNorm of sum_s o partials[s]   (vLLM fused_add_rms_norm)
+//   act           = SiLU(x . Wg^T) * (x . Wu^T)          (gate_up_proj -> SiluAndMul)
+//   partials[s]   = act[:, K_s] . Wd[:, K_s]^T           (down_proj, fp32 k-split partials; the residual-add RMSNorm
+//                                                         launched after the block sums them)
+// The products and the norm are those of the separate launches it replaces (skinny_gemm_kernel with the kEpiPartial
+// and kEpiSiluMul epilogues, add_norm_kernel); a gate_up tile is accumulated by one CTA over the whole k range
+// instead of a cluster of k-splits, and the norm's sum of squares is reduced in another order, so fp32 sums are
+// formed in another order.
 //
-// Why one launch: at 56 rows the block streams 101 MB of weights per layer and the row operands are tiny, so the
-// time is HBM time plus whatever stalls the weight stream. With two launches the stream stops at the boundary:
-// the down launch can start loading only when the gate_up grid has drained. Here one CTA per SM runs a fixed list
-// of units (its gate_up tiles, then down (tile, k-split) units) through ONE continuous ring, so the weights of its
-// down units stream while the gate_up phase finishes. Only the act operand of the down units waits: on one counter
-// per layer that every gate_up tile increments once stored (by whichever CTA computed it).
+// Why one launch: at 56 rows the layer streams 109 MB of these weights and the row operands are tiny, so the time
+// is HBM time plus whatever stalls the weight stream. With separate launches the stream stops at every kernel
+// boundary. Here one CTA per SM runs a fixed list of units (o units, norm rows, gate_up tiles, down units) through
+// ONE continuous ring, so the weights of a CTA's next units stream while the phase before finishes. Only the row
+// operands wait, each phase on one counter of this layer that the units of the phase before increment: the norm
+// rows on the o units, gate_up on the norm rows, down on the gate_up tiles.
 //
 // Every operand is one contiguous bulk copy per ring stage of two k-blocks: the weights come from packed copies
-// (pack.cu, 32 KB per stage), x and act as row tiles (common.cuh: x written by the residual-add RMSNorm before this
-// kernel, act by this kernel's SiLU epilogue). A stage therefore costs the SM's copy engine two operations for
-// 32 KB of weights; with 64-k stages and tensor-map boxes it took four, which paced the ring below HBM speed.
+// (pack.cu, 32 KB per stage), the row operands as row tiles (common.cuh: the attention output written by the
+// attention kernel, x by the norm rows, act by the SiLU epilogue). A stage therefore costs the SM's copy engine two
+// operations for 32 KB of weights; with 64-k stages and tensor-map boxes it took four, which paced the ring below
+// HBM speed.
 //
 // Warp roles (352 threads): warp 0 issues the weight copies (never waits on another kernel or CTA, only on free ring
-// stages), warp 10 issues the row-operand copies (x after the previous kernel, act after the gate_up counter),
-// warp 1 issues tcgen05.mma into one of two TMEM accumulators, warps 2-9 drain the other accumulator (SiLU * up
-// over all 256 epilogue threads, or the fp32 partial store), so the epilogue of one unit overlaps the MMAs of the
-// next. A ring stage completes when both producers' copies have landed (its full barrier expects two arrivals).
+// stages), warp 10 issues the row-operand copies (after the previous kernel, or after a phase counter), warp 1
+// issues tcgen05.mma into one of two TMEM accumulators, warps 2-9 run the epilogues (the fp32 partial store, SiLU *
+// up over all 256 epilogue threads) and the norm rows, so the epilogue of one unit overlaps the MMAs of the next.
+// A ring stage completes when both producers' copies have landed (its full barrier expects two arrivals).
 //
-// Progress: every CTA is resident at once (one CTA per SM, grid = SM count), gate_up units wait on nothing but the
-// previous kernel, and down units wait only on gate_up tiles, so every wait ends. Each wait is still bounded (one
-// second); on expiry the kernel records kErrTimeoutFlag / a stage timeout in the device error word, every role
-// stops, copies in flight are drained and TMEM is freed.
+// Progress: every CTA is resident at once (one CTA per SM, grid = SM count); every CTA runs its units in phase
+// order (o, norm, gate_up, down) and a unit only waits for units of earlier phases, so every wait ends. Each wait
+// is still bounded (one second); on expiry the kernel records kErrTimeoutFlag / a stage timeout in the device error
+// word, every role stops, copies in flight are drained and TMEM is freed.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -63,18 +68,17 @@ struct MlpShape {
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-// Unit code: bit 30 = down (else gate_up), bits 12..29 = tile, bits 0..11 = k-split.
-__host__ __device__ constexpr int mlp_unit(int down, int tile, int split) {
-  return (down << 30) | (tile << 12) | split;
+// Unit code: bits 28..29 = kind, bits 12..27 = tile (the row for a norm unit), bits 0..11 = k-split.
+enum BlockUnitKind : int { kUnitGate = 0, kUnitDown = 1, kUnitO = 2, kUnitNorm = 3 };
+__host__ __device__ constexpr int block_unit(int kind, int tile, int split) {
+  return (kind << 28) | (tile << 12) | split;
 }
 
+template <int NTOK>
+__device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int et, float* red, volatile int* abort_flag);
+
 template <typename T, int NTOK>
-__global__ void __launch_bounds__(kMlpThreads, 1)
-    mlp_block_kernel(const uint8_t* __restrict__ wg_tiles, const uint8_t* __restrict__ x_tiles,
-                     const uint8_t* __restrict__ wd_tiles, uint8_t* __restrict__ act_tiles,
-                     const int* __restrict__ sched, const int* __restrict__ sched_off, float* __restrict__ partials,
-                     int* gate_done, const int* epoch, int rows, int hidden, int intermediate, int down_splits,
-                     int* err) {
+__global__ void __launch_bounds__(kMlpThreads, 1) mlp_block_kernel(const BlockParams p) {
   using S = MlpShape<NTOK>;
   constexpr uint32_t IDESC = umma_idesc_f16(128, NTOK, std::is_same<T, __nv_bfloat16>::value);
 
@@ -92,8 +96,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   int* counts = reinterpret_cast<int*>(tmem_slot + 4);  // stages issued: [0] weights, [1] rows; [2] consumed
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int u_begin = sched_off[blockIdx.x], u_end = sched_off[blockIdx.x + 1];
-  const int gate_kb = hidden / kGemmBK, down_kb = intermediate / kGemmBK;
+  const int u_begin = p.sched_off[blockIdx.x], u_end = p.sched_off[blockIdx.x + 1];
+  const int gate_kb = p.hidden / kGemmBK, down_kb = p.intermediate / kGemmBK, o_kb = p.q_size / kGemmBK;
+  int* const err = p.err;
 
   if (tid == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -146,16 +151,20 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   };
   // k-block range of a unit, in whole stages (split boundaries fall on even k-blocks). Both producers walk a unit's
   // stages starting at stage (tile % stages) and wrapping around, so that the CTAs that read the same row operand
-  // (every gate_up tile reads all of x; the 16 tiles of a down split read the same act k-blocks) do not request
-  // the same k-block at the same moment; the MMA accumulates the stages in arrival order.
+  // (every gate_up tile reads all of x; the tiles of a down or o split read the same k-blocks) do not request the
+  // same k-block at the same moment; the MMA accumulates the stages in arrival order.
   auto unit_range = [&](int code, int& kb0, int& kb1) {
-    if (code >> 30) {
-      const int split = code & 0xfff, pairs = down_kb / kMlpStageKb;
-      kb0 = kMlpStageKb * (split * pairs / down_splits);
-      kb1 = kMlpStageKb * ((split + 1) * pairs / down_splits);
-    } else {
+    const int kind = (code >> 28) & 3, split = code & 0xfff;
+    if (kind == kUnitGate) {
       kb0 = 0;
       kb1 = gate_kb;
+    } else if (kind == kUnitNorm) {
+      kb0 = kb1 = 0;
+    } else {
+      const int pairs = (kind == kUnitDown ? down_kb : o_kb) / kMlpStageKb;
+      const int splits = kind == kUnitDown ? p.down_splits : p.o_splits;
+      kb0 = kMlpStageKb * (split * pairs / splits);
+      kb1 = kMlpStageKb * ((split + 1) * pairs / splits);
     }
   };
 
@@ -166,11 +175,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     int it = 0;
     bool ok = true;
     for (int u = u_begin; u < u_end && ok; ++u) {
-      const int code = sched[u];
-      const bool down = (code >> 30) != 0;
-      const int tile = (code >> 12) & 0x3ffff;
+      const int code = p.sched[u];
+      const int kind = (code >> 28) & 3, tile = (code >> 12) & 0xffff;
+      if (kind == kUnitNorm) continue;
       int kb0, kb1;
       unit_range(code, kb0, kb1);
+      const uint8_t* wbase = kind == kUnitGate ? p.wg_tiles + size_t(tile) * gate_kb * S::W_BLOCK
+                             : kind == kUnitDown ? p.wd_tiles + size_t(tile) * down_kb * S::W_BLOCK
+                                                 : p.wo_tiles + size_t(tile) * o_kb * S::W_BLOCK;
       const int n_st = (kb1 - kb0) / kMlpStageKb;
       for (int i = 0; i < n_st; ++i, ++it) {
         const int kb = kb0 + kMlpStageKb * ((i + tile) % n_st);  // rotated k order (see unit_range)
@@ -181,10 +193,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         }
         if (lane == 0) {
           // two consecutive packed blocks of the tile: the stage's swizzled shared-memory image (pack.cu)
-          const uint8_t* src = down ? wd_tiles + (size_t(tile) * down_kb + kb) * S::W_BLOCK
-                                    : wg_tiles + (size_t(tile) * gate_kb + kb) * S::W_BLOCK;
           mbar_arrive_expect_tx(full_bar + s, S::W_BYTES);
-          bulk_load(smem + s * S::STAGE, src, S::W_BYTES, full_bar + s, pol_w);
+          bulk_load(smem + s * S::STAGE, wbase + size_t(kb) * S::W_BLOCK, S::W_BYTES, full_bar + s, pol_w);
           counts[0] = it + 1;
         }
       }
@@ -193,37 +203,43 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     // ---------------- row-operand producer ----------------
     uint64_t pol_x = 0;
     if (lane == 0) pol_x = l2_policy_evict_last();
-    grid_dependency_wait();  // x and the epoch are written by earlier kernels of the stream
-    int it = 0;
-    bool ok = true, act_ready = false;
-    for (int u = u_begin; u < u_end && ok; ++u) {
-      const int code = sched[u];
-      const bool down = (code >> 30) != 0;
-      const int tile = (code >> 12) & 0x3ffff;
-      int kb0, kb1;
-      unit_range(code, kb0, kb1);
-      if (down && !act_ready) {
-        // Every gate_up tile of this forward is stored once the layer's counter reaches epoch * tiles. On a
-        // timeout the copies are still issued (stale data, error recorded) so that their stages can be drained.
-        if (lane == 0) {
-          const int target = *reinterpret_cast<const volatile int*>(epoch) * (intermediate / 64);
-          if (ld_acquire_gpu(gate_done) < target) {
-            const uint64_t start = global_timer_ns();
-            while (ld_acquire_gpu(gate_done) < target) {
-              if (*abort_flag) break;
-              if (global_timer_ns() - start > kWaitLimitNs) {
-                record_error(err, kErrTimeoutFlag);
-                *abort_flag = 1;
-                break;
-              }
+    grid_dependency_wait();  // the attention output is written by the previous kernel
+    // Waits once for a counter of this grid (norm rows, gate_up tiles). On a timeout the copies are still issued
+    // (stale data, error recorded) so that their stages can be drained.
+    auto wait_counter = [&](const int* counter, int target) {
+      if (lane == 0) {
+        if (ld_acquire_gpu(counter) < target) {
+          const uint64_t start = global_timer_ns();
+          while (ld_acquire_gpu(counter) < target) {
+            if (*abort_flag) break;
+            if (global_timer_ns() - start > kWaitLimitNs) {
+              record_error(err, kErrTimeoutFlag);
+              *abort_flag = 1;
+              break;
             }
           }
-          fence_proxy_async_global();  // the bulk reads of act below come after the acquire
         }
-        __syncwarp();
+        fence_proxy_async_global();  // the bulk reads below come after the acquire
+      }
+      __syncwarp();
+    };
+    int it = 0;
+    bool ok = true, x_ready = false, act_ready = false;
+    for (int u = u_begin; u < u_end && ok; ++u) {
+      const int code = p.sched[u];
+      const int kind = (code >> 28) & 3, tile = (code >> 12) & 0xffff;
+      if (kind == kUnitNorm) continue;
+      if (kind == kUnitGate && !x_ready) {
+        wait_counter(p.ctr + 1, p.rows);  // every row normed
+        x_ready = true;
+      }
+      if (kind == kUnitDown && !act_ready) {
+        wait_counter(p.ctr + 2, p.intermediate / 64);  // every gate_up tile stored
         act_ready = true;
       }
-      const uint8_t* rows_src = down ? act_tiles : x_tiles;
+      int kb0, kb1;
+      unit_range(code, kb0, kb1);
+      const uint8_t* rows_src = kind == kUnitGate ? p.x_tiles : kind == kUnitDown ? p.act_tiles : p.attn_tiles;
       const int n_st = (kb1 - kb0) / kMlpStageKb;
       for (int i = 0; i < n_st; ++i, ++it) {
         const int kb = kb0 + kMlpStageKb * ((i + tile) % n_st);  // rotated k order (see unit_range)
@@ -244,9 +260,11 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     // ---------------- MMA issuer ----------------
     int it = 0, n = 0;
     bool ok = true;
-    for (int u = u_begin; u < u_end && ok; ++u, ++n) {
+    for (int u = u_begin; u < u_end && ok; ++u) {
+      const int code = p.sched[u];
+      if (((code >> 28) & 3) == kUnitNorm) continue;
       int kb0, kb1;
-      unit_range(sched[u], kb0, kb1);
+      unit_range(code, kb0, kb1);
       const int buf = n & 1;
       if (n >= 2 && !warp_wait(acc_empty + buf, ((n >> 1) - 1) & 1, kErrTimeoutDone)) break;
       tc_fence_after();
@@ -275,6 +293,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       if (!ok) break;
       if (lane == 0) umma_commit(acc_full + buf);
       __syncwarp();
+      ++n;
     }
     if (lane == 0) umma_commit(done_bar);  // arrives once every MMA issued above has completed
     __syncwarp();
@@ -282,16 +301,20 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     // ---------------- epilogue warps 2..9 ----------------
     // Warp w reads TMEM lane slice w % 4 (features slice*32 .. +31 of the tile) for the column (row) blocks
     // half*32, half*32 + 64, ... with half = (w - 2) / 4, so the eight warps cover the accumulator once.
-    grid_dependency_wait();  // act and the partials may still be read by earlier kernels of the stream
+    grid_dependency_wait();  // the outputs may still be read by earlier kernels of the stream
     const int et = tid - 64;            // 0..255
     const int slice = warp & 3;
     const int half = (warp - 2) >> 2;
     const int feat = slice * 32 + lane;
-    int n = 0;
-    for (int u = u_begin; u < u_end; ++u, ++n) {
-      const int code = sched[u];
-      const bool down = (code >> 30) != 0;
-      const int tile = (code >> 12) & 0x3ffff, split = code & 0xfff;
+    const int rows = p.rows, hidden = p.hidden;
+    int n = 0;  // MMA units seen (the TMEM buffer parity)
+    for (int u = u_begin; u < u_end; ++u) {
+      const int code = p.sched[u];
+      const int kind = (code >> 28) & 3, tile = (code >> 12) & 0xffff, split = code & 0xfff;
+      if (kind == kUnitNorm) {
+        if (tile < rows) block_norm_row<NTOK>(p, tile, et, reinterpret_cast<float*>(gu), abort_flag);
+        continue;
+      }
       const int buf = n & 1;
       // One warp waits for the accumulator and publishes the verdict, so that all epilogue warps take the same
       // path through the named barriers below.
@@ -303,8 +326,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       if (verdict[n & 1] == 0) break;
       tc_fence_after();
       const uint32_t t_acc = tmem + (uint32_t(slice * 32) << 16) + uint32_t(buf * S::ACC_COLS);
-      if (down) {
-        float* part = partials + size_t(split) * rows * hidden;
+      if (kind != kUnitGate) {  // o or down: the fp32 partial of this k-split
+        float* part = p.partials + size_t(split) * rows * hidden;
         const int f = tile * 128 + feat;
         for (int c0 = half * 32; c0 < rows; c0 += 64) {
           float v[32];
@@ -316,6 +339,11 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + buf);
+        if (kind == kUnitO) {  // the norm rows wait for every o partial
+          __threadfence();
+          named_barrier_sync(3, kMlpEpiWarps * 32);
+          if (et == 0) red_release_gpu_add(p.ctr + 0, 1);
+        }
       } else {
         // TMEM lanes 0..63 are the gate rows, 64..127 the up rows of the same 64 intermediate features: each warp
         // stages its values (rounded to the model dtype, as the separate launch does) ...
@@ -334,7 +362,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         named_barrier_sync(2, kMlpEpiWarps * 32);  // gate and up staged
         // ... then all 256 threads form SiLU(gate) * up, eight features (one 16-byte chunk of the act row tile)
         // per thread and step.
-        uint4* act_chunks = reinterpret_cast<uint4*>(act_tiles);
+        uint4* act_chunks = reinterpret_cast<uint4*>(p.act_tiles);
         for (int idx = et; idx < rows * 8; idx += kMlpEpiWarps * 32) {
           const int r = idx >> 3, c = idx & 7;
           const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * 64 + c * 8);
@@ -352,8 +380,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         }
         __threadfence();
         named_barrier_sync(3, kMlpEpiWarps * 32);  // every feature of the tile is stored
-        if (et == 0) red_release_gpu_add(gate_done, 1);
+        if (et == 0) red_release_gpu_add(p.ctr + 2, 1);
       }
+      ++n;
     }
   }
 
@@ -380,41 +409,129 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   }
 }
 
+// One row of the residual-add RMSNorm after the o projection (the arithmetic of add_norm_kernel in
+// elementwise.cu, vLLM fused_add_rms_norm): x = the o partials summed in split order and rounded to bf16,
+// v = x + residual in fp32, residual <- bf16(v), normed = bf16(bf16(v * rstd) * w), written as row tiles for the
+// gate_up units. Run by the 256 epilogue threads once every o unit of the grid has signalled.
+template <int NTOK>
+__device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int et, float* red,
+                                               volatile int* abort_flag) {
+  using T = __nv_bfloat16;
+  constexpr int kThreads = kMlpEpiWarps * 32;
+  if (et == 0) {
+    const int target = p.o_units;
+    if (ld_acquire_gpu(p.ctr + 0) < target) {
+      const uint64_t start = global_timer_ns();
+      while (ld_acquire_gpu(p.ctr + 0) < target) {
+        if (*abort_flag) break;
+        if (global_timer_ns() - start > kWaitLimitNs) {
+          record_error(p.err, kErrTimeoutFlag);
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+  }
+  named_barrier_sync(4, kThreads);  // the partials of every o unit are visible from here on
+  const int chunks = p.hidden / 8;
+  T* res = reinterpret_cast<T*>(p.residual) + size_t(r) * p.hidden;
+  const T* w = reinterpret_cast<const T*>(p.norm_weight);
+  constexpr int kMaxChunks = 2;  // hidden <= 8 * 256 * 2
+  float v[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxChunks; ++j) {
+    const int c = et + j * kThreads;
+    if (c >= chunks) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < p.o_splits; ++sp) {
+      const float4* src = reinterpret_cast<const float4*>(p.partials + (size_t(sp) * p.rows + r) * p.hidden) + 2 * c;
+      const float4 lo = src[0], hi = src[1];
+      acc[0] += lo.x;
+      acc[1] += lo.y;
+      acc[2] += lo.z;
+      acc[3] += lo.w;
+      acc[4] += hi.x;
+      acc[5] += hi.y;
+      acc[6] += hi.z;
+      acc[7] += hi.w;
+    }
+    const uint4 rv = reinterpret_cast<const uint4*>(res)[c];
+    const T* r8 = reinterpret_cast<const T*>(&rv);
+    uint4 nr;
+    T* n8 = reinterpret_cast<T*>(&nr);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[j][q] = round_to<T>(acc[q]) + to_f32<T>(r8[q]);
+      n8[q] = from_f32<T>(v[j][q]);
+      ss += v[j][q] * v[j][q];
+    }
+    reinterpret_cast<uint4*>(res)[c] = nr;
+  }
+  ss = warp_sum(ss);
+  if ((et & 31) == 0) red[et >> 5] = ss;
+  named_barrier_sync(5, kThreads);
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMlpEpiWarps; ++i) total += red[i];
+  const float rstd = rsqrtf(total / float(p.hidden) + p.eps);
+  uint4* tiles = reinterpret_cast<uint4*>(p.x_tiles);
+#pragma unroll
+  for (int j = 0; j < kMaxChunks; ++j) {
+    const int c = et + j * kThreads;
+    if (c >= chunks) continue;
+    const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
+    const T* w8 = reinterpret_cast<const T*>(&wv);
+    uint4 o;
+    T* o8 = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o8[q] = from_f32<T>(round_to<T>(v[j][q] * rstd) * to_f32<T>(w8[q]));
+    tiles[row_tile_chunk(c >> 3, r, c & 7, NTOK)] = o;
+  }
+  __threadfence();
+  named_barrier_sync(6, kThreads);  // the row is stored (and red[] may be reused)
+  if (et == 0) red_release_gpu_add(p.ctr + 1, 1);
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // Host side.
 
-std::vector<int> mlp_schedule_units(int grid, int gate_tiles, int gate_kb, int down_tiles, int down_splits,
-                                    int down_kb, std::vector<int>* offsets) {
-  // Gate_up tiles go to the CTAs with the fewest gate k-blocks so far. The down units can only load their act
-  // operand once every gate_up tile is stored, so they are balanced on their own: each goes to the CTA with the
-  // fewest down k-blocks so far, preferring CTAs with less gate work, then the lowest index (deterministic).
-  // Within a CTA its gate_up units precede its down units.
+std::vector<int> mlp_schedule_units(const MlpSchedule& s, int hidden, int intermediate, int q_size,
+                                    std::vector<int>* offsets) {
+  // Phase by phase, in the order every CTA runs them:
+  //   o units: unit j on CTA grid - 1 - (j % grid), so the CTAs without a gate_up tile take them first;
+  //   norm rows: row r on CTA (gate_tiles + r) % grid, so the rows every forward has (the low ones) start on the
+  //     CTAs without a gate_up tile;
+  //   gate_up tiles: tile t on the CTA with the fewest gate k-blocks (CTA t when there are at most grid tiles);
+  //   down units: they load their act operand only once every gate_up tile is stored, so they are balanced on
+  //     their own: each goes to the CTA with the fewest down k-blocks, then less gate work, then the lowest index.
+  const int grid = s.grid;
   std::vector<std::vector<int>> lists(grid);
+  const int o_units = s.o_tiles * s.o_splits;
+  for (int j = 0; j < o_units; ++j)
+    lists[grid - 1 - (j % grid)].push_back(block_unit(kUnitO, j % s.o_tiles, j / s.o_tiles));
+  for (int r = 0; r < kMlpMaxRows; ++r) lists[(s.gate_tiles + r) % grid].push_back(block_unit(kUnitNorm, r, 0));
   std::vector<long> gate_load(grid, 0), down_load(grid, 0);
-  auto least = [&](bool down) {
-    int best = 0;
-    for (int c = 1; c < grid; ++c) {
-      const bool better = down ? (down_load[c] < down_load[best] ||
-                                  (down_load[c] == down_load[best] && gate_load[c] < gate_load[best]))
-                               : gate_load[c] < gate_load[best];
-      if (better) best = c;
-    }
-    return best;
-  };
-  for (int t = 0; t < gate_tiles; ++t) {
-    const int c = least(false);
-    lists[c].push_back(mlp_unit(0, t, 0));
+  const int gate_kb = hidden / kGemmBK, down_kb = intermediate / kGemmBK;
+  for (int t = 0; t < s.gate_tiles; ++t) {
+    int c = 0;
+    for (int i = 1; i < grid; ++i)
+      if (gate_load[i] < gate_load[c]) c = i;
+    lists[c].push_back(block_unit(kUnitGate, t, 0));
     gate_load[c] += gate_kb;
   }
-  for (int sp = 0; sp < down_splits; ++sp) {
-    const int pairs = down_kb / kMlpStageKb;  // as unit_range in the kernel
-    const int kb = kMlpStageKb * ((sp + 1) * pairs / down_splits - sp * pairs / down_splits);
-    for (int t = 0; t < down_tiles; ++t) {
-      const int c = least(true);
-      lists[c].push_back(mlp_unit(1, t, sp));
+  const int pairs = down_kb / kMlpStageKb;  // as unit_range in the kernel
+  for (int sp = 0; sp < s.down_splits; ++sp) {
+    const int kb = kMlpStageKb * ((sp + 1) * pairs / s.down_splits - sp * pairs / s.down_splits);
+    for (int t = 0; t < s.down_tiles; ++t) {
+      int c = 0;
+      for (int i = 1; i < grid; ++i)
+        if (down_load[i] < down_load[c] || (down_load[i] == down_load[c] && gate_load[i] < gate_load[c])) c = i;
+      lists[c].push_back(block_unit(kUnitDown, t, sp));
       down_load[c] += kb;
     }
   }
+  (void)q_size;
   std::vector<int> flat;
   offsets->assign(1, 0);
   for (int c = 0; c < grid; ++c) {
@@ -424,27 +541,30 @@ std::vector<int> mlp_schedule_units(int grid, int gate_tiles, int gate_kb, int d
   return flat;
 }
 
-int mlp_schedule_create(int num_sms, int hidden, int intermediate, MlpSchedule* out) {
+int mlp_schedule_create(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out) {
   *out = MlpSchedule{};
-  if (hidden % (kMlpStageKb * kGemmBK) != 0 || intermediate % (kMlpStageKb * kGemmBK) != 0 ||
-      intermediate / 64 >= (1 << 18))
-    return fail(PLM_ERR_UNSUPPORTED, "mlp block: hidden %d, intermediate %d (multiples of 128)", hidden, intermediate);
+  constexpr int kPair = kMlpStageKb * kGemmBK;
+  if (hidden % kPair != 0 || intermediate % kPair != 0 || q_size % kPair != 0 || hidden > 8 * 256 * 2 ||
+      intermediate / 64 >= (1 << 16))
+    return fail(PLM_ERR_UNSUPPORTED, "layer block: hidden %d, intermediate %d, q_size %d", hidden, intermediate,
+                q_size);
   MlpSchedule s;
   s.grid = num_sms;
   s.gate_tiles = intermediate / 64;
   s.down_tiles = (hidden + 127) / 128;
-  s.down_splits = std::min(kMlpMaxDownSplits, intermediate / (kMlpStageKb * kGemmBK));
+  s.down_splits = std::min(kMlpMaxDownSplits, intermediate / kPair);
+  s.o_tiles = (hidden + 127) / 128;
+  s.o_splits = std::max(1, std::min({kMlpMaxOSplits, q_size / kPair, num_sms / s.o_tiles}));
   std::vector<int> offsets;
-  std::vector<int> units = mlp_schedule_units(s.grid, s.gate_tiles, hidden / kGemmBK, s.down_tiles, s.down_splits,
-                                              intermediate / kGemmBK, &offsets);
-  int st = check_cuda(cudaMalloc(&s.sched, units.size() * sizeof(int)), "mlp schedule");
-  if (st == PLM_OK) st = check_cuda(cudaMalloc(&s.sched_off, offsets.size() * sizeof(int)), "mlp schedule");
+  std::vector<int> units = mlp_schedule_units(s, hidden, intermediate, q_size, &offsets);
+  int st = check_cuda(cudaMalloc(&s.sched, units.size() * sizeof(int)), "block schedule");
+  if (st == PLM_OK) st = check_cuda(cudaMalloc(&s.sched_off, offsets.size() * sizeof(int)), "block schedule");
   if (st == PLM_OK)
     st = check_cuda(cudaMemcpy(s.sched, units.data(), units.size() * sizeof(int), cudaMemcpyHostToDevice),
-                    "mlp schedule upload");
+                    "block schedule upload");
   if (st == PLM_OK)
     st = check_cuda(cudaMemcpy(s.sched_off, offsets.data(), offsets.size() * sizeof(int), cudaMemcpyHostToDevice),
-                    "mlp schedule upload");
+                    "block schedule upload");
   if (st != PLM_OK) {
     mlp_schedule_destroy(&s);
     return st;
@@ -462,51 +582,52 @@ void mlp_schedule_destroy(MlpSchedule* s) {
 namespace {
 
 template <typename T, int NTOK>
-int launch_block(const MlpSchedule& s, const MlpBlockArgs& a, cudaStream_t stream, bool pdl) {
+int launch_block(const MlpSchedule& s, const BlockParams& p, cudaStream_t stream, bool pdl) {
   using S = MlpShape<NTOK>;
   auto kernel = mlp_block_kernel<T, NTOK>;
   static bool attr_set = false;
   if (!attr_set) {
     int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM),
-                        "cudaFuncSetAttribute(mlp block smem)");
+                        "cudaFuncSetAttribute(block smem)");
     if (st != PLM_OK) return st;
     int per_sm = 0;
     st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kMlpThreads, S::SMEM),
-                    "mlp block occupancy");
+                    "block occupancy");
     if (st != PLM_OK) return st;
-    if (per_sm < 1) return fail(PLM_ERR_UNSUPPORTED, "mlp block: %d bytes of shared memory do not fit", S::SMEM);
+    if (per_sm < 1) return fail(PLM_ERR_UNSUPPORTED, "layer block: %d bytes of shared memory do not fit", S::SMEM);
     attr_set = true;
   }
-  return check_cuda(launch(kernel, dim3(s.grid), dim3(kMlpThreads), S::SMEM, stream, pdl,
-                           static_cast<const uint8_t*>(a.gate_up_tiles), static_cast<const uint8_t*>(a.x_tiles),
-                           static_cast<const uint8_t*>(a.down_tiles), static_cast<uint8_t*>(a.act_tiles),
-                           (const int*)s.sched, (const int*)s.sched_off,
-                           a.partials, a.gate_done, a.epoch, a.rows, a.hidden,
-                           a.intermediate, s.down_splits, a.err),
+  return check_cuda(launch(kernel, dim3(s.grid), dim3(kMlpThreads), S::SMEM, stream, pdl, p),
                     "mlp_block_kernel launch");
 }
 
 }  // namespace
 
-int mlp_block_launch(const MlpSchedule& s, const MlpBlockArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "mlp block: only bf16 is built");
-  if (s.sched == nullptr || s.grid < 1) return fail(PLM_ERR_INVALID, "mlp block: no schedule");
-  if (a.rows < 1 || a.rows > kMlpMaxRows) return fail(PLM_ERR_UNSUPPORTED, "mlp block: %d rows", a.rows);
-  if (a.hidden / 128 > s.down_tiles || a.intermediate / 64 != s.gate_tiles)
-    return fail(PLM_ERR_INVALID, "mlp block: shape differs from its schedule");
-  if (!a.act_tiles || !a.partials || !a.gate_done || !a.epoch || !a.gate_up_tiles || !a.down_tiles || !a.x_tiles)
-    return fail(PLM_ERR_INVALID, "mlp block: null operand");
-  switch (gemm_token_tile(a.rows)) {  // the row maps' box height
-    case 16: return launch_block<__nv_bfloat16, 16>(s, a, stream, pdl);
-    case 32: return launch_block<__nv_bfloat16, 32>(s, a, stream, pdl);
-    case 48: return launch_block<__nv_bfloat16, 48>(s, a, stream, pdl);
-    case 64: return launch_block<__nv_bfloat16, 64>(s, a, stream, pdl);
-    case 80: return launch_block<__nv_bfloat16, 80>(s, a, stream, pdl);
-    case 96: return launch_block<__nv_bfloat16, 96>(s, a, stream, pdl);
-    case 112: return launch_block<__nv_bfloat16, 112>(s, a, stream, pdl);
-    case 128: return launch_block<__nv_bfloat16, 128>(s, a, stream, pdl);
+int mlp_block_launch(const MlpSchedule& s, BlockParams p, int dtype, cudaStream_t stream, bool pdl) {
+  if (dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "layer block: only bf16 is built");
+  if (s.sched == nullptr || s.grid < 1) return fail(PLM_ERR_INVALID, "layer block: no schedule");
+  if (p.rows < 1 || p.rows > kMlpMaxRows) return fail(PLM_ERR_UNSUPPORTED, "layer block: %d rows", p.rows);
+  if ((p.hidden + 127) / 128 != s.down_tiles || p.intermediate / 64 != s.gate_tiles)
+    return fail(PLM_ERR_INVALID, "layer block: shape differs from its schedule");
+  if (!p.wo_tiles || !p.wg_tiles || !p.wd_tiles || !p.attn_tiles || !p.x_tiles || !p.act_tiles || !p.partials ||
+      !p.residual || !p.norm_weight || !p.ctr)
+    return fail(PLM_ERR_INVALID, "layer block: null operand");
+  p.sched = s.sched;
+  p.sched_off = s.sched_off;
+  p.o_splits = s.o_splits;
+  p.down_splits = s.down_splits;
+  p.o_units = s.o_tiles * s.o_splits;
+  switch (gemm_token_tile(p.rows)) {  // the row tiles' height
+    case 16: return launch_block<__nv_bfloat16, 16>(s, p, stream, pdl);
+    case 32: return launch_block<__nv_bfloat16, 32>(s, p, stream, pdl);
+    case 48: return launch_block<__nv_bfloat16, 48>(s, p, stream, pdl);
+    case 64: return launch_block<__nv_bfloat16, 64>(s, p, stream, pdl);
+    case 80: return launch_block<__nv_bfloat16, 80>(s, p, stream, pdl);
+    case 96: return launch_block<__nv_bfloat16, 96>(s, p, stream, pdl);
+    case 112: return launch_block<__nv_bfloat16, 112>(s, p, stream, pdl);
+    case 128: return launch_block<__nv_bfloat16, 128>(s, p, stream, pdl);
   }
-  return fail(PLM_ERR_UNSUPPORTED, "mlp block: %d rows", a.rows);
+  return fail(PLM_ERR_UNSUPPORTED, "layer block: %d rows", p.rows);
 }
 
 }  // namespace plm

@@ -1,5 +1,6 @@
-// The Llama MLP block of the round as one persistent launch (mlp.cu): gate_up with SiLU(gate) * up, then down
-// written as fp32 k-split partials, which the residual-add RMSNorm after it sums in split order.
+// One persistent launch per layer for everything between attention and the next layer's input norm (mlp.cu): the
+// o projection, the residual-add RMSNorm after it, gate_up with SiLU(gate) * up, and down written as fp32 k-split
+// partials, which the residual-add RMSNorm after the block sums in split order.
 #pragma once
 
 #include <cuda.h>
@@ -10,40 +11,51 @@
 
 namespace plm {
 
-constexpr int kMlpMaxRows = 128;        // widest row tile of the block kernel; wider forwards use two launches
+constexpr int kMlpMaxRows = 128;        // widest row tile of the block kernel; wider forwards use separate launches
 constexpr int kMlpMaxDownSplits = 16;   // k-splits of down (partials summed by the norm that follows)
+constexpr int kMlpMaxOSplits = 16;      // k-splits of o (partials summed by the block's own norm rows)
 
-// Work assignment of one block launch: every CTA of the grid runs a list of units, its gate_up tiles first, then
-// (down tile, k-split) units. Host-built once per model shape; `sched` and `sched_off` are device arrays.
+// Work assignment of one block launch: every CTA of the grid runs a list of units: its o (tile, k-split) units,
+// its norm rows, its gate_up tiles, then its down (tile, k-split) units. Host-built once per model shape; `sched`
+// and `sched_off` are device arrays.
 struct MlpSchedule {
-  int grid = 0;            // CTAs (one per SM)
-  int gate_tiles = 0;      // intermediate / 64
-  int down_tiles = 0;      // ceil(hidden / 128)
-  int down_splits = 0;     // k-splits of down
-  int* sched = nullptr;    // unit codes, CTA after CTA
+  int grid = 0;              // CTAs (one per SM)
+  int gate_tiles = 0;        // intermediate / 64
+  int down_tiles = 0;        // ceil(hidden / 128)
+  int down_splits = 0;       // k-splits of down
+  int o_tiles = 0;           // ceil(hidden / 128)
+  int o_splits = 0;          // k-splits of o
+  int* sched = nullptr;      // unit codes, CTA after CTA
   int* sched_off = nullptr;  // [grid + 1] offsets into sched
 };
 
-struct MlpBlockArgs {
-  int dtype;
-  const void* gate_up_tiles;  // the gate_up weight packed by pack_weight_tiles with gate_offset = intermediate
-  const void* down_tiles;     // the down weight packed by pack_weight_tiles (128-row tiles)
-  const void* x_tiles;        // the normed input as row tiles (common.cuh) of gemm_token_tile(rows) rows, k = hidden
-  void* act_tiles;            // SiLU(gate) * up written as row tiles of the same height, k = intermediate
-  float* partials;            // [down_splits][rows][hidden]
-  int rows, hidden, intermediate;
-  int* gate_done;          // this layer's counter: +1 per gate_up tile stored, so epoch * (intermediate / 64)
-                           // once a forward's act is complete
-  const int* epoch;        // MLP block forwards run so far, this one included
+// Kernel parameters of one launch (pointers are device addresses).
+struct BlockParams {
+  const uint8_t* wo_tiles;    // o weight packed by pack_weight_tiles (128-row tiles), k = q_size
+  const uint8_t* wg_tiles;    // gate_up weight packed with gate_offset = intermediate
+  const uint8_t* wd_tiles;    // down weight packed (128-row tiles), k = intermediate
+  const uint8_t* attn_tiles;  // attention output as row tiles (common.cuh) of gemm_token_tile(rows) rows
+  uint8_t* x_tiles;           // the normed rows, written by the block's norm rows, read by gate_up
+  uint8_t* act_tiles;         // SiLU(gate) * up, written by gate_up, read by down
+  const int* sched;
+  const int* sched_off;
+  float* partials;            // [splits][rows][hidden]: o partials, then (after the norm) down partials
+  void* residual;             // [>= rows][hidden] model dtype, updated by the norm rows
+  const void* norm_weight;    // post-attention RMSNorm weight [hidden]
+  float eps;
+  int* ctr;                   // this layer's counters, zero at the start of the forward: [0] o units stored,
+                              // [1] rows normed, [2] gate_up tiles stored
+  int rows, hidden, intermediate, q_size;
+  int o_splits, down_splits, o_units;
   int* err;
 };
 
-// Balanced assignment of units to `grid` CTAs by k-block count (deterministic); see mlp.cu.
-std::vector<int> mlp_schedule_units(int grid, int gate_tiles, int gate_kb, int down_tiles, int down_splits,
-                                    int down_kb, std::vector<int>* offsets);
-int mlp_schedule_create(int num_sms, int hidden, int intermediate, MlpSchedule* out);
+// Assignment of units to `grid` CTAs (deterministic); see mlp.cu.
+std::vector<int> mlp_schedule_units(const MlpSchedule& s, int hidden, int intermediate, int q_size,
+                                    std::vector<int>* offsets);
+int mlp_schedule_create(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out);
 void mlp_schedule_destroy(MlpSchedule* s);
-// One launch of the block for `rows` (1..kMlpMaxRows) rows.
-int mlp_block_launch(const MlpSchedule& s, const MlpBlockArgs& a, cudaStream_t stream, bool pdl);
+// One launch of the block for `p.rows` (1..kMlpMaxRows) rows; fills the schedule fields of `p`.
+int mlp_block_launch(const MlpSchedule& s, BlockParams p, int dtype, cudaStream_t stream, bool pdl);
 
 }  // namespace plm

@@ -78,11 +78,10 @@ struct plm_handle {
   int attn_splits_round = 1;
   // MLP block kernel: schedule, per-layer gate_up counters and the forward counter they are compared with
   plm::MlpSchedule mlp;
-  int* mlp_flags = nullptr;  // [layers] gate_up tiles stored, summed over the block forwards
-  void* mlp_tiles = nullptr;  // per layer: packed gate_up then packed down (pack.cu)
-  void *x_tiles = nullptr, *act_tiles = nullptr;  // the MLP block's row operands as row tiles (common.cuh)
-  size_t mlp_gate_up_bytes = 0, mlp_layer_bytes = 0;
-  int* epoch = nullptr;
+  int* block_ctr = nullptr;  // [layers][4] phase counters of the layer blocks, zeroed by every forward's prologue
+  void* block_tiles = nullptr;  // per layer: packed o, gate_up, down (pack.cu)
+  void *attn_tiles = nullptr, *x_tiles = nullptr, *act_tiles = nullptr;  // row operands as row tiles (common.cuh)
+  size_t block_o_bytes = 0, block_gate_up_bytes = 0, block_layer_bytes = 0;
 };
 
 namespace plm {
@@ -172,9 +171,9 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
   p.normed = h->x_norm;
   p.positions = h->positions;
   p.slots = h->slots;
-  const bool mlp_block = h->mlp.sched != nullptr && rows <= kMlpMaxRows;
-  p.epoch = h->epoch;
-  p.epoch_step = mlp_block ? 1 : 0;
+  const bool layer_block = h->mlp.sched != nullptr && rows <= kMlpMaxRows;
+  p.counters = h->block_ctr;
+  p.n_counters = h->block_ctr != nullptr ? 4 * m.num_layers : 0;
   p.err = h->ctx->err;
   int st = prologue_launch(p, rows, s, true);
   if (st != PLM_OK) return st;
@@ -213,46 +212,51 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     a.num_kv_heads = m.num_kv_heads;
     a.head_dim = hd;
     a.scale_log2 = float(1.4426950408889634 / sqrt(double(hd)));
-    a.out = h->attn;
+    if (layer_block) {  // the block reads the attention output as row tiles
+      a.row_tiles = h->attn_tiles;
+      a.tile_rows = gemm_token_tile(rows);
+    } else {
+      a.out = h->attn;
+    }
     a.splits = attn_splits;
     st = attention_launch(h->ctx, a, s, true);
     if (st != PLM_OK) return st;
 
-    // o and down write their k-split partials; the residual-add RMSNorm that follows sums them in split order
+    // o and down write their k-split partials; the residual-add RMSNorm that follows each sums them in split order
     plm_gemm_epilogue part = {};
     part.kind = PLM_EPI_PARTIAL;
     const int64_t slice = int64_t(rows) * hidden;
-    const int s_o = gemm_partial_splits(h->ctx, hidden, q_size, rows);
-    st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, part, h->partials, hidden, s, s_o);
-    if (st != PLM_OK) return st;
-    AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
-                      h->partials, s_o, slice};
-    if (mlp_block) {  // the MLP block reads its input as row tiles
-      n1.row_tiles = h->x_tiles;
-      n1.tile_rows = gemm_token_tile(rows);
-    }
-    st = add_norm_launch(n1, rows, s, true);
-    if (st != PLM_OK) return st;
-
     int s_d = 0;
-    if (mlp_block) {
-      MlpBlockArgs b = {};
-      b.dtype = m.dtype;
-      b.gate_up_tiles = static_cast<const uint8_t*>(h->mlp_tiles) + size_t(l) * h->mlp_layer_bytes;
-      b.down_tiles = static_cast<const uint8_t*>(b.gate_up_tiles) + h->mlp_gate_up_bytes;
-      b.x_tiles = h->x_tiles;
-      b.act_tiles = h->act_tiles;
+    if (layer_block) {  // o, its norm, gate_up and down in one launch
+      BlockParams b = {};
+      const uint8_t* w = static_cast<const uint8_t*>(h->block_tiles) + size_t(l) * h->block_layer_bytes;
+      b.wo_tiles = w;
+      b.wg_tiles = w + h->block_o_bytes;
+      b.wd_tiles = w + h->block_o_bytes + h->block_gate_up_bytes;
+      b.attn_tiles = static_cast<const uint8_t*>(h->attn_tiles);
+      b.x_tiles = static_cast<uint8_t*>(h->x_tiles);
+      b.act_tiles = static_cast<uint8_t*>(h->act_tiles);
       b.partials = h->partials;
+      b.residual = h->residual;
+      b.norm_weight = h->post_norm[l];
+      b.eps = m.rms_eps;
+      b.ctr = h->block_ctr + 4 * l;
       b.rows = rows;
       b.hidden = hidden;
       b.intermediate = m.intermediate;
-      b.gate_done = h->mlp_flags + l;
-      b.epoch = h->epoch;
+      b.q_size = q_size;
       b.err = h->ctx->err;
-      st = mlp_block_launch(h->mlp, b, s, true);
+      st = mlp_block_launch(h->mlp, b, m.dtype, s, true);
       if (st != PLM_OK) return st;
       s_d = h->mlp.down_splits;
     } else {
+      const int s_o = gemm_partial_splits(h->ctx, hidden, q_size, rows);
+      st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, part, h->partials, hidden, s, s_o);
+      if (st != PLM_OK) return st;
+      AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
+                        h->partials, s_o, slice};
+      st = add_norm_launch(n1, rows, s, true);
+      if (st != PLM_OK) return st;
       plm_gemm_epilogue silu = {};
       silu.kind = PLM_EPI_SILU_MUL;
       silu.gate_offset = m.intermediate;
@@ -400,8 +404,8 @@ int plm_destroy(plm_handle* h) {
                   h->verify_logits, h->best_val, h->best_idx, h->verify, h->flags, h->st_relpos, h->st_relaux,
                   h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
-                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->mlp_flags,
-                  h->epoch, h->mlp_tiles, h->x_tiles, h->act_tiles};
+                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->block_ctr,
+                  h->block_tiles, h->attn_tiles, h->x_tiles, h->act_tiles};
   for (void* b : bufs) cudaFree(b);
   mlp_schedule_destroy(&h->mlp);
   if (h->own_table) cudaFree(h->table);
@@ -489,28 +493,32 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   if (st == PLM_OK) st = dev_alloc(&h->best_idx, size_t(h->lm_tiles) * h->W, "argmax partials");
   if (st == PLM_OK) st = dev_alloc(&h->verify, 32, "verify");
   if (st == PLM_OK) st = dev_alloc(&h->flags, 32, "flags");
-  if (st == PLM_OK && rd->separate_mlp == 0 && hidden % 128 == 0 && I % 128 == 0) {
-    st = mlp_schedule_create(h->ctx->num_sms, hidden, I, &h->mlp);
+  if (st == PLM_OK && rd->separate_mlp == 0 && hidden % 128 == 0 && I % 128 == 0 && q_size % 128 == 0 &&
+      hidden <= 4096) {
+    st = mlp_schedule_create(h->ctx->num_sms, hidden, I, q_size, &h->mlp);
     // row tiles of up to kMlpMaxRows rows, zeroed once (rows past a forward's count are read but never stored)
-    if (st == PLM_OK) st = check_cuda(cudaMalloc(&h->x_tiles, size_t(kMlpMaxRows) * hidden * 2), "row tiles");
-    if (st == PLM_OK) st = check_cuda(cudaMalloc(&h->act_tiles, size_t(kMlpMaxRows) * I * 2), "row tiles");
-    if (st == PLM_OK) st = check_cuda(cudaMemset(h->x_tiles, 0, size_t(kMlpMaxRows) * hidden * 2), "memset");
-    if (st == PLM_OK) st = check_cuda(cudaMemset(h->act_tiles, 0, size_t(kMlpMaxRows) * I * 2), "memset");
-    if (st == PLM_OK) st = dev_alloc(&h->mlp_flags, size_t(L), "mlp gate_up counters");
-    if (st == PLM_OK) st = dev_alloc(&h->epoch, 1, "mlp epoch");
-    if (st == PLM_OK) st = check_cuda(cudaMemset(h->mlp_flags, 0, size_t(L) * sizeof(int)), "memset");
-    if (st == PLM_OK) st = check_cuda(cudaMemset(h->epoch, 0, sizeof(int)), "memset");
-    // the MLP weights are read once here into their packed layout
-    h->mlp_gate_up_bytes = packed_tiles_bytes(2 * I, hidden, I);
-    h->mlp_layer_bytes = h->mlp_gate_up_bytes + packed_tiles_bytes(hidden, I, 0);
-    if (st == PLM_OK)
-      st = check_cuda(cudaMalloc(&h->mlp_tiles, size_t(L) * h->mlp_layer_bytes), "packed MLP weights");
-    for (int l = 0; l < L && st == PLM_OK; ++l) {
-      uint8_t* dst = static_cast<uint8_t*>(h->mlp_tiles) + size_t(l) * h->mlp_layer_bytes;
-      st = pack_weight_tiles(h->gate_up[l], 2 * I, hidden, I, dst, nullptr);
-      if (st == PLM_OK) st = pack_weight_tiles(h->down[l], hidden, I, 0, dst + h->mlp_gate_up_bytes, nullptr);
+    const size_t tile_elems[3] = {size_t(kMlpMaxRows) * q_size, size_t(kMlpMaxRows) * hidden, size_t(kMlpMaxRows) * I};
+    void** tiles[3] = {&h->attn_tiles, &h->x_tiles, &h->act_tiles};
+    for (int i = 0; i < 3 && st == PLM_OK; ++i) {
+      st = check_cuda(cudaMalloc(tiles[i], tile_elems[i] * 2), "row tiles");
+      if (st == PLM_OK) st = check_cuda(cudaMemset(*tiles[i], 0, tile_elems[i] * 2), "memset");
     }
-    if (st == PLM_OK) st = check_cuda(cudaDeviceSynchronize(), "packing the MLP weights");
+    if (st == PLM_OK) st = dev_alloc(&h->block_ctr, size_t(4) * L, "layer block counters");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->block_ctr, 0, size_t(4) * L * sizeof(int)), "memset");
+    // the o, gate_up and down weights are read once here into their packed layout
+    h->block_o_bytes = packed_tiles_bytes(hidden, q_size, 0);
+    h->block_gate_up_bytes = packed_tiles_bytes(2 * I, hidden, I);
+    h->block_layer_bytes = h->block_o_bytes + h->block_gate_up_bytes + packed_tiles_bytes(hidden, I, 0);
+    if (st == PLM_OK)
+      st = check_cuda(cudaMalloc(&h->block_tiles, size_t(L) * h->block_layer_bytes), "packed layer weights");
+    for (int l = 0; l < L && st == PLM_OK; ++l) {
+      uint8_t* dst = static_cast<uint8_t*>(h->block_tiles) + size_t(l) * h->block_layer_bytes;
+      st = pack_weight_tiles(h->o[l], hidden, q_size, 0, dst, nullptr);
+      if (st == PLM_OK) st = pack_weight_tiles(h->gate_up[l], 2 * I, hidden, I, dst + h->block_o_bytes, nullptr);
+      if (st == PLM_OK)
+        st = pack_weight_tiles(h->down[l], hidden, I, 0, dst + h->block_o_bytes + h->block_gate_up_bytes, nullptr);
+    }
+    if (st == PLM_OK) st = check_cuda(cudaDeviceSynchronize(), "packing the layer weights");
   }
   if (st != PLM_OK) return guard(st);
   // zero the activations once: rows past `rows` are read by TMA boxes but never stored
