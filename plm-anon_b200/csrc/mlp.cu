@@ -340,9 +340,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_block_kernel(const BlockPa
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + buf);
         if (kind == kUnitO) {  // the norm rows wait for every o partial
-          __threadfence();
           named_barrier_sync(3, kMlpEpiWarps * 32);
-          if (et == 0) red_release_gpu_add(p.ctr + 0, 1);
+          if (et == 0) signal_stored(p.ctr + 0);
         }
       } else {
         // TMEM lanes 0..63 are the gate rows, 64..127 the up rows of the same 64 intermediate features: each warp
@@ -378,9 +377,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_block_kernel(const BlockPa
           }
           act_chunks[row_tile_chunk(tile, r, c, NTOK)] = out;
         }
-        __threadfence();
         named_barrier_sync(3, kMlpEpiWarps * 32);  // every feature of the tile is stored
-        if (et == 0) red_release_gpu_add(p.ctr + 2, 1);
+        if (et == 0) signal_stored(p.ctr + 2);
       }
       ++n;
     }
@@ -488,9 +486,8 @@ __device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int 
     for (int q = 0; q < 8; ++q) o8[q] = from_f32<T>(round_to<T>(v[j][q] * rstd) * to_f32<T>(w8[q]));
     tiles[row_tile_chunk(c >> 3, r, c & 7, NTOK)] = o;
   }
-  __threadfence();
   named_barrier_sync(6, kThreads);  // the row is stored (and red[] may be reused)
-  if (et == 0) red_release_gpu_add(p.ctr + 1, 1);
+  if (et == 0) signal_stored(p.ctr + 1);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
