@@ -241,6 +241,29 @@ def _gemm_graph(decoder, cfg):
     return graph, keep, 4 * c.num_layers + 1
 
 
+def _block_graph(decoder, cfg):
+    """A graph of exactly the round's layer-block launches (o projection, its norm, gate_up and down of every layer,
+    over the round's rows), each after the counter reset a forward's prologue does."""
+    import torch
+
+    body = lambda: [decoder.handle.layer_block(layer, decoder.width) for layer in range(cfg.num_layers)]  # noqa: E731
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        body()
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    return graph, (), cfg.num_layers
+
+
+def block_weight_bytes(cfg) -> int:
+    """Weight bytes one round's layer blocks stream: o, gate_up and down of every layer."""
+    q_size = cfg.num_heads * cfg.head_dim
+    return cfg.num_layers * 2 * (cfg.hidden * q_size + 3 * cfg.intermediate * cfg.hidden)
+
+
 def _time_graph(graph, reps: int) -> float:
     import torch
 
@@ -328,8 +351,11 @@ def run_reference(args) -> None:
 
 # DRAM bytes (read + write) of the weight GEMMs of one round of the benchmark shape, from one ncu capture of each
 # GEMM shape (profiles/skinny_gemm_plm-1.3b_rows56.md): 24 x (qkv 25.47 + o 8.69 + gate_up 68.12 + down 34.64) MB
-# + lm_head 209.7 MB.
+# + lm_head 209.7 MB. Used for the separate-launch configuration.
 GEMM_DRAM_BYTES_PER_ROUND = 3.495e9
+# DRAM bytes (read + write) of one layer-block launch of the benchmark shape, from one ncu capture
+# (profiles/layer_block_plm-1.3b_rows56.md): 109.80 MB read + 5.31 MB written.
+BLOCK_DRAM_BYTES_PER_LAUNCH = 115.1e6
 
 
 def run_native(args) -> None:
@@ -365,12 +391,20 @@ def run_native(args) -> None:
     ms_per_step = elapsed_ms / args.steps
     value = total_tokens / (elapsed_ms / 1000)
 
-    # dominant kernel: the round's weight GEMMs, timed live
-    graph, keep, gemm_launches = _gemm_graph(decoder, cfg)
-    gemm_ms = _time_graph(graph, max(5, args.steps // 2))
+    # dominant kernel, timed live: the layer blocks (o, its norm, gate_up, down of every layer), or with separate
+    # launches the round's weight GEMMs
     bytes_ = round_bytes(cfg, ctx_mean, K)
     peak, peak_kind = _peaks()
-    achieved = bytes_["weights"] / (gemm_ms / 1000) / 1e9
+    if args.separate_mlp:
+        graph, keep, dom_launches = _gemm_graph(decoder, cfg)
+        dom_kernel, dom_bytes, dom_traffic = "skinny_gemm_kernel (all weight GEMMs of a round)", bytes_["weights"], \
+            GEMM_DRAM_BYTES_PER_ROUND
+    else:
+        graph, keep, dom_launches = _block_graph(decoder, cfg)
+        dom_kernel, dom_bytes = "mlp_block_kernel (the layer blocks of a round)", block_weight_bytes(cfg)
+        dom_traffic = None if BLOCK_DRAM_BYTES_PER_LAUNCH is None else BLOCK_DRAM_BYTES_PER_LAUNCH * cfg.num_layers
+    dom_ms = _time_graph(graph, max(5, args.steps // 2))
+    achieved = dom_bytes / (dom_ms / 1000) / 1e9
     round_achieved = bytes_["total"] / (ms_per_step / 1000) / 1e9
     del graph, keep
 
@@ -397,7 +431,8 @@ def run_native(args) -> None:
         cpu = cpu_baseline(weights, decoder, cfg, rounds=1)
 
     if rank == 0:
-        launches_per_round = 1 + 7 * cfg.num_layers + 2
+        # prologue, per layer qkv + attention + (block | o, norm, gate_up, down) + norm, then lm_head and verify
+        launches_per_round = 1 + (7 if args.separate_mlp else 4) * cfg.num_layers + 2
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -409,11 +444,11 @@ def run_native(args) -> None:
                        "l2": "inputs larger than L2 (3.4 GB weights per round), no flush"},
             "round_us": 1000 * ms_per_step,
             "tokens_per_round": total_tokens / (args.steps * world),
-            "roofline": {"bound": "hbm", "kernel": "skinny_gemm_kernel (all weight GEMMs of a round)",
+            "roofline": {"bound": "hbm", "kernel": dom_kernel,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": peak_kind, "traffic": GEMM_DRAM_BYTES_PER_ROUND,
-                         "bytes_per_round": bytes_["weights"],
-                         "ms_per_round": gemm_ms, "launches_per_round": gemm_launches},
+                         "peak_source": peak_kind, "traffic": dom_traffic,
+                         "bytes_per_round": dom_bytes,
+                         "ms_per_round": dom_ms, "launches_per_round": dom_launches},
             "round_roofline": {"bound": "hbm", "achieved": round_achieved, "peak": peak, "unit": "GB/s",
                                "frac": round_achieved / peak, "bytes_per_round": bytes_},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": PROMPT_E2E * 8,

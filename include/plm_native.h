@@ -324,6 +324,12 @@ int plm_prefill(plm_handle* h, void* stream);
 int plm_round0(plm_handle* h, void* stream);
 /* One steady round: forward of k + k^2 rows, lm_head, verify decode, acceptance, commit. Graph-capturable. */
 int plm_round(plm_handle* h, void* stream);
+/* One decoder layer's o_proj, post_attention_layernorm and mlp (vLLM llama.py:198-250 LlamaDecoderLayer.forward
+ * after self_attn; plm/decoder.py:336 runs it inside the model forward) as the round runs it: the layer block over
+ * the handle's first `rows` (1..128) activation rows, reading the attention output the last forward left and
+ * updating the residual and the down partials. For measurement and tests; PLM_ERR_UNSUPPORTED when the handle was
+ * created with separate_mlp. */
+int plm_layer_block(plm_handle* h, int32_t layer, int32_t rows, void* stream);
 int plm_state(plm_handle* h, plm_state_ptrs* out);
 int plm_check(plm_handle* h, int32_t* device_error);
 

@@ -132,6 +132,32 @@ int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, 
   return gemm_launch(h->ctx, d, mw, mx, s, true);
 }
 
+// Layer `l`'s block (mlp.cu): o projection, the residual-add RMSNorm after it, gate_up + SiLU and down as k-split
+// partials, over `rows` rows whose attention output is in the row tiles. The block's phase counters must be zero
+// (every forward's prologue zeroes them).
+int layer_block_launch(plm_handle* h, int l, int rows, cudaStream_t s) {
+  const plm_model_desc& m = h->m;
+  BlockParams b = {};
+  const uint8_t* w = static_cast<const uint8_t*>(h->block_tiles) + size_t(l) * h->block_layer_bytes;
+  b.wo_tiles = w;
+  b.wg_tiles = w + h->block_o_bytes;
+  b.wd_tiles = w + h->block_o_bytes + h->block_gate_up_bytes;
+  b.attn_tiles = static_cast<const uint8_t*>(h->attn_tiles);
+  b.x_tiles = static_cast<uint8_t*>(h->x_tiles);
+  b.act_tiles = static_cast<uint8_t*>(h->act_tiles);
+  b.partials = h->partials;
+  b.residual = h->residual;
+  b.norm_weight = h->post_norm[l];
+  b.eps = m.rms_eps;
+  b.ctr = h->block_ctr + 4 * l;
+  b.rows = rows;
+  b.hidden = m.hidden;
+  b.intermediate = m.intermediate;
+  b.q_size = m.num_heads * m.head_dim;
+  b.err = h->ctx->err;
+  return mlp_block_launch(h->mlp, b, m.dtype, s, true);
+}
+
 // The Llama forward of `rows` rows whose logical KV indices start at *offset_ptr (vLLM llama.py:253-314):
 // prologue (+ layer-0 input norm), then per layer qkv(+RoPE, KV scatter) -> attention -> o -> add+norm ->
 // gate_up(+SiLU) -> down -> add+norm (the next layer's input norm, or the final norm).
@@ -228,25 +254,7 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     const int64_t slice = int64_t(rows) * hidden;
     int s_d = 0;
     if (layer_block) {  // o, its norm, gate_up and down in one launch
-      BlockParams b = {};
-      const uint8_t* w = static_cast<const uint8_t*>(h->block_tiles) + size_t(l) * h->block_layer_bytes;
-      b.wo_tiles = w;
-      b.wg_tiles = w + h->block_o_bytes;
-      b.wd_tiles = w + h->block_o_bytes + h->block_gate_up_bytes;
-      b.attn_tiles = static_cast<const uint8_t*>(h->attn_tiles);
-      b.x_tiles = static_cast<uint8_t*>(h->x_tiles);
-      b.act_tiles = static_cast<uint8_t*>(h->act_tiles);
-      b.partials = h->partials;
-      b.residual = h->residual;
-      b.norm_weight = h->post_norm[l];
-      b.eps = m.rms_eps;
-      b.ctr = h->block_ctr + 4 * l;
-      b.rows = rows;
-      b.hidden = hidden;
-      b.intermediate = m.intermediate;
-      b.q_size = q_size;
-      b.err = h->ctx->err;
-      st = mlp_block_launch(h->mlp, b, m.dtype, s, true);
+      st = layer_block_launch(h, l, rows, s);
       if (st != PLM_OK) return st;
       s_d = h->mlp.down_splits;
     } else {
@@ -680,6 +688,18 @@ int plm_round0(plm_handle* h, void* stream) {
                    h->attn_splits_round, -1, s);
   if (st == PLM_OK) st = lm_head(h, h->x_norm, h->W, 1, s);
   if (st == PLM_OK) st = verify(h, 1, kBookRound0, h->base, s);
+  return st;
+}
+
+int plm_layer_block(plm_handle* h, int32_t layer, int32_t rows, void* stream) {
+  if (!h) return fail(PLM_ERR_INVALID, "plm_layer_block: null handle");
+  if (h->mlp.sched == nullptr) return fail(PLM_ERR_UNSUPPORTED, "plm_layer_block: the handle runs separate launches");
+  if (layer < 0 || layer >= h->m.num_layers || rows < 1 || rows > kMlpMaxRows)
+    return fail(PLM_ERR_INVALID, "plm_layer_block: layer %d, rows %d", layer, rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the phase counters of this layer start at zero, as after a forward's prologue
+  int st = check_cuda(cudaMemsetAsync(h->block_ctr + 4 * layer, 0, 4 * sizeof(int), s), "plm_layer_block counters");
+  if (st == PLM_OK) st = layer_block_launch(h, layer, rows, s);
   return st;
 }
 

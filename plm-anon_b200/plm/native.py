@@ -147,6 +147,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_prefill": [c_void_p, c_void_p],
     "plm_round0": [c_void_p, c_void_p],
     "plm_round": [c_void_p, c_void_p],
+    "plm_layer_block": [c_void_p, c_int32, c_int32, c_void_p],
     "plm_state": [c_void_p, POINTER(StatePtrs)],
     "plm_check": [c_void_p, POINTER(c_int32)],
 }
@@ -312,6 +313,10 @@ class Handle:
 
     def round(self, stream=None) -> None:
         check(library().plm_round(self.handle, stream_handle(stream)), "plm_round")
+
+    def layer_block(self, layer: int, rows: int, stream=None) -> None:
+        """One decoder layer's o projection, post-attention norm and MLP as the round runs it (plm_layer_block)."""
+        check(library().plm_layer_block(self.handle, layer, rows, stream_handle(stream)), "plm_layer_block")
 
     def check(self) -> None:
         code = c_int32(0)

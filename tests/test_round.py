@@ -240,3 +240,27 @@ def test_generate_cli_end_to_end(tmp_path):
         assert all(len(r["token_ids"]) == 40 for r in p["results"])
     first, second = (p["results"] for p in result["passes"])
     assert [r["token_ids"] for r in first] == [r["token_ids"] for r in second]
+
+
+def test_layer_block_entry_point():
+    """plm_layer_block runs one layer's block as the round does (over the rows the last forward left); a handle
+    created with separate launches rejects it."""
+    from plm import native
+    from plm.decoder import RoundDecoder
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config("plm-tiny")
+    weights = PLMWeights.random(cfg, seed=4)
+    prompt = torch.randint(0, cfg.vocab, (40,), generator=torch.Generator().manual_seed(4))
+    decoder = RoundDecoder(weights, 7, block_size=16, kv_cache_bytes=64 << 20, max_model_len=1024)
+    decoder.handle.load_prompt(prompt.pin_memory())
+    decoder.handle.prefill()
+    decoder.handle.round0()
+    for layer in range(cfg.num_layers):
+        decoder.handle.layer_block(layer, decoder.width)
+    decoder.check()
+    decoder.close()
+    separate = RoundDecoder(weights, 7, block_size=16, kv_cache_bytes=64 << 20, max_model_len=1024, separate_mlp=True)
+    with pytest.raises(native.NativeError):
+        separate.handle.layer_block(0, separate.width)
+    separate.close()
