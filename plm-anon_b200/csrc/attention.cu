@@ -80,8 +80,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   const int64_t offset = *a.offset;
   const int64_t seq_len = offset + a.rows;
   const int n_tiles = int((seq_len + kKeysPerTile - 1) / kKeysPerTile);
-  const int t0 = int(int64_t(split) * n_tiles / a.splits);  // tiles spread evenly over the splits
-  const int t1 = int(int64_t(split + 1) * n_tiles / a.splits);
+  // Tiles spread evenly over the splits, the larger shares first: the last split holds the masked tiles of the
+  // round's own keys, so it gets the smaller share.
+  const int t0 = n_tiles - int(int64_t(a.splits - split) * n_tiles / a.splits);
+  const int t1 = n_tiles - int(int64_t(a.splits - split - 1) * n_tiles / a.splits);
   const int n_local = t1 - t0;
   int* pages = reinterpret_cast<int*>(smem + 2 * kStages * TILE_BYTES);
   const int64_t lp0 = (int64_t(t0) * kKeysPerTile) >> a.page_shift;
