@@ -196,6 +196,11 @@ __host__ __device__ __forceinline__ size_t row_tile_chunk(int kb, int r, int c, 
   return (size_t(kb) * ntok + r) * 8 + size_t(c ^ (r & 7));
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) from global memory into L2; nothing waits for it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ----------------------------------------------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA (kind::f16, both operands from shared memory), commit and loads.
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {

@@ -199,6 +199,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_block_kernel(const BlockPa
         }
       }
     }
+    if (lane == 0 && p.next_weights != nullptr) {
+      // This CTA's slice (4 KB aligned) of the weights the next kernel reads first, into L2 in 64 KB prefetches.
+      const long long per = ((p.next_bytes / gridDim.x) + 4095) & ~4095LL;
+      const long long b0 = per * blockIdx.x;
+      const long long n = p.next_bytes - b0 < per ? p.next_bytes - b0 : per;
+      for (long long off = 0; off < n; off += 65536)
+        bulk_prefetch_l2(p.next_weights + b0 + off, uint32_t(n - off < 65536 ? n - off : 65536));
+    }
   } else if (warp == kMlpRowWarp) {
     // ---------------- row-operand producer ----------------
     uint64_t pol_x = 0;

@@ -47,6 +47,11 @@ struct BlockParams {
                               // [1] rows normed, [2] gate_up tiles stored
   int rows, hidden, intermediate, q_size;
   int o_splits, down_splits, o_units;
+  // Weights the kernel after this block reads first (the next layer's qkv, or the head of lm_head): each CTA
+  // prefetches its slice into L2 once its own weight copies are issued, while the down phase and the norm after it
+  // leave HBM idle. May be null.
+  const uint8_t* next_weights;
+  long long next_bytes;
   int* err;
 };
 

@@ -154,6 +154,16 @@ int layer_block_launch(plm_handle* h, int l, int rows, cudaStream_t s) {
   b.hidden = m.hidden;
   b.intermediate = m.intermediate;
   b.q_size = m.num_heads * m.head_dim;
+  // the next kernel's first weights: the next layer's qkv, or after the last layer the head of lm_head (as much as
+  // the idle tail of the block and the norm after it can bring in)
+  constexpr long long kLmHeadPrefetch = 32ll << 20;
+  if (l + 1 < m.num_layers) {
+    b.next_weights = static_cast<const uint8_t*>(h->qkv[l + 1]);
+    b.next_bytes = (long long)(m.num_heads + 2 * m.num_kv_heads) * m.head_dim * m.hidden * 2;
+  } else {
+    b.next_weights = static_cast<const uint8_t*>(h->lm_head);
+    b.next_bytes = std::min<long long>((long long)m.vocab * m.hidden * 2, kLmHeadPrefetch) & ~15LL;
+  }
   b.err = h->ctx->err;
   return mlp_block_launch(h->mlp, b, m.dtype, s, true);
 }
