@@ -348,43 +348,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       out[size_t(c_begin + lc) * args.ldo + j0 + f] = from_f32<T>(act);
     }
   } else if (EPI == kEpiQkvRope) {
+    // Thread tid owns feature tile * 128 + tid of every row of the slice, so what depends on the feature alone (its
+    // head, rotary partner, plane) is worked out once, and a power-of-two page splits a slot with a shift and a
+    // mask instead of a 64-bit division. The row data (positions, slots, the rotary table) is read-only during the
+    // launch and is read through the non-coherent path.
+    static_assert(kGemmThreads == 128, "one feature per thread");
     const QkvEpilogue& q = args.qkv;
     const int hd = q.head_dim, half = hd >> 1;
     const int q_size = q.num_heads * hd, kv_size = q.num_kv_heads * hd;
-    const int n0 = tile * 128;
+    const int f = tid, F = tile * 128 + f;
+    const int d = F % hd;
+    const bool rope = F < q_size + kv_size, is_q = F < q_size, is_k = !is_q && rope;
+    const int dh = d < half ? d : d - half;
+    const int fp = d < half ? f + half : f - half;
+    const int g = is_q ? 0 : (is_k ? F - q_size : F - q_size - kv_size) / hd;
+    const bool pow2_page = (q.page_size & (q.page_size - 1)) == 0;
+    const int page_shift = __ffs(q.page_size) - 1;
     const T* cs_tab = reinterpret_cast<const T*>(q.cos_sin);
-    for (int idx = tid; idx < ncols * 128; idx += kGemmThreads) {
-      const int lc = idx >> 7, f = idx & 127;
+    T* plane = reinterpret_cast<T*>(is_k ? q.k_cache : q.v_cache);
+    // the last tile may run past n_out when (heads + 2 kv_heads) * head_dim is not a multiple of 128
+    for (int lc = 0; lc < (F < args.n_out ? ncols : 0); ++lc) {
       const int c = c_begin + lc;
-      const int F = n0 + f;
       const float x = round_to<T>(red[lc * kStagePad + f]);
-      const int d = F % hd;
       float y = x;
-      if (F < q_size + kv_size) {
-        const int pos = q.positions[c];
+      if (rope) {
+        const int pos = __ldg(q.positions + c);
         if (pos < 0 || pos >= q.max_pos) {
           record_error(args.err, kErrBadIndex);
           continue;
         }
-        const int dh = d < half ? d : d - half;
-        const int fp = d < half ? f + half : f - half;
         const float xp = round_to<T>(red[lc * kStagePad + fp]);
-        const float cv = to_f32<T>(cs_tab[size_t(pos) * hd + dh]);
-        const float sv = to_f32<T>(cs_tab[size_t(pos) * hd + half + dh]);
+        const float cv = to_f32<T>(__ldg(cs_tab + size_t(pos) * hd + dh));
+        const float sv = to_f32<T>(__ldg(cs_tab + size_t(pos) * hd + half + dh));
         y = d < half ? x * cv - xp * sv : x * cv + xp * sv;
       }
-      if (F < q_size) {
+      if (is_q) {
         reinterpret_cast<T*>(q.q_out)[size_t(c) * q_size + F] = from_f32<T>(y);
       } else {
-        const bool is_k = F < q_size + kv_size;
-        const int g = (is_k ? F - q_size : F - q_size - kv_size) / hd;
-        const int64_t slot = q.slots[c];
+        const int64_t slot = __ldg(q.slots + c);
         if (slot < 0 || slot >= q.num_slots) {
           record_error(args.err, kErrBadIndex);
           continue;
         }
-        const int64_t page = slot / q.page_size, within = slot % q.page_size;
-        T* plane = reinterpret_cast<T*>(is_k ? q.k_cache : q.v_cache);
+        const int64_t page = pow2_page ? slot >> page_shift : slot / q.page_size;
+        const int64_t within = pow2_page ? slot & (q.page_size - 1) : slot % q.page_size;
         plane[((page * q.num_kv_heads + g) * q.page_size + within) * hd + d] = from_f32<T>(y);
       }
     }

@@ -124,7 +124,9 @@ def _cos_sin(max_pos, hd, theta=10000.0):
     return torch.cat([f.cos(), f.sin()], dim=-1).to(torch.bfloat16).cuda()
 
 
-@pytest.mark.parametrize("heads,kv_heads,hd,rows,page", [(16, 16, 128, 56, 16), (8, 8, 64, 42, 16), (16, 4, 128, 56, 32)])
+# (3, 1, 64): n_out = 320 leaves the last 128-feature tile half empty; page 24 is not a power of two
+@pytest.mark.parametrize("heads,kv_heads,hd,rows,page", [(16, 16, 128, 56, 16), (8, 8, 64, 42, 16), (16, 4, 128, 56, 32),
+                                                         (3, 1, 64, 20, 16), (8, 8, 64, 42, 24)])
 def test_qkv_rope_kv_epilogue(ctx, heads, kv_heads, hd, rows, page):
     from plm import native
 
@@ -166,6 +168,7 @@ def test_qkv_rope_kv_epilogue(ctx, heads, kv_heads, hd, rows, page):
     mask = torch.ones(num_pages * page, dtype=torch.bool, device="cuda")
     mask[slots] = False
     assert torch.count_nonzero(k_cache.permute(0, 2, 1, 3).reshape(num_pages * page, -1)[mask]) == 0
+    assert torch.count_nonzero(v_cache.permute(0, 2, 1, 3).reshape(num_pages * page, -1)[mask]) == 0
 
 
 @pytest.mark.parametrize("n_verify,rows", [(7, 56), (1, 56), (1, 1), (6, 42)])
