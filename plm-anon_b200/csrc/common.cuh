@@ -117,10 +117,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 
 // ----------------------------------------------------------------------------------------------------------------
 // Hand-off between CTAs of one grid through global counters. The threads that store the data synchronise on a CTA
-// barrier, then one of them calls signal_stored: a gpu-scope fence and a release add, whose cumulativity covers the
-// stores the barrier ordered before it. The reader polls with acquire loads, synchronises its own threads on a
-// barrier, and before reading the data with the async proxy (TMA, bulk copies) orders that read after the acquire
-// with fence.proxy.async.global.
+// barrier, then one of them calls signal_stored: a gpu-scope acquire-release fence and a relaxed add (the release
+// pattern), whose cumulativity covers the stores the barrier ordered before it. The reader polls with acquire
+// loads, synchronises its own threads on a barrier, and before reading the data with the async proxy (TMA, bulk
+// copies) orders that read after the acquire with fence.proxy.async.global.
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -130,8 +130,7 @@ __device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void signal_stored(int* counter) {
-  __threadfence();
-  red_release_gpu_add(counter, 1);
+  asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.s32 [%0], 1;" ::"l"(counter) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
