@@ -426,7 +426,7 @@ def run_native(args) -> None:
     e2e_value = e2e_tokens / e2e_s if e2e_s else None
 
     cpu = None
-    if rank == 0 and not args.skip_cpu:
+    if rank == 0 and world == 1 and not args.skip_cpu:  # the CPU baseline is an N=1 figure
         _seed_context(decoder, cfg)
         cpu = cpu_baseline(weights, decoder, cfg, rounds=1)
 
