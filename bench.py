@@ -354,8 +354,11 @@ def run_reference(args) -> None:
 # + lm_head 209.7 MB. Used for the separate-launch configuration.
 GEMM_DRAM_BYTES_PER_ROUND = 3.495e9
 # DRAM bytes (read + write) of one layer-block launch of the benchmark shape, from one ncu capture
-# (profiles/layer_block_plm-1.3b_rows56.md): 109.80 MB read + 5.31 MB written.
-BLOCK_DRAM_BYTES_PER_LAUNCH = 115.1e6
+# (profiles/layer_block_plm-1.3b_rows56.md): 134.92 MB read + 5.08 MB written. The reads are the block's own
+# 109.7 MB (packed weights and row operands) plus the 25.2 MB of the next layer's qkv weights that its tail
+# prefetches into L2, which the qkv GEMM then reads from L2 instead of DRAM.
+BLOCK_DRAM_BYTES_PER_LAUNCH = 140.0e6
+BLOCK_PREFETCH_BYTES_PER_LAUNCH = 25.2e6
 
 
 def run_native(args) -> None:
@@ -447,6 +450,8 @@ def run_native(args) -> None:
             "roofline": {"bound": "hbm", "kernel": dom_kernel,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_kind, "traffic": dom_traffic,
+                         "traffic_prefetch": None if args.separate_mlp else
+                         BLOCK_PREFETCH_BYTES_PER_LAUNCH * cfg.num_layers,
                          "bytes_per_round": dom_bytes,
                          "ms_per_round": dom_ms, "launches_per_round": dom_launches},
             "round_roofline": {"bound": "hbm", "achieved": round_achieved, "peak": peak, "unit": "GB/s",
