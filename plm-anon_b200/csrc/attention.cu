@@ -393,13 +393,8 @@ template <int HD>
 int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool pdl) {
   constexpr int SMEM = 2 * kStages * kKeysPerTile * HD * 2 + kMaxPageSlice * 4;
   auto kernel = round_attention_kernel<HD>;
-  static bool attr = false;
-  if (!attr) {
-    int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
-                        "cudaFuncSetAttribute(attention smem)");
-    if (st != PLM_OK) return st;
-    attr = true;
-  }
+  const int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(attention smem)");
+  if (st != PLM_OK) return st;
   return check_cuda(launch_ex(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl,
                               a.splits, a),
                     "round_attention_kernel");

@@ -59,12 +59,9 @@ int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, c
   constexpr int STAGES = stages_for<NTOK, EPI>();
   constexpr int SMEM = gemm_smem_bytes<NTOK, STAGES>();
   auto kernel = skinny_gemm_kernel<T, NTOK, STAGES, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
-                        "cudaFuncSetAttribute(gemm smem)");
+  {
+    const int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(gemm smem)");
     if (st != PLM_OK) return st;
-    attr_set = true;
   }
   const int tiles = tiles_for(EPI, d.n_out, d.epi.gate_offset);
   const int total_kb = d.k / kGemmBK;

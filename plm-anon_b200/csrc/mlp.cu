@@ -606,18 +606,13 @@ template <typename T, int NTOK>
 int launch_block(const MlpSchedule& s, const BlockParams& p, cudaStream_t stream, bool pdl) {
   using S = MlpShape<NTOK>;
   auto kernel = mlp_block_kernel<T, NTOK>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM),
-                        "cudaFuncSetAttribute(block smem)");
-    if (st != PLM_OK) return st;
-    int per_sm = 0;
-    st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kMlpThreads, S::SMEM),
-                    "block occupancy");
-    if (st != PLM_OK) return st;
-    if (per_sm < 1) return fail(PLM_ERR_UNSUPPORTED, "layer block: %d bytes of shared memory do not fit", S::SMEM);
-    attr_set = true;
-  }
+  int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), S::SMEM, "cudaFuncSetAttribute(block smem)");
+  if (st != PLM_OK) return st;
+  int per_sm = 0;
+  st = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kMlpThreads, S::SMEM),
+                  "block occupancy");
+  if (st != PLM_OK) return st;
+  if (per_sm < 1) return fail(PLM_ERR_UNSUPPORTED, "layer block: %d bytes of shared memory do not fit", S::SMEM);
   return check_cuda(launch(kernel, dim3(s.grid), dim3(kMlpThreads), S::SMEM, stream, pdl, p),
                     "mlp_block_kernel launch");
 }

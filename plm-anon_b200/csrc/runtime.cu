@@ -1,7 +1,9 @@
 // Context lifetime, error reporting and TMA descriptor encoding for libplm_native.so.
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "runtime.h"
 
@@ -25,8 +27,7 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Split-reduction scratch of a context: enough for the widest launch of the round (lm_head over 50k features
-// at 3 splits and 64 rows is 38.6 MB).
+// Arrival counters of a context (zero between launches).
 constexpr int kCounters = 64;
 }  // namespace
 
@@ -44,6 +45,21 @@ int check_cuda(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return PLM_OK;
   return fail(e == cudaErrorMemoryAllocation ? PLM_ERR_NOMEM : PLM_ERR_CUDA, "%s: %s (%s)", what,
               cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int raise_smem_limit(const void* kernel, int bytes, const char* what) {
+  int dev = 0;
+  int st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (st != PLM_OK) return st;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> raised;  // (kernel, device) -> the limit set so far
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(kernel, dev);
+  const auto it = raised.find(key);
+  if (it != raised.end() && it->second >= bytes) return PLM_OK;
+  st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (st == PLM_OK) raised[key] = bytes;
+  return st;
 }
 
 int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,

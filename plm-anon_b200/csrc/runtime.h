@@ -35,6 +35,11 @@ int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
 
+// Raises `kernel`'s dynamic shared memory limit to at least `bytes` on the current device. The attribute belongs to
+// a (function, device) pair, so each device a process launches on gets its own call; later calls that need no more
+// than an earlier one return at once. Thread-safe.
+int raise_smem_limit(const void* kernel, int bytes, const char* what);
+
 // Launch with optional programmatic dependent launch and an optional cluster of cluster_x * cluster_y CTAs.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

@@ -1032,13 +1032,9 @@ template <typename T, int SL>
 int launch_verify(const VerifyArgs& a, int n_rows, cudaStream_t stream, bool pdl) {
   const size_t smem = sizeof(VerifySmem);
   auto kernel = verify_decode_kernel<T, SL>;
-  static bool attr = false;
-  if (!attr) {
-    int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                        "cudaFuncSetAttribute(verify smem)");
-    if (st != PLM_OK) return st;
-    attr = true;
-  }
+  const int st =
+      raise_smem_limit(reinterpret_cast<const void*>(kernel), int(smem), "cudaFuncSetAttribute(verify smem)");
+  if (st != PLM_OK) return st;
   return check_cuda(launch_cluster(kernel, dim3(kCluster * n_rows), dim3(kThreads), smem, stream, pdl, kCluster, 1, a),
                     "verify_decode_kernel");
 }
