@@ -13,7 +13,8 @@ a rounding point here too (``_r``). The paged KV cache has the GPU's layout
 
 RoundOracle strings the pieces into the RoundDecoder of plm/decoder.py: prefill (369-403, first token 384),
 round 0 (275-310) and steady rounds (312-365), with the verify decode of ``oracle.voronoi`` and the bookkeeping of
-``oracle.rounds``.
+``oracle.rounds``. Given a ``ptp.PTPScheme`` (and optionally adapters) the model is instead the gated-LoRA PTP model
+of ``oracle.ptp``: blended auxiliary inputs, adapters on the gated rows and the inverse-CDF verify decode.
 """
 
 from __future__ import annotations
@@ -24,6 +25,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from . import ptp as optp
 from . import rounds as orounds
 from . import voronoi as ov
 
@@ -58,9 +60,12 @@ class OracleModel:
     """Llama forward over a paged KV cache; ``weights`` maps the Llama / auxiliary-scheme names to CPU tensors."""
 
     def __init__(self, shape: ModelShape, weights: dict, dtype: str, page_size: int, num_pages: int,
-                 block_table: np.ndarray, cos_sin: torch.Tensor | None = None, accumulate: str = "float32"):
+                 block_table: np.ndarray, cos_sin: torch.Tensor | None = None, accumulate: str = "float32",
+                 ptp: "optp.PTPScheme | None" = None, adapters: "list[dict] | None" = None):
         """``accumulate="float64"`` runs every matmul and attention product in double precision (then rounds to
-        float32): the same model with another summation order, to measure how far rounding alone moves the output."""
+        float32): the same model with another summation order, to measure how far rounding alone moves the output.
+        ``ptp``: the linear-interpolation scheme replaces the logit-Voronoi auxiliary inputs; ``adapters``: per layer,
+        projection name ("qkv", "o", "gate_up", "down") -> ``optp.Adapter``, applied on the gated rows."""
         self.s, self.dtype, self.tdtype = shape, dtype, TORCH_DTYPES[dtype]
         self.acc = torch.float64 if accumulate == "float64" else torch.float32
         f = lambda t: t.detach().to("cpu", torch.float32)  # noqa: E731
@@ -77,6 +82,8 @@ class OracleModel:
         self.page_size, self.num_pages = page_size, num_pages
         self.block_table = np.asarray(block_table, dtype=np.int64)
         self.kv = torch.zeros(shape.num_layers, 2, num_pages, shape.num_kv_heads, page_size, shape.head_dim)
+        self.ptp = ptp
+        self.adapters = adapters if adapters is not None else [{} for _ in range(shape.num_layers)]
 
     # ------------------------------------------------------------------ helpers
     def _r(self, x: torch.Tensor) -> torch.Tensor:
@@ -98,20 +105,30 @@ class OracleModel:
         return pages, logical % self.page_size
 
     def embed_rows(self, ids: np.ndarray, aux_values: np.ndarray) -> torch.Tensor:
-        """plm/decoder.py:264-268 with LogitVoronoiAuxiliary.embed (plm/auxiliary.py:50-54)."""
+        """plm/decoder.py:264-268 with LogitVoronoiAuxiliary.embed (plm/auxiliary.py:50-54), or with the PTP
+        scheme's blend cast to the model dtype."""
         V, A = self.s.vocab, self.s.aux_vocab
         ids = torch.as_tensor(ids, dtype=torch.int64)
-        values = torch.as_tensor(aux_values, dtype=torch.int64)
         aux_mask = (ids >= V) & (ids < V + self.s.num_aux_tokens)
         token = self.embed[ids.masked_fill(aux_mask, 0).clamp(0, V - 1)]
+        if self.ptp is not None:
+            blend = optp.linear_interpolation_embed(np.asarray(aux_values, dtype=np.float32), self.ptp.embedding)
+            return torch.where(aux_mask[:, None], self._r(torch.from_numpy(blend)), token)
+        values = torch.as_tensor(aux_values, dtype=torch.int64)
         vectors = self.aux_vocab[values.clamp(max=A - 1).clamp(min=0)]
         vectors = torch.where((values == A)[:, None], self.mask_aux[None, :], vectors)
         return torch.where(aux_mask[:, None], vectors, token)
 
+    def _proj(self, index: int, name: str, x: torch.Tensor, gated_from: int | None) -> torch.Tensor:
+        """One projection of layer ``index`` in the model dtype, with its adapters on the gated rows."""
+        weight = self.layers[index][name]
+        return optp.gated_projection(x, weight, self.adapters[index].get(name), gated_from, self._r, self._mm)
+
     # ------------------------------------------------------------------ forward
     def forward(self, embeds: torch.Tensor, positions: np.ndarray, offset: int, depth: np.ndarray,
-                own_start: np.ndarray) -> torch.Tensor:
-        """Rows at logical KV indices offset + r; writes their K/V into the cache; returns the final-norm output."""
+                own_start: np.ndarray, gated_from: int | None = None) -> torch.Tensor:
+        """Rows at logical KV indices offset + r; writes their K/V into the cache; returns the final-norm output.
+        ``gated_from``: the first row the adapters apply to (None: none)."""
         s = self.s
         rows, hd = embeds.shape[0], s.head_dim
         half = hd // 2
@@ -128,7 +145,7 @@ class OracleModel:
         residual = embeds.clone()
         x = self._rmsnorm(residual, self.layers[0]["input_norm"])
         for index, layer in enumerate(self.layers):
-            qkv = self._r(self._mm(x, layer["qkv"].T))
+            qkv = self._proj(index, "qkv", x, gated_from)
             q = qkv[:, :q_size].view(rows, s.num_heads, hd)
             k = qkv[:, q_size:q_size + kv_size].view(rows, s.num_kv_heads, hd)
             v = qkv[:, q_size + kv_size:].view(rows, s.num_kv_heads, hd)
@@ -148,14 +165,14 @@ class OracleModel:
             scores = scores.masked_fill(~mask[None], float("-inf"))
             probs = torch.softmax(scores, dim=-1)
             attn = self._r(self._einsum("hrk,khd->rhd", probs, values).reshape(rows, q_size))
-            y = self._r(self._mm(attn, layer["o"].T))
+            y = self._proj(index, "o", attn, gated_from)
             summed = y + residual
             residual = self._r(summed)
             x = self._rmsnorm(summed, layer["post_norm"])
-            gu = self._r(self._mm(x, layer["gate_up"].T))
+            gu = self._proj(index, "gate_up", x, gated_from)
             gate, up = gu[:, : s.intermediate], gu[:, s.intermediate:]
             act = self._r(gate / (1.0 + torch.exp(-gate)) * up)
-            y = self._r(self._mm(act, layer["down"].T))
+            y = self._proj(index, "down", act, gated_from)
             summed = y + residual
             residual = self._r(summed)
             weight = self.layers[index + 1]["input_norm"] if index + 1 < len(self.layers) else self.final_norm
@@ -173,24 +190,32 @@ class RoundOracle:
     def __init__(self, model: OracleModel, table: np.ndarray, k: int, rule: str = "nucleus",
                  threshold: float | None = None, config: ov.VoronoiConfig = ov.VoronoiConfig(),
                  capacity: int = 4096, aux_stream: np.ndarray | None = None):
-        self.model, self.table, self.k, self.width = model, np.asarray(table, dtype=np.float32), k, k + k * k
+        self.model, self.k, self.width = model, k, k + k * k
+        self.table = None if table is None else np.asarray(table, dtype=np.float32)  # unused by the PTP scheme
         self.rule, self.threshold = rule, (-1.0 if threshold is None else float(threshold))
         self.config = config
         self.state = orounds.RoundState(k, capacity)
-        self.aux = np.zeros(orounds.AUX_STREAM_LENGTH, dtype=np.int64) if aux_stream is None else aux_stream
+        self.ptp = model.ptp
+        # the PTP scheme streams uniforms and gives non-auxiliary rows the value 0 (plm/decoder.py:107-108, 137)
+        stream_dtype = np.float32 if self.ptp is not None else np.int64
+        self.sentinel = 0 if self.ptp is not None else model.s.aux_vocab
+        self.aux = np.zeros(orounds.AUX_STREAM_LENGTH, dtype=stream_dtype) if aux_stream is None else aux_stream
         self.steady = orounds.steady_layout(k)
         self.r0 = orounds.round0_layout(k)
         self.last_logits = None
         self.last_hidden = None
 
-    def decode(self, logits_row: np.ndarray, cell: int) -> int:
-        return ov.decode_row(logits_row, self.table, int(cell), self.model.dtype, self.config).token
+    def decode(self, logits_row: np.ndarray, value) -> int:
+        """The verify decode of one row: the Voronoi cell's token, or the PTP scheme's inverse CDF at u."""
+        if self.ptp is not None:
+            return optp.icdf_decode_row(logits_row, float(value), self.ptp.top_k)
+        return ov.decode_row(logits_row, self.table, int(value), self.model.dtype, self.config).token
 
     # ---- forward halves (write KV, return the final-norm hidden rows and their logits) ----
     def prefill_forward(self, prompt: np.ndarray, chunk: int = 256):
         """Causal prefill in chunks (plm/decoder.py:369-403); returns (hidden, logits) of the last prompt row."""
         prompt = np.asarray(prompt, dtype=np.int64)
-        n, sentinel = prompt.size, self.model.s.aux_vocab
+        n, sentinel = prompt.size, self.sentinel
         for start in range(0, n, chunk):
             rows = min(chunk, n - start)
             _, _, depth, own = orounds.chunk_layout(rows)
@@ -201,15 +226,16 @@ class RoundOracle:
 
     def round0_forward(self):
         st, layout = self.state, self.r0
-        ids, values, positions, _ = orounds.round0_prologue(st, layout, self.model.s.vocab, self.model.s.aux_vocab,
-                                                            self.aux)
-        hidden = self.model.forward(self.model.embed_rows(ids, values), positions, st.offset, layout[2], layout[3])
+        ids, values, positions, _ = orounds.round0_prologue(st, layout, self.model.s.vocab, self.sentinel, self.aux)
+        hidden = self.model.forward(self.model.embed_rows(ids, values), positions, st.offset, layout[2], layout[3],
+                                    gated_from=1)
         return hidden, self.model.logits(hidden).numpy()
 
     def round_forward(self):
         st, layout = self.state, self.steady
-        ids, values, positions, _ = orounds.prologue(st, layout, self.model.s.vocab, self.model.s.aux_vocab, self.aux)
-        hidden = self.model.forward(self.model.embed_rows(ids, values), positions, st.offset, layout[2], layout[3])
+        ids, values, positions, _ = orounds.prologue(st, layout, self.model.s.vocab, self.sentinel, self.aux)
+        hidden = self.model.forward(self.model.embed_rows(ids, values), positions, st.offset, layout[2], layout[3],
+                                    gated_from=self.k)
         return hidden, self.model.logits(hidden).numpy()
 
     # ---- commits (acceptance / bookkeeping on given logits) ----

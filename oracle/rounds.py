@@ -102,7 +102,7 @@ def prologue(state: RoundState, layout, vocab: int, sentinel: int, aux_buf: np.n
     aux_values = np.where(rel_aux < 0, sentinel, aux_buf[np.maximum(aux_index, 0)])
     positions = rel_positions + state.offset
     slots = state.offset + np.arange(width, dtype=np.int64)
-    return ids, aux_values.astype(np.int64), positions, slots
+    return ids, aux_values.astype(aux_buf.dtype), positions, slots
 
 
 def round0_prologue(state: RoundState, layout, vocab: int, sentinel: int, aux_buf: np.ndarray):
@@ -113,7 +113,7 @@ def round0_prologue(state: RoundState, layout, vocab: int, sentinel: int, aux_bu
     ids[0] = state.anchor
     aux_index = state.base + rel_aux
     aux_values = np.where(rel_aux < 0, sentinel, aux_buf[np.maximum(aux_index, 0)])
-    return ids, aux_values.astype(np.int64), rel_positions + state.offset, state.offset + np.arange(width)
+    return ids, aux_values.astype(aux_buf.dtype), rel_positions + state.offset, state.offset + np.arange(width)
 
 
 def epilogue(state: RoundState, verify: np.ndarray, accepted_rule: np.ndarray, proposal_argmax: np.ndarray) -> int:

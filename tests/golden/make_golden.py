@@ -13,7 +13,10 @@ running its own functions on the CPU:
                     kernels run by the Triton interpreter (TRITON_INTERPRET=1; autotuning bypassed with fixed launch
                     meta GROUP=8, BLOCK=32; the compiled argmin replaced by its eager implementation);
   llama.npz         the Llama forward of Hugging Face transformers (LlamaForCausalLM, eager attention, fp32) over a
-                    prompt plus one round under the round mask, pinning the oracle's paged forward.
+                    prompt plus one round under the round mask, pinning the oracle's paged forward;
+  ptp.npz           the PTP scheme of the gated-LoRA model: LinearInterpolationAuxiliary.embed / decode_unmasked
+                    (plm/auxiliary.py) and GatedLoraMethod.apply under gated_lora.rows_from (plm/gated_lora.py; its
+                    GEMMs are vLLM's default unquantized GEMM, torch.nn.functional.linear, on the CPU).
 Inputs that are large (logits rows, cost tables, model weights) are regenerated from the stored seeds by torch's CPU
 generator, which is deterministic across machines; fixtures store their checksums so tests can confirm.
 """
@@ -79,6 +82,37 @@ VORONOI_CASES = [  # seed, rows, vocab, aux, kind
     (103, 2, 8000, 512, "bf16"),
 ]
 ACCEPT_CASES = [(200, 6, 50257), (201, 6, 4096)]
+
+
+PTP_EMBED = (500, 24, 32, 3)                 # seed, values, hidden, embedding rows
+PTP_DECODE = ((510, 16, 300, 16), (511, 16, 300, 128), (512, 4, 1000, 128))  # seed, rows, vocab, top_k
+PTP_GATED = ((520, "float32"), (521, "bfloat16"))  # seed, dtype; shapes in ptp_gated_inputs
+PTP_GATED_SHAPE = dict(rows=10, rows_from=3, d_in=64, shards=(48, 16, 16), rank=8)
+
+
+def ptp_embed_inputs(seed: int, n: int, hidden: int, rows: int):
+    g = torch.Generator().manual_seed(seed)
+    table = torch.randn(rows, hidden, generator=g)
+    values = torch.rand(n, generator=g)
+    values[:6] = torch.tensor([0.0, 0.25, 0.5, 0.75, 1e-8, 0.99999994])
+    return table, values
+
+
+def ptp_decode_inputs(seed: int, n: int, vocab: int):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(n, vocab, generator=g) * 3.0).bfloat16().float(), torch.rand(n, generator=g)
+
+
+def ptp_gated_inputs(seed: int, dtype: str):
+    sh = PTP_GATED_SHAPE
+    g = torch.Generator().manual_seed(seed)
+    dt = getattr(torch, dtype)
+    n_out = sum(sh["shards"])
+    x = torch.randn(sh["rows"], sh["d_in"], generator=g).to(dt)
+    weight = (torch.randn(n_out, sh["d_in"], generator=g) * 0.05).to(dt)
+    lora_a = (torch.randn(len(sh["shards"]) * sh["rank"], sh["d_in"], generator=g) * 0.1).to(dt)
+    lora_bs = [(torch.randn(w, sh["rank"], generator=g) * 0.1).to(dt) for w in sh["shards"]]
+    return x, weight, lora_a, lora_bs
 
 
 def checksum(t: torch.Tensor) -> float:
@@ -281,6 +315,43 @@ def gen_llama(ref, out: Path):
                         prompt_len=prompt_len, **{f"cfg_{key}": value for key, value in c.items()})
 
 
+def gen_ptp(ref, out: Path):
+    from plm import gated_lora
+    from plm.auxiliary import LinearInterpolationAuxiliary
+
+    res = {}
+    seed, n, hidden, rows = PTP_EMBED
+    table, values = ptp_embed_inputs(seed, n, hidden, rows)
+    scheme = LinearInterpolationAuxiliary(hidden_size=hidden, text_vocab_size=100, num_embeddings=rows, top_k=16)
+    with torch.no_grad():
+        scheme.embedding.weight.copy_(table)
+        ids = torch.full((n,), 100, dtype=torch.long)
+        res["embed/out"] = scheme.embed(ids, values, ids == 100).numpy()
+    res["embed/checksum"] = np.asarray(checksum(table) + checksum(values))
+    for seed, n, vocab, top_k in PTP_DECODE:
+        logits, u = ptp_decode_inputs(seed, n, vocab)
+        scheme = LinearInterpolationAuxiliary(hidden_size=8, text_vocab_size=vocab, top_k=top_k)
+        res[f"decode/{seed}/tokens"] = scheme.decode_unmasked(logits, None, None, u).numpy()
+        res[f"decode/{seed}/checksum"] = np.asarray(checksum(logits) + checksum(u))
+
+    class PlainLinear:  # the wrapped layer's own linear method
+        def apply(self, layer, x, bias=None):
+            return torch.nn.functional.linear(x, layer.weight, bias)
+
+    for seed, dtype in PTP_GATED:
+        x, weight, lora_a, lora_bs = ptp_gated_inputs(seed, dtype)
+        layer = torch.nn.Module()
+        layer.weight = torch.nn.Parameter(weight, requires_grad=False)
+        layer.register_buffer("lora_a", lora_a, persistent=False)
+        method = gated_lora.GatedLoraMethod(PlainLinear(), lora_bs)
+        with torch.no_grad(), gated_lora.rows_from(PTP_GATED_SHAPE["rows_from"]):
+            res[f"gated/{seed}/out"] = method.apply(layer, x).float().numpy()
+        with torch.no_grad(), gated_lora.rows_from(None):
+            res[f"gated/{seed}/ungated"] = method.apply(layer, x).float().numpy()
+        res[f"gated/{seed}/checksum"] = np.asarray(checksum(x.float()) + checksum(weight.float()))
+    np.savez_compressed(out / "ptp.npz", **res)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--reference", required=True, help="checkout of justuswill/PLM-anon")
@@ -291,7 +362,7 @@ def main() -> None:
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     gens = {"layout": gen_layout, "quota": gen_quota, "accept": gen_accept, "epilogue": gen_epilogue,
-            "voronoi": gen_voronoi, "llama": gen_llama}
+            "voronoi": gen_voronoi, "llama": gen_llama, "ptp": gen_ptp}
     for name, fn in gens.items():
         if args.only is None or name in args.only:
             fn(args.reference, out)
