@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 3
+#define PLM_ABI_VERSION 4
 
 enum plm_status {
   PLM_OK = 0,
@@ -308,6 +308,23 @@ int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* desc, void* stream);
  * (with that device current) resolves the scratch's address with cudaGetSymbolAddress, so make it before any stream
  * capture. Calls on one device share the scratch: overlapping calls (other streams or threads) race. */
 int plm_verify_decode_static(const plm_verify_desc* desc, int32_t* device_error, void* stream);
+
+/* The PTP scheme's verify decode (plm/auxiliary.py:104-113, LinearInterpolationAuxiliary.decode_unmasked, which
+ * the reference's RoundDecoder calls through _decode_verify at plm/decoder.py:260-262): per row, the softmax at
+ * temperature 1, its top_k largest probabilities in token-id order renormalised, and the token of the first bin
+ * whose right edge exceeds u[row] (the last edge is 1; ties at the top_k-th probability go to the lowest ids). */
+typedef struct plm_icdf_desc {
+  const float* logits; /* [n_rows][ld] float32 */
+  int64_t ld;
+  const float* u;      /* [n_rows] uniforms in [0, 1) */
+  int32_t n_rows;
+  int32_t vocab;       /* 1..53248 */
+  int32_t top_k;       /* 1..256, at most vocab */
+  int64_t* tokens;     /* [n_rows] out */
+  int32_t* ids_out;    /* optional [n_rows][top_k] out: the chosen ids, ascending */
+  float* edges_out;    /* optional [n_rows][top_k] out: the right bin edges */
+} plm_icdf_desc;
+int plm_icdf_decode(plm_ctx* ctx, const plm_icdf_desc* desc, void* stream);
 int plm_attention(plm_ctx* ctx, const plm_attention_desc* desc, void* stream);
 int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* desc, void* stream);
 int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* desc, void* stream);

@@ -99,6 +99,11 @@ class ModelDesc(ctypes.Structure):
                 ("endpoint", ctypes.c_double)]
 
 
+class IcdfDesc(ctypes.Structure):
+    _fields_ = [("logits", c_void_p), ("ld", c_int64), ("u", c_void_p), ("n_rows", c_int32), ("vocab", c_int32),
+                ("top_k", c_int32), ("tokens", c_void_p), ("ids_out", c_void_p), ("edges_out", c_void_p)]
+
+
 class WeightPtrs(ctypes.Structure):
     _fields_ = [("embed", c_void_p), ("lm_head", c_void_p), ("final_norm", c_void_p), ("aux_vocab", c_void_p),
                 ("mask_aux", c_void_p), ("cos_sin", c_void_p), ("qkv", POINTER(c_void_p)), ("o", POINTER(c_void_p)),
@@ -139,6 +144,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_attention": [c_void_p, POINTER(AttentionDesc), c_void_p],
     "plm_kv_append": [c_void_p, POINTER(KvAppendDesc), c_void_p],
     "plm_add_rmsnorm": [c_void_p, POINTER(AddRmsNormDesc), c_void_p],
+    "plm_icdf_decode": [c_void_p, POINTER(IcdfDesc), c_void_p],
     "plm_create": [POINTER(ModelDesc), POINTER(WeightPtrs), POINTER(RoundDesc), POINTER(c_void_p)],
     "plm_destroy": [c_void_p],
     "plm_set_block_table": [c_void_p, POINTER(c_int32), c_int32],
@@ -256,6 +262,16 @@ def kv_append(ctx: Context, desc: KvAppendDesc, stream=None) -> None:
 
 def add_rmsnorm(ctx: Context, desc: AddRmsNormDesc, stream=None) -> None:
     check(library().plm_add_rmsnorm(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_add_rmsnorm")
+
+
+def icdf_decode(ctx: Context, logits, u, top_k: int, tokens, ids_out=None, edges_out=None, stream=None) -> None:
+    """The PTP scheme's inverse-CDF verify decode of ``logits`` ([rows, vocab] float32 on the device) at the
+    uniforms ``u`` ([rows] float32) into ``tokens`` ([rows] int64); optionally the chosen ids and bin edges."""
+    desc = IcdfDesc(logits=logits.data_ptr(), ld=logits.stride(0), u=u.data_ptr(), n_rows=logits.shape[0],
+                    vocab=logits.shape[1], top_k=top_k, tokens=tokens.data_ptr(),
+                    ids_out=None if ids_out is None else ids_out.data_ptr(),
+                    edges_out=None if edges_out is None else edges_out.data_ptr())
+    check(library().plm_icdf_decode(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_icdf_decode")
 
 
 class _DeviceArray:
