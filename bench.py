@@ -350,11 +350,11 @@ def run_reference(args) -> None:
 
 
 # DRAM bytes (read + write) of the weight GEMMs of one round of the benchmark shape, from one ncu capture of each
-# GEMM shape (profiles/skinny_gemm_plm-1.3b_rows56.md): 24 x (qkv 25.47 + o 8.69 + gate_up 68.12 + down 34.64) MB
-# + lm_head 209.7 MB. Used for the separate-launch configuration.
+# GEMM shape at 56 rows: 24 x (qkv 25.47 + o 8.69 + gate_up 68.12 + down 34.64) MB + lm_head 209.7 MB. Used for the
+# separate-launch configuration.
 GEMM_DRAM_BYTES_PER_ROUND = 3.495e9
-# DRAM bytes (read + write) of one layer-block launch of the benchmark shape, from one ncu capture
-# (profiles/layer_block_plm-1.3b_rows56.md): 134.92 MB read + 5.08 MB written. The reads are the block's own
+# DRAM bytes (read + write) of one layer-block launch of the benchmark shape, from one ncu capture of a block of a
+# 2-layer model of the same shape: 134.92 MB read + 5.08 MB written. The reads are the block's own
 # 109.7 MB (packed weights and row operands) plus the 25.2 MB of the next layer's qkv weights that its tail
 # prefetches into L2, which the qkv GEMM then reads from L2 instead of DRAM.
 BLOCK_DRAM_BYTES_PER_LAUNCH = 140.0e6
