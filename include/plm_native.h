@@ -347,6 +347,14 @@ int plm_round(plm_handle* h, void* stream);
  * updating the residual and the down partials. For measurement and tests; PLM_ERR_UNSUPPORTED when the handle was
  * created with separate_mlp. */
 int plm_layer_block(plm_handle* h, int32_t layer, int32_t rows, void* stream);
+/* The layer block's unit schedule for num_sms CTAs (host only: no device is touched). No counterpart in the
+ * reference: it exposes how plm_layer_block spreads o / norm / gate_up / down work over the SMs, for tests and
+ * inspection. units gets *n_units codes, CTA after CTA; offsets[c] .. offsets[c + 1] are CTA c's (offsets has
+ * num_sms + 1 entries). A code holds the kind in bits 28-29 (0 gate_up tile, 1 down unit, 2 o unit, 3 norm row),
+ * the tile (the row of a norm unit) in bits 12-27 and the k-split in bits 0-11. PLM_ERR_INVALID with *n_units set
+ * when capacity is too small; PLM_ERR_UNSUPPORTED for shapes the block does not take. */
+int plm_block_schedule(int32_t num_sms, int32_t hidden, int32_t intermediate, int32_t q_size, int32_t* units,
+                       int32_t capacity, int32_t* offsets, int32_t* n_units);
 int plm_state(plm_handle* h, plm_state_ptrs* out);
 int plm_check(plm_handle* h, int32_t* device_error);
 

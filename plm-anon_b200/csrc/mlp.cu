@@ -562,20 +562,27 @@ std::vector<int> mlp_schedule_units(const MlpSchedule& s, int hidden, int interm
   return flat;
 }
 
-int mlp_schedule_create(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out) {
+int mlp_schedule_plan(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out) {
   *out = MlpSchedule{};
   constexpr int kPair = kMlpStageKb * kGemmBK;
-  if (hidden % kPair != 0 || intermediate % kPair != 0 || q_size % kPair != 0 || hidden > 8 * 256 * 2 ||
-      intermediate / 64 >= (1 << 16))
-    return fail(PLM_ERR_UNSUPPORTED, "layer block: hidden %d, intermediate %d, q_size %d", hidden, intermediate,
-                q_size);
+  if (num_sms < 1 || hidden < kPair || intermediate < kPair || q_size < kPair || hidden % kPair != 0 ||
+      intermediate % kPair != 0 || q_size % kPair != 0 || hidden > 8 * 256 * 2 || intermediate / 64 >= (1 << 16))
+    return fail(PLM_ERR_UNSUPPORTED, "layer block: %d SMs, hidden %d, intermediate %d, q_size %d", num_sms, hidden,
+                intermediate, q_size);
+  out->grid = num_sms;
+  out->gate_tiles = intermediate / 64;
+  out->down_tiles = (hidden + 127) / 128;
+  out->down_splits = std::min(kMlpMaxDownSplits, intermediate / kPair);
+  out->o_tiles = (hidden + 127) / 128;
+  out->o_splits = std::max(1, std::min({kMlpMaxOSplits, q_size / kPair, num_sms / out->o_tiles}));
+  return PLM_OK;
+}
+
+int mlp_schedule_create(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out) {
   MlpSchedule s;
-  s.grid = num_sms;
-  s.gate_tiles = intermediate / 64;
-  s.down_tiles = (hidden + 127) / 128;
-  s.down_splits = std::min(kMlpMaxDownSplits, intermediate / kPair);
-  s.o_tiles = (hidden + 127) / 128;
-  s.o_splits = std::max(1, std::min({kMlpMaxOSplits, q_size / kPair, num_sms / s.o_tiles}));
+  int plan = mlp_schedule_plan(num_sms, hidden, intermediate, q_size, &s);
+  *out = MlpSchedule{};
+  if (plan != PLM_OK) return plan;
   std::vector<int> offsets;
   std::vector<int> units = mlp_schedule_units(s, hidden, intermediate, q_size, &offsets);
   int st = check_cuda(cudaMalloc(&s.sched, units.size() * sizeof(int)), "block schedule");
@@ -647,3 +654,22 @@ int mlp_block_launch(const MlpSchedule& s, BlockParams p, int dtype, cudaStream_
 }
 
 }  // namespace plm
+
+using namespace plm;
+
+extern "C" int plm_block_schedule(int32_t num_sms, int32_t hidden, int32_t intermediate, int32_t q_size,
+                                  int32_t* units, int32_t capacity, int32_t* offsets, int32_t* n_units) {
+  if (!offsets || !n_units || (capacity > 0 && !units))
+    return fail(PLM_ERR_INVALID, "plm_block_schedule: null argument");
+  MlpSchedule s;
+  int st = mlp_schedule_plan(num_sms, hidden, intermediate, q_size, &s);
+  if (st != PLM_OK) return st;
+  std::vector<int> off;
+  const std::vector<int> flat = mlp_schedule_units(s, hidden, intermediate, q_size, &off);
+  *n_units = int32_t(flat.size());
+  if (capacity < int32_t(flat.size()))
+    return fail(PLM_ERR_INVALID, "plm_block_schedule: %zu units, capacity %d", flat.size(), capacity);
+  std::copy(flat.begin(), flat.end(), units);
+  std::copy(off.begin(), off.end(), offsets);
+  return PLM_OK;
+}

@@ -58,6 +58,9 @@ struct BlockParams {
 // Assignment of units to `grid` CTAs (deterministic); see mlp.cu.
 std::vector<int> mlp_schedule_units(const MlpSchedule& s, int hidden, int intermediate, int q_size,
                                     std::vector<int>* offsets);
+// The schedule's sizes for a shape (host only, nothing allocated); PLM_ERR_UNSUPPORTED for shapes the block
+// does not take.
+int mlp_schedule_plan(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out);
 int mlp_schedule_create(int num_sms, int hidden, int intermediate, int q_size, MlpSchedule* out);
 void mlp_schedule_destroy(MlpSchedule* s);
 // One launch of the block for `p.rows` (1..kMlpMaxRows) rows; fills the schedule fields of `p`.

@@ -145,6 +145,8 @@ _SIGNATURES: dict[str, list] = {
     "plm_kv_append": [c_void_p, POINTER(KvAppendDesc), c_void_p],
     "plm_add_rmsnorm": [c_void_p, POINTER(AddRmsNormDesc), c_void_p],
     "plm_icdf_decode": [c_void_p, POINTER(IcdfDesc), c_void_p],
+    "plm_block_schedule": [c_int32, c_int32, c_int32, c_int32, POINTER(c_int32), c_int32, POINTER(c_int32),
+                           POINTER(c_int32)],
     "plm_create": [POINTER(ModelDesc), POINTER(WeightPtrs), POINTER(RoundDesc), POINTER(c_void_p)],
     "plm_destroy": [c_void_p],
     "plm_set_block_table": [c_void_p, POINTER(c_int32), c_int32],
@@ -262,6 +264,20 @@ def kv_append(ctx: Context, desc: KvAppendDesc, stream=None) -> None:
 
 def add_rmsnorm(ctx: Context, desc: AddRmsNormDesc, stream=None) -> None:
     check(library().plm_add_rmsnorm(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_add_rmsnorm")
+
+
+def block_schedule(num_sms: int, hidden: int, intermediate: int, q_size: int) -> list[list[int]]:
+    """The layer block's unit codes per CTA (host only; see plm_block_schedule)."""
+    lib = library()
+    n = c_int32(0)
+    offsets = (c_int32 * (num_sms + 1))()
+    status = lib.plm_block_schedule(num_sms, hidden, intermediate, q_size, None, 0, offsets, ctypes.byref(n))
+    if status != 0 and n.value == 0:
+        check(status, "plm_block_schedule")
+    units = (c_int32 * n.value)()
+    check(lib.plm_block_schedule(num_sms, hidden, intermediate, q_size, units, n.value, offsets, ctypes.byref(n)),
+          "plm_block_schedule")
+    return [list(units[offsets[c]:offsets[c + 1]]) for c in range(num_sms)]
 
 
 def icdf_decode(ctx: Context, logits, u, top_k: int, tokens, ids_out=None, edges_out=None, stream=None) -> None:

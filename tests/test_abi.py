@@ -35,12 +35,12 @@ def test_library_exports_every_declared_symbol():
 
 STRUCTS = ["plm_gemm_epilogue", "plm_gemm_desc", "plm_bookkeeping", "plm_verify_desc", "plm_attention_desc",
            "plm_kv_append_desc", "plm_add_rmsnorm_desc", "plm_model_desc", "plm_weight_ptrs", "plm_round_desc",
-           "plm_state_ptrs"]
+           "plm_state_ptrs", "plm_icdf_desc"]
 MIRRORS = {"plm_gemm_epilogue": "GemmEpilogue", "plm_gemm_desc": "GemmDesc", "plm_bookkeeping": "Bookkeeping",
            "plm_verify_desc": "VerifyDesc", "plm_attention_desc": "AttentionDesc",
            "plm_kv_append_desc": "KvAppendDesc", "plm_add_rmsnorm_desc": "AddRmsNormDesc",
            "plm_model_desc": "ModelDesc", "plm_weight_ptrs": "WeightPtrs", "plm_round_desc": "RoundDesc",
-           "plm_state_ptrs": "StatePtrs"}
+           "plm_state_ptrs": "StatePtrs", "plm_icdf_desc": "IcdfDesc"}
 
 
 def test_ctypes_structs_match_c_layout(tmp_path):
