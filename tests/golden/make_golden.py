@@ -9,6 +9,8 @@ running its own functions on the CPU:
   accept.npz        plm.decoder.nucleus_acceptance / floor_acceptance on seeded logits;
   epilogue.npz      RoundDecoder._epilogue (steady round bookkeeping) and _prologue (ids, aux cells, embeddings,
                     positions, slots), called unbound on CPU tensors with a stand-in ``self``;
+  round0.npz        RoundDecoder._round0 (round 0's inputs and commit) called unbound with a stand-in ``self`` whose
+                    forward, logits and verify decode return seeded values;
   voronoi.npz       Voronoi.assign through LogitVoronoiAuxiliary (plm/iterate.py, plm/auxiliary.py) with the Triton
                     kernels run by the Triton interpreter (TRITON_INTERPRET=1; autotuning bypassed with fixed launch
                     meta GROUP=8, BLOCK=32; the compiled argmin replaced by its eager implementation);
@@ -227,6 +229,69 @@ def gen_epilogue(ref, out: Path):
     np.savez_compressed(out / "epilogue.npz", **records)
 
 
+ROUND0_CASES = ((600, 7, 45), (601, 4, 300), (602, 6, 1))  # seed, k, prompt length
+
+
+def gen_round0(ref, out: Path):
+    """RoundDecoder._round0 of plm/decoder.py, unbound, with the model calls stubbed by seeded values."""
+    from plm.decoder import RoundDecoder
+    from plm.mask import round_layout
+
+    records = {}
+    vocab, bs = 50257, 16
+    for seed, k, prompt_len in ROUND0_CASES:
+        width = k + k * k
+        logits, verify_token, first, aux_buf = round0_inputs(seed, k, vocab)
+        seen = {}
+
+        def embed(ids, aux_values):
+            seen["ids"], seen["aux_values"] = ids.clone(), aux_values.clone()
+            return torch.zeros(ids.numel(), 4)
+
+        def forward(md, slot_mapping, num_tokens, positions, embeds, gated_from=None):
+            seen["positions"], seen["slot_mapping"], seen["gated_from"] = positions.clone(), slot_mapping.clone(), gated_from
+            return torch.zeros(num_tokens, 4)
+
+        def decode_verify(lg, hidden, index):
+            seen["verify_index"] = index.clone()
+            return verify_token.clone()
+
+        fake = types.SimpleNamespace(
+            k=k, width=width, block_size=bs, vocab=vocab, sentinel=1024, device=torch.device("cpu"),
+            offset_t=torch.tensor(999), base_t=torch.tensor(999), out=torch.full((64,), 5, dtype=torch.long),
+            prompt_len_t=torch.tensor(prompt_len), first=first.clone(), anchor=torch.tensor([7]),
+            pending=torch.full((k - 1,), 9, dtype=torch.long), round0_layout=round_layout([width - 1], torch.device("cpu")),
+            steady_layout=round_layout([k] * k, torch.device("cpu")), _install_tables=lambda layout: None,
+            mask=types.SimpleNamespace(offset=torch.zeros((), dtype=torch.long)), ids_buf=torch.empty(width, dtype=torch.long),
+            aux_buf=aux_buf, _embed=embed, seq_lens=torch.zeros(1, dtype=torch.int32),
+            md=types.SimpleNamespace(decode_offset=torch.zeros(1, dtype=torch.int32)),
+            slot_mapping=torch.zeros(width, dtype=torch.long), rows=torch.arange(width),
+            kv_num_blocks=torch.zeros(1, dtype=torch.int32), _forward=forward,
+            model=types.SimpleNamespace(compute_logits=lambda h: logits), _decode_verify=decode_verify,
+            kidx=torch.arange(k))
+        RoundDecoder._round0(fake)
+        rec = {"out": fake.out, "base": fake.base_t, "offset": fake.offset_t, "anchor": fake.anchor,
+               "pending": fake.pending, "first": first, "verify_token": verify_token,
+               "inputs_checksum": np.float64(checksum(logits[:, :vocab]) + checksum(aux_buf)), "ids": seen["ids"],
+               "aux_values": seen["aux_values"], "positions": seen["positions"], "slot_mapping": seen["slot_mapping"],
+               "gated_from": torch.tensor(seen["gated_from"]), "verify_index": seen["verify_index"],
+               "seq_lens": fake.seq_lens, "kv_num_blocks": fake.kv_num_blocks}
+        for key, value in rec.items():
+            records[f"{seed}/{key}"] = value.numpy() if isinstance(value, torch.Tensor) else np.asarray(value)
+    np.savez_compressed(out / "round0.npz", **records)
+
+
+def round0_inputs(seed: int, k: int, vocab: int = 50257):
+    """gen_round0's seeded stand-ins: logits at compute_logits' padded width (cut to the vocabulary by _round0),
+    the verify decode's token, the prefill's first token and the auxiliary stream."""
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(k + k * k, vocab + 7, generator=g)
+    verify_token = torch.randint(0, vocab, (1,), generator=g)
+    first = torch.randint(0, vocab, (1,), generator=g)
+    aux_buf = torch.randint(0, 1024, (8192,), generator=g)
+    return logits, verify_token, first, aux_buf
+
+
 def gen_voronoi(ref, out: Path):
     import plm.iterate as it
     from plm.auxiliary import LogitVoronoiAuxiliary
@@ -362,7 +427,7 @@ def main() -> None:
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     gens = {"layout": gen_layout, "quota": gen_quota, "accept": gen_accept, "epilogue": gen_epilogue,
-            "voronoi": gen_voronoi, "llama": gen_llama, "ptp": gen_ptp}
+            "voronoi": gen_voronoi, "llama": gen_llama, "ptp": gen_ptp, "round0": gen_round0}
     for name, fn in gens.items():
         if args.only is None or name in args.only:
             fn(args.reference, out)

@@ -203,3 +203,35 @@ def test_round_to_dtype_matches_torch():
     x[:5] = torch.tensor([0.0, -0.0, float("inf"), 1e-40, 65504.0])
     np.testing.assert_array_equal(exact.round_to_dtype(x.numpy(), "bfloat16"), x.bfloat16().float().numpy())
     np.testing.assert_array_equal(exact.round_to_dtype(x.numpy(), "float16"), x.half().float().numpy())
+
+
+@pytest.mark.parametrize("case", mg.ROUND0_CASES)
+def test_round0_matches_reference(case):
+    """Round 0 after the prefill (plm/decoder.py:275-310, run unbound with its model calls stubbed): the oracle's
+    state reset, inputs and commit equal the reference's."""
+    seed, k, prompt_len = case
+    data = np.load(GOLDEN / "round0.npz")
+    d = {key.split("/", 1)[1]: data[key] for key in data.files if key.startswith(f"{seed}/")}
+    vocab, page = 50257, 16
+    logits, verify_token, first, aux_buf = mg.round0_inputs(seed, k, vocab)
+    logits = logits[:, :vocab]
+    assert math.isclose(mg.checksum(logits) + mg.checksum(aux_buf), float(d["inputs_checksum"]), rel_tol=1e-12)
+
+    state = orounds.RoundState(k, 64)
+    orounds.first_token(state, int(first[0]), prompt_len)
+    layout = orounds.round0_layout(k)
+    ids, values, positions, slots = orounds.round0_prologue(state, layout, vocab, 1024, aux_buf.numpy())
+    np.testing.assert_array_equal(ids, d["ids"])
+    np.testing.assert_array_equal(values, d["aux_values"])
+    np.testing.assert_array_equal(positions, d["positions"])
+    np.testing.assert_array_equal(slots + page, d["slot_mapping"])  # the reference's slots skip its null page
+    assert int(d["gated_from"]) == 1
+    assert int(d["verify_index"][0]) == state.base  # round 0 decodes its verify row at aux_buf[base]
+    assert int(d["seq_lens"][0]) == prompt_len + k + k * k
+    assert int(d["kv_num_blocks"][0]) == -(-(prompt_len + k + k * k) // page)
+
+    orounds.round0_epilogue(state, int(verify_token[0]), orounds.argmax_first(logits[1:].numpy()))
+    np.testing.assert_array_equal(state.out[:64], d["out"])
+    assert state.base == int(d["base"]) and state.offset == int(d["offset"])
+    assert state.anchor == int(d["anchor"][0])
+    np.testing.assert_array_equal(state.pending, d["pending"])
