@@ -80,3 +80,6 @@ def test_calls_fail_loudly_without_gpu():
     buf = ctypes.create_string_buffer(256)
     native.library().plm_last_error(buf, 256)
     assert buf.value  # the failure left a message
+    # entry points that take a context reject a missing one before touching a device
+    desc = native.IcdfDesc(n_rows=1, vocab=8, top_k=4)
+    assert native.library().plm_icdf_decode(None, ctypes.byref(desc), None) != 0
