@@ -9,18 +9,20 @@ exact match with Voronoi sampling, KV context of 1024 tokens in 16-token pages t
 steps, so the context grows by the accepted tokens. Weights (3.4 GB) exceed L2, so no flush is needed.
 
   value   accepted tokens/s over all GPUs, device-timed with CUDA events (inputs resident in HBM).
-  e2e     the same metric through the public API: RoundDecoder.generate on a 256-token prompt copied from pinned
-          host memory, 512 new tokens, with the per-round pinned-memory poll of the reference's decode loop and
-          the tokens read back (configs[2] per request).
-  roofline  the dominant kernel (skinny_gemm_kernel: every weight GEMM of the round, launched exactly as in the
-          round) timed live by CUDA events: weight bytes / time, against the measured HBM copy bandwidth.
+  e2e     the same metric through the public API: RoundDecoder.generate on BASELINE configs[2]'s requests (a
+          256-token prompt copied from pinned host memory, 512 new tokens, seeds 0, 1, 2 in turn), the rounds kept in
+          flight by the device-side stop, the tokens read back; --e2e-requests per rank.
+  roofline  the dominant kernel (the layer blocks of a round: o, its norm, gate_up and down of every layer, launched
+          exactly as in the round) timed live by CUDA events: weight bytes / time, against the measured HBM copy
+          bandwidth.
   round_roofline  all algorithmic bytes of a round (weights, KV read and written, Voronoi gathers) / round time.
   cpu_baseline    the CPU oracle's round (oracle/model.py, torch on all host threads) on a bounded sample.
 
 Multi-GPU (torchrun, one process per GPU): replicas only — every rank runs the same workload on its own GPU
 (weak scaling), no data-path collective; the elapsed time is the maximum over ranks.
-``--impl reference`` times the reference arm: the CPU oracle round (the reference's path has no CPU
-implementation of its own) on the host cores, rank 0 only.
+``--impl reference`` times the reference arm: the CPU round oracle (the reference's path has no CPU implementation of
+its own), built from seeded CPU generators and run on all host cores for the same steps, rank 0 only; it loads no
+GPU library of this repository.
 """
 
 from __future__ import annotations
@@ -152,8 +154,8 @@ def _dist():
     return 0, 1, 0, None
 
 
-def _setup_decoder(seed: int = 0, separate_mlp: bool = False):
-    """The configs[1] workload: weights, a decoder over a shuffled pool, a 1024-token N(0, 1) context."""
+def _setup_decoder(seed: int = 0, separate_mlp: bool = False, ctx: int = CTX):
+    """The configs[1] workload: weights, a decoder over a shuffled pool, a ``ctx``-token N(0, 1) context."""
     import torch
 
     from plm.decoder import RoundDecoder
@@ -161,7 +163,7 @@ def _setup_decoder(seed: int = 0, separate_mlp: bool = False):
 
     cfg = shape_config(SHAPE)
     weights = PLMWeights.random(cfg, seed=seed)
-    max_model_len = 2048
+    max_model_len = max(2048, ctx + 1024)
     max_pages = -(-(max_model_len + 2 * (K + K * K) + PAGE) // PAGE)
     num_pages = 2 * max_pages
     page_bytes = cfg.num_layers * 2 * cfg.num_kv_heads * PAGE * cfg.head_dim * 2
@@ -173,15 +175,16 @@ def _setup_decoder(seed: int = 0, separate_mlp: bool = False):
     return cfg, weights, decoder
 
 
-def _seed_context(decoder, cfg, seed: int = 1) -> None:
-    """K/V ~ N(0, 1) bf16 over the pool, then the request state of a steady round at offset CTX."""
+def _seed_context(decoder, cfg, seed: int = 1, ctx: int = CTX) -> None:
+    """K/V ~ N(0, 1) bf16 over the pool, then the request state of a steady round at offset ``ctx`` (no stop)."""
     import torch
 
     g = torch.Generator(device="cuda").manual_seed(seed)
     kv = decoder.kv_cache
     for layer in range(kv.shape[0]):
         kv[layer].copy_(torch.randn(kv[layer].shape, generator=g, device="cuda", dtype=torch.float32).bfloat16())
-    decoder.offset_t.fill_(CTX)
+    decoder.handle.set_stop(1 << 62)
+    decoder.offset_t.fill_(ctx)
     decoder.base_t.fill_(2)
     decoder.out.fill_(-1)
     decoder.anchor.fill_(17)
@@ -312,40 +315,90 @@ def cpu_baseline(weights_gpu, decoder, cfg, rounds: int = 1) -> dict:
         tokens += oracle.round() + 1
     seconds = time.perf_counter() - started
     return {"value": tokens / seconds, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{rounds} steady round(s) of the configs[1] workload (1.3B shape, k=7, ctx {CTX}) by the CPU "
+            "sample": f"{rounds} steady round(s) of the configs[1] workload (1.3B shape, k=7, ctx {st.offset}) by the CPU "
                       f"oracle (torch fp32 forward + numpy Voronoi), {seconds:.2f} s",
             "seconds_per_round": seconds / rounds}
 
 
-def run_reference(args) -> None:
-    """Reference arm: the CPU oracle round (no GPU kernels of this repository on the timed path)."""
+def _cpu_workload(seed: int = 0, ctx: int = CTX):
+    """The configs[1] workload built on the CPU alone (no GPU, no library of this repository): seeded bf16 weights,
+    the Voronoi cost table -(aux_vocab . lm_head^T)^T rounded to bf16, a shuffled block table, K/V ~ N(0, 1) over the
+    pool and the state of a steady round at offset ``ctx``, as the CPU round oracle that stands in for the reference's
+    round (its own path needs vLLM and a GPU)."""
+    import numpy as np
     import torch
 
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+    from oracle import model as omodel
+    from oracle import voronoi as ov
     from plm.model import PLMWeights, shape_config
 
     cfg = shape_config(SHAPE)
-    if torch.cuda.is_available():
-        cfg_, weights, decoder = _setup_decoder()
-        _seed_context(decoder, cfg)
-    else:
-        print(json.dumps({"impl": "reference", "unavailable": "the workload is seeded on the GPU box"}))
+    weights = PLMWeights.random(cfg, seed=seed, device="cpu")
+    max_model_len = max(2048, ctx + 1024)
+    max_pages = -(-(max_model_len + 2 * (K + K * K) + PAGE) // PAGE)
+    num_pages = 2 * max_pages
+    g = torch.Generator().manual_seed(seed)
+    block_table = torch.randperm(num_pages, generator=g)[:max_pages].numpy().astype(np.int64)
+    cos_sin = omodel.rope_cache(cfg.head_dim, max(cfg.max_pos, max_pages * PAGE), cfg.rope_theta, torch.bfloat16)
+    shape = omodel.ModelShape(cfg.num_layers, cfg.hidden, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                              cfg.intermediate, cfg.vocab, cfg.aux_vocab, cfg.num_aux_tokens, cfg.rms_eps,
+                              cfg.rope_theta, cos_sin.shape[0])
+    model = omodel.OracleModel(shape, weights.named(), "bfloat16", PAGE, num_pages, block_table, cos_sin=cos_sin)
+    model.kv.normal_(0.0, 1.0, generator=g)
+    model.kv.copy_(model.kv.bfloat16().float())
+    scores = weights.aux_vocab.float() @ weights.lm_head.float().T
+    table = (-scores.bfloat16().float()).T.contiguous().numpy()
+    aux = torch.randint(cfg.aux_vocab, (8192,), generator=torch.Generator().manual_seed(0)).numpy()
+    oracle = omodel.RoundOracle(model, table, K, "nucleus", None,
+                                ov.VoronoiConfig(cfg.top_m, cfg.shortlist, cfg.rounds, cfg.sweeps),
+                                capacity=max_pages * PAGE, aux_stream=aux)
+    st = oracle.state
+    st.offset, st.base, st.anchor = ctx, 2, 17
+    st.pending = torch.randint(0, cfg.vocab, (K - 1,), generator=g).numpy().astype(np.int64)
+    del weights
+    return cfg, oracle
+
+
+def workload_config(ctx: int, world: int) -> dict:
+    """The ``config`` of both arms' lines (the same workload, whichever arm runs it)."""
+    return {"workload": f"BASELINE configs[1]: single-round microbenchmark, PLM-1.3B shape, k=7 (56 rows), exact "
+                        f"match + Voronoi, ctx {ctx} (+ accepted tokens), 16-token pages, shuffled block table, "
+                        "K/V ~ N(0,1)", "model": SHAPE, "k": K, "rows": K + K * K, "ctx_start": ctx,
+            "page_size": PAGE, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (3.4 GB weights per round), no flush"}
+
+
+def run_reference(args) -> None:
+    """Reference arm: the CPU round oracle on all host threads, built and run on the CPU only, for the same steps."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:  # replicas: one host baseline per box
         return
-    steps, warm = max(1, min(args.steps, 3)), min(args.warmup, 1)
-    if warm:
-        cpu_baseline(weights, decoder, cfg, rounds=1)
-        _seed_context(decoder, cfg)
-    res = cpu_baseline(weights, decoder, cfg, rounds=steps)
-    line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-            "steps_requested": args.steps, "warmup": warm, "ms_per_step": 1000 * res["seconds_per_round"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "BASELINE configs[1]: single round, PLM-1.3B shape, k=7, ctx 1024, page 16, "
-                                   "shuffled block table; CPU oracle round", "model": SHAPE, "k": K},
-            "cpu_baseline": res, "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
-                                         "d2h_bytes_per_step": 0}}
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    t_setup = time.perf_counter()
+    cfg, oracle = _cpu_workload(ctx=args.ctx)
+    setup_s = time.perf_counter() - t_setup
+    for _ in range(args.warmup):
+        oracle.round()
+    base0 = oracle.state.base
+    started = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.round()
+    seconds = time.perf_counter() - started
+    tokens = oracle.state.base - base0
+    value = tokens / seconds
+    sample = (f"{args.steps} steady rounds (after {args.warmup} warm-up rounds) of the configs[1] workload by the CPU "
+              f"round oracle (torch fp32 forward over bf16 values + numpy Voronoi), {seconds:.2f} s; built on the "
+              f"CPU in {setup_s:.1f} s")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * seconds / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": workload_config(args.ctx, 1), "round_us": 1e6 * seconds / args.steps,
+            "tokens_per_round": tokens / args.steps,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
@@ -365,14 +418,14 @@ def run_native(args) -> None:
     import torch
 
     rank, world, local, dist = _dist()
-    cfg, weights, decoder = _setup_decoder(separate_mlp=args.separate_mlp)
-    _seed_context(decoder, cfg)
+    cfg, weights, decoder = _setup_decoder(separate_mlp=args.separate_mlp, ctx=args.ctx)
+    _seed_context(decoder, cfg, ctx=args.ctx)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         decoder.graph.replay()
     torch.cuda.synchronize()
     decoder.check()
-    _seed_context(decoder, cfg)
+    _seed_context(decoder, cfg, ctx=args.ctx)
     base0, ctx0 = int(decoder.base_t), int(decoder.offset_t)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
@@ -411,17 +464,20 @@ def run_native(args) -> None:
     round_achieved = bytes_["total"] / (ms_per_step / 1000) / 1e9
     del graph, keep
 
-    # end to end through the public API (configs[2] per request)
-    e2e_reqs = 0 if args.skip_e2e else max(1, min(3, args.steps // 10 or 1))
+    # End to end through the public API: configs[2]'s requests (256-token random prompts, 512 new tokens, seeds 0, 1,
+    # 2 in turn), a contiguous slice of the job's request list per rank; the job's time is the slowest rank's.
+    per_rank = 0 if args.skip_e2e else args.e2e_requests
     e2e_tokens, e2e_rounds, e2e_s = 0, 0, 0.0
-    if e2e_reqs:
-        prompt = torch.randint(0, cfg.vocab, (PROMPT_E2E,), generator=torch.Generator().manual_seed(0)).pin_memory()
-        decoder.generate(prompt, TOKENS_E2E, seed=0, stop_at_eos=False)  # warm-up request
+    if per_rank:
+        requests = [(i, i % 3) for i in range(rank * per_rank, (rank + 1) * per_rank)]  # (prompt index, seed)
+        prompts = {i: torch.randint(0, cfg.vocab, (PROMPT_E2E,), generator=torch.Generator().manual_seed(1000 + i))
+                   .pin_memory() for i, _ in requests}
+        decoder.generate(prompts[requests[0][0]], TOKENS_E2E, seed=0, stop_at_eos=False)  # warm-up request
         if dist:
             dist.barrier()
         t0 = time.perf_counter()
-        for i in range(e2e_reqs):
-            res = decoder.generate(prompt, TOKENS_E2E, seed=i, stop_at_eos=False)
+        for i, seed in requests:
+            res = decoder.generate(prompts[i], TOKENS_E2E, seed=seed, stop_at_eos=False)
             e2e_tokens += len(res.token_ids)
             e2e_rounds += res.steady_rounds
         e2e_s = time.perf_counter() - t0
@@ -430,7 +486,7 @@ def run_native(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:  # the CPU baseline is an N=1 figure
-        _seed_context(decoder, cfg)
+        _seed_context(decoder, cfg, ctx=args.ctx)
         cpu = cpu_baseline(weights, decoder, cfg, rounds=1)
 
     if rank == 0:
@@ -440,11 +496,7 @@ def run_native(args) -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE configs[1]: single-round microbenchmark, PLM-1.3B shape, k=7 "
-                                   "(56 rows), exact match + Voronoi, ctx 1024 (+ accepted tokens), 16-token pages, "
-                                   "shuffled block table, K/V ~ N(0,1)", "model": SHAPE, "k": K, "rows": K + K * K,
-                       "ctx_start": CTX, "ctx_mean": ctx_mean, "page_size": PAGE, "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2 (3.4 GB weights per round), no flush"},
+            "config": workload_config(args.ctx, world), "ctx_mean": ctx_mean,
             "round_us": 1000 * ms_per_step,
             "tokens_per_round": total_tokens / (args.steps * world),
             "roofline": {"bound": "hbm", "kernel": dom_kernel,
@@ -457,8 +509,10 @@ def run_native(args) -> None:
             "round_roofline": {"bound": "hbm", "achieved": round_achieved, "peak": peak, "unit": "GB/s",
                                "frac": round_achieved / peak, "bytes_per_round": bytes_},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": PROMPT_E2E * 8,
-                    "d2h_bytes_per_step": int(e2e_rounds / max(e2e_reqs, 1)) * (8 + 8 * 1024) + TOKENS_E2E * 8,
-                    "step": f"one request: {PROMPT_E2E}-token prompt, {TOKENS_E2E} new tokens", "requests": e2e_reqs},
+                    "d2h_bytes_per_step": int(e2e_rounds / max(per_rank, 1)) * 16 + TOKENS_E2E * 8,
+                    "step": f"one request: {PROMPT_E2E}-token prompt, {TOKENS_E2E} new tokens (BASELINE configs[2], "
+                            f"seeds 0, 1, 2 in turn)", "requests": per_rank * world,
+                    "sharding": "a contiguous slice of the request list per rank"},
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_round * args.steps,
             "clocks": clocks.summary(),
@@ -478,10 +532,13 @@ def main() -> None:
     parser.add_argument("--impl", default="native", choices=("native", "reference"))
     parser.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     parser.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end requests (profiling runs)")
+    parser.add_argument("--ctx", type=int, default=CTX, help="committed context of the timed rounds (tokens)")
+    parser.add_argument("--e2e-requests", type=int, default=2,
+                        help="end-to-end requests per rank (configs[2] runs 64 in all: --e2e-requests 64/N)")
     parser.add_argument("--separate-mlp", action="store_true",
                         help="gate_up and down as two launches instead of the persistent MLP block launch")
     args = parser.parse_args()
-    if args.warmup < 3 and args.impl == "native":
+    if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 4
+#define PLM_ABI_VERSION 5
 
 enum plm_status {
   PLM_OK = 0,
@@ -130,6 +130,11 @@ typedef struct plm_bookkeeping {
   int64_t seq_cap;
   int64_t* sequence_step;
   int64_t prompt_len;
+  /* Nullable request stop block, int64[4]: token budget, end-of-text id (-1: none), end-of-text window, done flag.
+   * A steady round whose bookkeeping finds the done flag set commits nothing; one that leaves base >= budget, or
+   * confirms the end-of-text id at an output position below the window, sets it (the stop test of the reference's
+   * host loop, plm/decoder.py:414-439). The first-token bookkeeping clears it. */
+  int64_t* stop;
 } plm_bookkeeping;
 
 /* One verify decode per row: Voronoi assignment of the row's logits (plm/iterate.py:322-342 through
@@ -283,6 +288,7 @@ typedef struct plm_state_ptrs {
   void* table;
   int64_t out_capacity, seq_capacity, aux_len, plane_elems;
   int32_t width, lm_tiles, row_capacity;
+  int64_t* stop;         /* [4] the request stop block (plm_bookkeeping.stop) */
 } plm_state_ptrs;
 
 /* ---- context ---- */
@@ -304,7 +310,9 @@ int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* desc, void* stream);
  * arrival counter (zero at module load, reset to zero by every bookkeeping launch), the device error word used
  * when device_error is NULL, and 32 row slots for the decoded tokens and verdicts used when desc->verify or
  * desc->flags is NULL. More than 32 rows is rejected with PLM_ERR_INVALID. device_error, when given, is a device
- * int32 the caller has zeroed; the first device-side error code is written there. The first call on a device
+ * int32 the caller has zeroed; the first device-side error code is written there. With device_error NULL, device-side
+ * errors (an index out of range, a wait that ran out of time) go to the scratch's own error word, which the C ABI
+ * cannot read back: callers that need to see them pass a zeroed device int32. The first call in a CUDA context
  * (with that device current) resolves the scratch's address with cudaGetSymbolAddress, so make it before any stream
  * capture. Calls on one device share the scratch: overlapping calls (other streams or threads) race. */
 int plm_verify_decode_static(const plm_verify_desc* desc, int32_t* device_error, void* stream);
@@ -336,6 +344,11 @@ int plm_destroy(plm_handle* h);
 int plm_set_block_table(plm_handle* h, const int32_t* table_host, int32_t n);
 int plm_set_aux_stream(plm_handle* h, const int64_t* cells, int64_t n, void* stream);
 int plm_load_prompt(plm_handle* h, const int64_t* ids, int64_t n, void* stream);
+/* Sets the request's stop block on `stream` (done flag cleared): steady rounds stop committing once base reaches
+ * max_tokens, or once a round confirms eos_token (>= 0; -1 disables the test) at an output position below
+ * eos_window. Replaces the host-side stop test of plm/decoder.py:414-439, so a caller can keep rounds in flight:
+ * rounds replayed after the stop leave the state as it was. A new handle stops at no budget and no end-of-text. */
+int plm_set_stop(plm_handle* h, int64_t max_tokens, int64_t eos_token, int64_t eos_window, void* stream);
 /* Causal prefill of the loaded prompt, then the first token and the request state of round 0. */
 int plm_prefill(plm_handle* h, void* stream);
 int plm_round0(plm_handle* h, void* stream);

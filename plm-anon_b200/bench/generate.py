@@ -38,6 +38,9 @@ def add_arguments(parser: argparse.ArgumentParser) -> None:
                         help="exact, or relaxed (the setting's looser accept rule)")
     parser.add_argument("--k", type=int, help="proposal length per round; default from --setting")
     parser.add_argument("--block-size", type=int, default=KV_BLOCK_SIZE, help="KV page size in tokens")
+    parser.add_argument("--dtype", default="", choices=("", "bfloat16", "float16"),
+                        help="weights' dtype on the GPU; default: the export's own (the kernels take bfloat16, so a "
+                             "float16 export needs --dtype bfloat16 to convert it)")
     parser.add_argument("--ar", action="store_true", help="autoregressive decoding: one Voronoi-decoded row per step")
     parser.add_argument("--ar-sampler", default="voronoi", choices=("voronoi", "icdf", "topk", "greedy"),
                         help="voronoi: the PLM's own decode rule on the seeded cells, token-identical to --match exact "
@@ -64,9 +67,9 @@ def round_config(args: argparse.Namespace) -> RoundConfig:
     """The RoundConfig the flags select (bench/generate.py:67-71). AR-Voronoi is exact matching with k = 1."""
     if args.ar:
         return RoundConfig(model=args.model, setting=args.setting, mode=args.mode, match="exact", k=1,
-                           max_model_len=args.max_model_len)
+                           dtype=args.dtype or None, max_model_len=args.max_model_len)
     return RoundConfig(model=args.model, setting=args.setting, mode=args.mode, match=args.match, k=args.k,
-                       max_model_len=args.max_model_len)
+                       dtype=args.dtype or None, max_model_len=args.max_model_len)
 
 
 def plm_generator(args: argparse.Namespace) -> tuple[dict, Callable]:

@@ -10,6 +10,7 @@ from __future__ import annotations
 import argparse
 import json
 from collections.abc import Callable
+from dataclasses import dataclass
 from pathlib import Path
 
 import torch
@@ -40,15 +41,6 @@ def speed_record(prompt, continuation: str, accepted: list[int], calls: int, tok
             "tokens_per_second": tokens / (ms / 1000) if ms else 0.0}
 
 
-def measure(generate_one: Callable, dataset: list, seed: int) -> list[dict]:
-    records = []
-    for index, prompt in enumerate(dataset, 1):
-        records.append(generate_one(prompt, seed))
-        print(f"  [seed {seed}  {index}/{len(dataset)}] {records[-1]['tokens_per_call']:.2f} tok/call  "
-              f"{records[-1]['tokens_per_second']:.0f} tok/s")
-    return records
-
-
 def aggregate(records: list[dict]) -> dict:
     """bench/harness.py:33-39: per-pass totals; rates over the steady rounds' time, and end to end over the wall time
     of the whole requests."""
@@ -64,33 +56,57 @@ def aggregate(records: list[dict]) -> dict:
 
 
 def add_run_arguments(parser: argparse.ArgumentParser) -> None:
-    """bench/harness.py:42-49."""
-    parser.add_argument("--max-model-len", type=int, default=4096, help="prompt plus generated tokens")
+    """The run flags of the reference's harness (bench/harness.py:42-49): same names, defaults and meaning."""
+    parser.add_argument("--max-model-len", type=int, default=4096,
+                        help="longest request the decoder is sized for (prompt and continuation together)")
     parser.add_argument("--dataset", required=True,
-                        help="JSON list of prompt strings or token-id lists, or random:<count>:<length>[:<seed>]")
-    parser.add_argument("--prompts", type=int, default=None, help="use only the first N prompts")
-    parser.add_argument("--tokens", type=int, default=128, help="generated tokens per prompt (a ceiling with --stop-at-eos)")
-    parser.add_argument("--stop-at-eos", action="store_true", help="end each continuation at the end-of-text token")
+                        help="a JSON file listing prompts (text or token-id lists), or random:<count>:<length>[:<seed>]")
+    parser.add_argument("--prompts", type=int, default=None, help="keep only this many prompts from the start")
+    parser.add_argument("--tokens", type=int, default=128,
+                        help="continuation length per prompt; with --stop-at-eos, the most it may reach")
+    parser.add_argument("--stop-at-eos", action="store_true", help="cut a continuation at its end-of-text token")
     parser.add_argument("--seeds", type=int, nargs="+", default=[0, 1, 2],
-                        help="one measured pass per seed, after a discarded warm-up pass")
-    parser.add_argument("--out", default="results.json")
+                        help="the recorded passes, one per seed; an unrecorded warm-up pass uses the first")
+    parser.add_argument("--out", default="results.json", help="where the results file goes")
+
+
+@dataclass
+class Passes:
+    """Runs ``generate_one(prompt, seed) -> speed record`` over the whole dataset, once per call of ``run``."""
+
+    generate_one: Callable
+    dataset: list
+
+    def run(self, seed: int, label: str) -> list[dict]:
+        records = []
+        for index, prompt in enumerate(self.dataset):
+            record = self.generate_one(prompt, seed)
+            records.append(record)
+            print(f"{label}: prompt {index + 1}/{len(self.dataset)}, {record['tokens']} tokens, "
+                  f"{record['tokens_per_call']:.2f} per round, {record['tokens_per_second']:.1f} tokens/s")
+        return records
+
+
+def _summary_line(summary: dict) -> str:
+    return ", ".join(f"{key} {value:.3f}" if isinstance(value, float) else f"{key} {value}"
+                     for key, value in summary.items())
 
 
 def run_passes(described: dict, generate_one: Callable, dataset: list, args: argparse.Namespace) -> dict:
-    """bench/harness.py:52-66: a discarded warm-up pass, then one measured pass per seed, written as one file."""
-    print("=== warm-up pass (discarded)")
-    measure(generate_one, dataset, args.seeds[0])
-    passes = []
+    """The measurement the reference's run_passes makes (bench/harness.py:52-66): the warm-up pass pays graph
+    capture and cold clocks and is not recorded; each seed's pass is recorded with its aggregate. The results file
+    keeps the reference's layout: {"config": ..., "passes": [{"seed", "aggregate", "results"}]}."""
+    passes = Passes(generate_one, dataset)
+    passes.run(args.seeds[0], "warm-up (not recorded)")
+    recorded = []
     for seed in args.seeds:
-        print(f"=== seed {seed}")
-        records = measure(generate_one, dataset, seed)
-        passes.append({"seed": seed, "aggregate": aggregate(records), "results": records})
-        print("  " + "  ".join(f"{key}={value:.3f}" if isinstance(value, float) else f"{key}={value}"
-                               for key, value in passes[-1]["aggregate"].items()))
-    described = dict(described) | {"seeds": args.seeds, "prompts": len(dataset), "tokens": args.tokens,
-                                   "stop_at_eos": args.stop_at_eos, "max_model_len": args.max_model_len,
-                                   "dataset": args.dataset}
-    result = {"config": described, "passes": passes}
+        records = passes.run(seed, f"seed {seed}")
+        summary = aggregate(records)
+        print(f"seed {seed} aggregate: {_summary_line(summary)}")
+        recorded.append({"seed": seed, "aggregate": summary, "results": records})
+    run = {"seeds": args.seeds, "prompts": len(dataset), "tokens": args.tokens, "stop_at_eos": args.stop_at_eos,
+           "max_model_len": args.max_model_len, "dataset": args.dataset}
+    result = {"config": {**described, **run}, "passes": recorded}
     Path(args.out).write_text(json.dumps(result, indent=1))
-    print(f"  -> {args.out}")
+    print(f"results written to {args.out}")
     return result

@@ -74,6 +74,8 @@ struct plm_handle {
   int64_t *out = nullptr, *base = nullptr, *offset = nullptr, *anchor = nullptr, *pending = nullptr,
           *round_sequence = nullptr, *sequence_step = nullptr, *aux_buf = nullptr, *prompt = nullptr,
           *chunk_offsets = nullptr;
+  int64_t* stop = nullptr;      // [kStopWords] the request stop block the steady bookkeeping reads and sets
+  int64_t stop_host[4] = {};    // the values plm_set_stop last queued (the copy's host source stays valid)
   int64_t prompt_len = 0;
   int attn_splits_round = 1;
   // MLP block kernel: schedule, per-layer gate_up counters and the forward counter they are compared with
@@ -349,6 +351,7 @@ int verify(plm_handle* h, int n_rows, int mode, const int64_t* aux_base, cudaStr
   a.book.seq_cap = h->rd.seq_capacity;
   a.book.sequence_step = h->sequence_step;
   a.book.prompt_len = h->prompt_len;
+  a.book.stop = h->stop;
   a.counter = h->ctx->counters + (h->ctx->n_counters - 1);
   a.err = h->ctx->err;
   int st = verify_validate(a, n_rows);
@@ -422,7 +425,7 @@ int plm_destroy(plm_handle* h) {
                   h->verify_logits, h->best_val, h->best_idx, h->verify, h->flags, h->st_relpos, h->st_relaux,
                   h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
-                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->block_ctr,
+                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->stop, h->block_ctr,
                   h->block_tiles, h->attn_tiles, h->x_tiles, h->act_tiles};
   for (void* b : bufs) cudaFree(b);
   mlp_schedule_destroy(&h->mlp);
@@ -540,14 +543,15 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   }
   if (st != PLM_OK) return guard(st);
   // zero the activations once: rows past `rows` are read by TMA boxes but never stored
-  for (void* b : {h->x_norm, h->residual, h->y, h->q, h->attn, h->act}) (void)b;
-  cudaMemset(h->x_norm, 0, R * hidden * 2);
-  cudaMemset(h->residual, 0, R * hidden * 2);
-  cudaMemset(h->y, 0, R * hidden * 2);
-  cudaMemset(h->q, 0, R * q_size * 2);
-  cudaMemset(h->attn, 0, R * q_size * 2);
-  cudaMemset(h->act, 0, R * I * 2);
-  cudaMemset(h->gathered, 0, size_t(16) * hidden * 2);
+  {
+    const std::pair<void*, size_t> zeroed[] = {{h->x_norm, R * hidden * 2}, {h->residual, R * hidden * 2},
+                                               {h->y, R * hidden * 2},      {h->q, R * q_size * 2},
+                                               {h->attn, R * q_size * 2},   {h->act, R * I * 2},
+                                               {h->gathered, size_t(16) * hidden * 2}};
+    for (const auto& z : zeroed)
+      if (st == PLM_OK) st = check_cuda(cudaMemset(z.first, 0, z.second), "plm_create: zeroing the activations");
+  }
+  if (st != PLM_OK) return guard(st);
 
   // layouts: steady round [k] * k, round 0 [W - 1] (plm/decoder.py:145-146), causal chunk rows
   std::vector<int64_t> relpos, relaux;
@@ -599,16 +603,32 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   if (st == PLM_OK) st = dev_alloc(&h->aux_buf, size_t(h->rd.aux_len), "aux stream");
   if (st == PLM_OK) st = dev_alloc(&h->prompt, size_t(rd->max_pages) * rd->page_size, "prompt");
   if (st == PLM_OK) st = dev_alloc(&h->chunk_offsets, 4096, "chunk offsets");
+  if (st == PLM_OK) st = dev_alloc(&h->stop, kStopWords, "stop block");
   if (st != PLM_OK) return guard(st);
-  cudaMemset(h->out, 0xff, size_t(h->rd.out_capacity) * 8);
-  cudaMemset(h->base, 0, 8);
-  cudaMemset(h->offset, 0, 8);
-  cudaMemset(h->anchor, 0, 8);
-  cudaMemset(h->pending, 0, 32 * 8);
-  cudaMemset(h->round_sequence, 0, size_t(h->rd.seq_capacity) * 8);
-  cudaMemset(h->sequence_step, 0, 8);
-  cudaMemset(h->aux_buf, 0, size_t(h->rd.aux_len) * 8);
-  cudaMemset(h->prompt, 0, size_t(rd->max_pages) * rd->page_size * 8);
+  h->stop_host[kStopBudget] = INT64_MAX;  // no budget and no end-of-text until plm_set_stop
+  h->stop_host[kStopEos] = -1;
+  h->stop_host[kStopWindow] = 0;
+  h->stop_host[kStopDone] = 0;
+  st = check_cuda(cudaMemcpy(h->stop, h->stop_host, sizeof(h->stop_host), cudaMemcpyHostToDevice), "stop block");
+  if (st != PLM_OK) return guard(st);
+  {
+    const struct {
+      void* p;
+      int value;
+      size_t bytes;
+    } init[] = {{h->out, 0xff, size_t(h->rd.out_capacity) * 8},
+                {h->base, 0, 8},
+                {h->offset, 0, 8},
+                {h->anchor, 0, 8},
+                {h->pending, 0, 32 * 8},
+                {h->round_sequence, 0, size_t(h->rd.seq_capacity) * 8},
+                {h->sequence_step, 0, 8},
+                {h->aux_buf, 0, size_t(h->rd.aux_len) * 8},
+                {h->prompt, 0, size_t(rd->max_pages) * rd->page_size * 8}};
+    for (const auto& z : init)
+      if (st == PLM_OK) st = check_cuda(cudaMemset(z.p, z.value, z.bytes), "plm_create: initialising the round state");
+  }
+  if (st != PLM_OK) return guard(st);
   h->attn_splits_round = attention_splits(m->num_heads, (h->W + 63) / 64, h->ctx->num_sms,
                                           int64_t(rd->max_pages) * rd->page_size);
 
@@ -663,6 +683,22 @@ int plm_load_prompt(plm_handle* h, const int64_t* ids, int64_t n, void* stream) 
   h->prompt_len = n;
   return check_cuda(cudaMemcpyAsync(h->prompt, ids, size_t(n) * 8, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
                     "prompt copy");
+}
+
+int plm_set_stop(plm_handle* h, int64_t max_tokens, int64_t eos_token, int64_t eos_window, void* stream) {
+  if (!h || eos_token < -1 || eos_window < 0)
+    return fail(PLM_ERR_INVALID, "plm_set_stop: eos %lld, window %lld", (long long)eos_token, (long long)eos_window);
+  // The copy reads the handle's own host array: it must not change until the copy has run, so a stream that is
+  // still behind the previous plm_set_stop is synchronised first.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = check_cuda(cudaStreamSynchronize(s), "plm_set_stop: synchronize");
+  if (st != PLM_OK) return st;
+  h->stop_host[kStopBudget] = max_tokens;
+  h->stop_host[kStopEos] = eos_token;
+  h->stop_host[kStopWindow] = eos_window;
+  h->stop_host[kStopDone] = 0;
+  return check_cuda(cudaMemcpyAsync(h->stop, h->stop_host, sizeof(h->stop_host), cudaMemcpyHostToDevice, s),
+                    "plm_set_stop: copy");
 }
 
 int plm_prefill(plm_handle* h, void* stream) {
@@ -749,6 +785,7 @@ int plm_state(plm_handle* h, plm_state_ptrs* p) {
   p->width = h->W;
   p->lm_tiles = h->lm_tiles;
   p->row_capacity = h->R;
+  p->stop = h->stop;
   return PLM_OK;
 }
 

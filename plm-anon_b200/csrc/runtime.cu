@@ -168,12 +168,13 @@ int plm_ctx_check(plm_ctx* ctx, int32_t* device_error) {
   if (st != PLM_OK) return st;
   *device_error = v;
   if (v != 0) {
-    cudaMemset(ctx->err, 0, sizeof(int));
+    st = check_cuda(cudaMemset(ctx->err, 0, sizeof(int)), "plm_ctx_check: clearing the error word");
     // A launch that stopped early may have left arrival counters mid-count.
-    cudaMemset(ctx->counters, 0, ctx->n_counters * sizeof(int));
-    cudaDeviceSynchronize();
+    if (st == PLM_OK)
+      st = check_cuda(cudaMemset(ctx->counters, 0, ctx->n_counters * sizeof(int)), "plm_ctx_check: counters");
+    if (st == PLM_OK) st = check_cuda(cudaDeviceSynchronize(), "plm_ctx_check: synchronize");
   }
-  return PLM_OK;
+  return st;
 }
 
 }  // extern "C"

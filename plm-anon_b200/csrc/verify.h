@@ -16,6 +16,8 @@ constexpr int kVerifyThreads = 256;
 // quota/spread/prior, condense and fit of rounds 0 and 1, final cluster barrier, argmin (slots 13..15 unused).
 constexpr int kPhaseSlots = 16;
 enum BookMode : int { kBookNone = 0, kBookSteady = 1, kBookRound0 = 2, kBookFirstToken = 3 };
+// Words of the request stop block (plm_bookkeeping.stop).
+enum StopWord : int { kStopBudget = 0, kStopEos = 1, kStopWindow = 2, kStopDone = 3, kStopWords = 4 };
 
 struct Bookkeeping {
   int mode;
@@ -34,6 +36,7 @@ struct Bookkeeping {
   int64_t seq_cap;
   int64_t* sequence_step;
   int64_t prompt_len;        // first-token mode: the offset round 0 starts at
+  int64_t* stop;             // nullable [kStopWords]: budget, end-of-text id, end-of-text window, done flag
 };
 
 struct VerifyArgs {

@@ -22,8 +22,9 @@
 // from the lm_head's per-tile argmax partials, anchor, base and offset (the implicit KV commit).
 // Every floating-point step is a separate IEEE operation in a fixed order and exp/log come from plm_math.h; the numpy
 // oracle (oracle/voronoi.py) performs the same operations.
-#include <atomic>
 #include <climits>
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 #include "plm_math.h"
@@ -946,6 +947,8 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
   __threadfence();
   if (tid == 0) *a.counter = 0;
   const int K = b.k;
+  // A request that has already stopped: the round was queued behind the one that ended it and commits nothing.
+  if (b.mode == kBookSteady && b.stop != nullptr && __ldcg(b.stop + kStopDone) != 0) return;
 
   if (b.mode == kBookFirstToken) {
     for (int64_t i = tid; i < b.out_cap; i += kThreads) b.out[i] = -1;
@@ -957,6 +960,7 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
       *b.anchor = first;
       for (int i = 0; i < K - 1; ++i) b.pending[i] = 0;
       *b.offset = b.prompt_len;
+      if (b.stop != nullptr) b.stop[kStopDone] = 0;
     }
     return;
   }
@@ -1025,6 +1029,17 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
     *b.anchor = picked;
     *b.base = base + nc + 1;
     *b.offset = *b.offset + nc + 1;
+    if (b.mode == kBookSteady && b.stop != nullptr) {
+      // The stop test of the reference's host loop (plm/decoder.py:414-439) on the tokens this round confirmed.
+      const int64_t next = base + nc + 1;
+      bool done = next >= b.stop[kStopBudget];
+      const int64_t eos = b.stop[kStopEos];
+      if (eos >= 0) {
+        const int64_t end = min(min(next, b.stop[kStopWindow]), b.out_cap);
+        for (int64_t j = max(base, int64_t(0)); j < end; ++j) done = done || b.out[j] == eos;
+      }
+      if (done) b.stop[kStopDone] = 1;
+    }
   }
 }
 
@@ -1125,7 +1140,7 @@ extern "C" int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* d, void* s
   const plm_bookkeeping& b = d->book;
   a.book = Bookkeeping{b.mode,       b.k,     b.best_val, b.best_idx,       b.n_tiles, b.rows,
                        b.out,        b.out_cap, b.base,   b.offset,         b.anchor,  b.pending,
-                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len};
+                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len, b.stop};
   a.counter = ctx->counters + (ctx->n_counters - 1);
   a.err = ctx->err;
   int st = verify_validate(a, d->n_rows);
@@ -1149,30 +1164,61 @@ constexpr int kStaticFlagsOffset = 512;  // int32 verdicts [kStaticRows]
 static_assert(kStaticTokensOffset + 8 * kStaticRows <= kStaticFlagsOffset, "static scratch layout");
 static_assert(kStaticFlagsOffset + 4 * kStaticRows <= kStaticScratchBytes, "static scratch layout");
 
-// Word 0: arrival counter (zero at module load; the last cluster of every bookkeeping launch resets it to zero).
-// Word 1: device error word when the caller passes none (first error wins; never cleared, never read back).
+// Word 0: arrival counter. It is zero at module load, and every launch leaves it at zero: each cluster's rank 0
+// arrives exactly once (a wait that runs out of time still reaches the arrival), and the last to arrive resets it.
+// Word 1: device error word when the caller passes none. Errors recorded there cannot be read back through the
+// C ABI; callers that need them pass their own zeroed int32.
 static __device__ __align__(256) unsigned char g_verify_static_scratch[kStaticScratchBytes];
 
-constexpr int kStaticMaxDevices = 64;
-std::atomic<unsigned char*> g_static_scratch_ptr[kStaticMaxDevices];
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Device address of the scratch on the current device, resolved once per device by cudaGetSymbolAddress.
+// The context's process-unique id (cuCtxGetId), or 0 when there is no current context or the driver lacks the call.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  return get_id(ctx, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of the scratch in the current context, resolved by cudaGetSymbolAddress the first time a context
+// calls. The cache is keyed on the context's process-unique id, so a context created after cudaDeviceReset (which
+// reloads the module elsewhere) resolves its own address instead of reusing a stale one.
 int static_scratch(unsigned char** out) {
-  int dev = 0;
-  int st = check_cuda(cudaGetDevice(&dev), "plm_verify_decode_static: cudaGetDevice");
-  if (st != PLM_OK) return st;
-  if (dev < 0 || dev >= kStaticMaxDevices)
-    return fail(PLM_ERR_UNSUPPORTED, "plm_verify_decode_static: device %d beyond %d", dev, kStaticMaxDevices);
-  unsigned char* p = g_static_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    void* addr = nullptr;
-    st = check_cuda(cudaGetSymbolAddress(&addr, g_verify_static_scratch),
-                    "plm_verify_decode_static: cudaGetSymbolAddress(scratch)");
-    if (st != PLM_OK) return st;
-    p = static_cast<unsigned char*>(addr);
-    g_static_scratch_ptr[dev].store(p, std::memory_order_release);
+  static std::mutex mu;
+  static std::map<unsigned long long, unsigned char*> resolved;
+  unsigned long long id = current_context_id();
+  if (id != 0) {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = resolved.find(id);
+    if (it != resolved.end()) {
+      *out = it->second;
+      return PLM_OK;
+    }
   }
-  *out = p;
+  void* addr = nullptr;
+  const int st = check_cuda(cudaGetSymbolAddress(&addr, g_verify_static_scratch),
+                            "plm_verify_decode_static: cudaGetSymbolAddress(scratch)");
+  if (st != PLM_OK) return st;
+  *out = static_cast<unsigned char*>(addr);
+  id = current_context_id();  // the call above made the device's primary context current if none was
+  if (id != 0) {
+    std::lock_guard<std::mutex> lock(mu);
+    resolved[id] = *out;
+  }
   return PLM_OK;
 }
 
@@ -1220,7 +1266,7 @@ extern "C" int plm_verify_decode_static(const plm_verify_desc* d, int32_t* devic
   const plm_bookkeeping& b = d->book;
   a.book = Bookkeeping{b.mode,       b.k,     b.best_val, b.best_idx,       b.n_tiles, b.rows,
                        b.out,        b.out_cap, b.base,   b.offset,         b.anchor,  b.pending,
-                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len};
+                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len, b.stop};
   a.counter = reinterpret_cast<int*>(scratch);
   a.err = device_error != nullptr ? device_error : reinterpret_cast<int*>(scratch) + 1;
   st = verify_validate(a, d->n_rows);

@@ -3,14 +3,16 @@
 One request at a time. A round decodes ``W = k + k*k`` query positions: ``k`` verify rows and ``k`` proposal
 blocks of ``k`` rows. All loop-carried state lives on the device inside the native handle, so a steady round is
 one CUDA-graph replay of ``plm_round`` (forward, lm_head, verify decode, acceptance and commit all in kernels),
-followed by a non-blocking copy of ``base`` and the first output tokens into pinned memory — the reference's
-hot loop (plm/decoder.py:312-324, 414-447) without vLLM, FlexAttention, Triton or torch.compile.
+followed by a non-blocking copy of ``base`` and the done flag into pinned memory. The stop test (token budget,
+end-of-text) of the reference's hot loop (plm/decoder.py:312-324, 414-447) runs on the device, so the host keeps
+rounds queued instead of waiting for each one; no vLLM, FlexAttention, Triton or torch.compile is involved.
 """
 
 from __future__ import annotations
 
 import math
 import time
+from collections import deque
 from dataclasses import dataclass
 
 import torch
@@ -19,7 +21,8 @@ from . import native
 from .model import PLMWeights, rope_cache
 
 AUX_STREAM_LENGTH = 8192  # plm/decoder.py:28
-EOS_WINDOW = 1024         # plm/decoder.py:29
+EOS_WINDOW = 1024         # plm/decoder.py:29: end-of-text is looked for among the first EOS_WINDOW output positions
+ROUNDS_IN_FLIGHT = 2      # steady-round replays queued ahead of the one the host waits for
 
 
 @dataclass
@@ -56,6 +59,12 @@ class RoundDecoder:
             raise native.NativeError("RoundDecoder needs an sm_100a GPU; there is no CPU path")
         self.weights, self.config = weights, weights.config
         c = self.config
+        stored = {t.dtype for t in [weights.embed, weights.lm_head, weights.aux_vocab, *weights.qkv, *weights.o,
+                                     *weights.gate_up, *weights.down]}
+        if stored != {torch.bfloat16}:
+            raise native.NativeError(f"RoundDecoder: weights stored as {sorted(map(str, stored))}; the sm_100a kernels "
+                                     "are built for bfloat16 only (convert explicitly, e.g. RoundConfig(dtype="
+                                     "'bfloat16') or PLMWeights.from_export(..., dtype='bfloat16'))")
         self.k, self.width = k, k + k * k
         self.block_size = block_size
         self.accept_rule, self.threshold = accept_rule, threshold
@@ -107,120 +116,115 @@ class RoundDecoder:
         self.kv_cache = native.device_view(
             st.kv_cache, (c.num_layers, 2, self.num_pages, c.num_kv_heads, block_size, c.head_dim), torch.bfloat16)
         self.table = native.device_view(st.table, (c.vocab, c.aux_vocab), torch.bfloat16)
-        self.base_host = torch.zeros((), dtype=torch.long).pin_memory()
-        self.tokens_host = torch.empty(EOS_WINDOW, dtype=torch.long).pin_memory()
+        self.stop_block = native.device_view(st.stop, (4,), torch.int64)
+        # [base, done] of the newest finished round, copied by every replay into pinned host memory
+        self.poll_host = torch.zeros(2, dtype=torch.long).pin_memory()
         self.aux_seed: int | None = None
         self.graph: torch.cuda.CUDAGraph | None = None
 
     # ------------------------------------------------------------------ construction
     def prepare(self) -> None:
-        """Capture the steady round (plus the pinned-memory reads) into a CUDA graph."""
+        """Capture the steady round and its pinned-memory poll into one CUDA graph. The round runs twice eagerly
+        first, from a harmless state (empty context, base 1, no stop), so every kernel has been loaded and tuned."""
         self._fill_aux(0)
-        # the capture runs the round twice eagerly on a benign state first (offset 0, base 1)
         self.offset_t.zero_()
         self.base_t.fill_(1)
-        stream = torch.cuda.Stream()
-        stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(stream):
-            for _ in range(2):
-                self._round_body()
-        torch.cuda.current_stream().wait_stream(stream)
+        self.handle.set_stop(1 << 62)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self._enqueue_round()
+            self._enqueue_round()
+        torch.cuda.current_stream().wait_stream(side)
         self.handle.check()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            self._round_body()
-        self.graph = graph
+            self._enqueue_round()
         torch.cuda.synchronize()
         self.handle.check()
+        self.graph = graph
 
-    def _round_body(self) -> None:
+    def _enqueue_round(self) -> None:
         self.handle.round()
-        self.base_host.copy_(self.base_t, non_blocking=True)
-        self.tokens_host.copy_(self.out[:EOS_WINDOW], non_blocking=True)
+        self.poll_host[0].copy_(self.base_t, non_blocking=True)
+        self.poll_host[1].copy_(self.stop_block[3], non_blocking=True)
 
     def _fill_aux(self, seed: int) -> None:
-        """The request's auxiliary cell stream: randint(A) from a CUDA generator seeded with ``seed``
-        (plm/decoder.py:407-412 with LogitVoronoiAuxiliary.sample_prior, plm/auxiliary.py:46-48)."""
-        if self.aux_seed == seed:
+        """Per request: A-ary auxiliary cells from a CUDA generator seeded with ``seed`` (the stream of
+        plm/decoder.py:407-412, drawn as LogitVoronoiAuxiliary.sample_prior does, plm/auxiliary.py:46-48). A seed
+        already in the handle is not drawn again."""
+        if seed == self.aux_seed:
             return
-        generator = torch.Generator(device="cuda").manual_seed(seed)
-        cells = torch.randint(self.config.aux_vocab, (AUX_STREAM_LENGTH,), device="cuda", generator=generator,
-                              dtype=torch.long)
+        cells = torch.randint(self.config.aux_vocab, (AUX_STREAM_LENGTH,), dtype=torch.long, device="cuda",
+                              generator=torch.Generator(device="cuda").manual_seed(seed))
         self.handle.set_aux_stream(cells)
-        torch.cuda.current_stream().synchronize()
+        torch.cuda.current_stream().synchronize()  # ``cells`` must outlive the copy
         self.aux_seed = seed
 
     # ------------------------------------------------------------------ the request
-    def _prompt_ids(self, prompt) -> torch.Tensor:
+    def _as_ids(self, prompt) -> torch.Tensor:
         if isinstance(prompt, str):
             if self.tokenizer is None:
                 raise ValueError("a text prompt needs a tokenizer; pass token ids instead")
             prompt = self.tokenizer(prompt).input_ids
-        ids = torch.as_tensor(prompt, dtype=torch.long).flatten()
-        return ids.pin_memory() if not ids.is_cuda else ids
+        ids = torch.as_tensor(prompt, dtype=torch.long).reshape(-1)
+        return ids if ids.is_cuda else ids.pin_memory()
 
-    def _replay_until_tokens(self, num_tokens: int) -> int:
-        replays = 0
-        while True:
-            self.graph.replay()
-            replays += 1
-            event = torch.cuda.Event()
-            event.record()
-            event.synchronize()
-            if int(self.base_host) >= num_tokens:
-                return replays
+    def _decode_rounds(self) -> int:
+        """Replay steady rounds until the device reports the request finished; return how many rounds committed.
 
-    def _replay_until_eos_or_tokens(self, num_tokens: int) -> int:
-        end_of_text, limit = self.eos_token_id, min(num_tokens, EOS_WINDOW)
-        replays, seen = 0, 2  # round 0 confirms exactly one token, so base is 2 when the loop starts
-        while True:
-            self.graph.replay()
-            replays += 1
-            event = torch.cuda.Event()
-            event.record()
-            event.synchronize()
-            base = int(self.base_host)
-            if end_of_text in self.tokens_host[seen:min(base, limit)].tolist() or base >= num_tokens:
-                return replays
-            seen = base
-
-    def _steady_loop(self, num_tokens: int, stop_at_eos: bool) -> tuple[int, float]:
-        start_event, end_event = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start_event.record()
-        if stop_at_eos and self.eos_token_id is not None:
-            replays = self._replay_until_eos_or_tokens(num_tokens)
-        else:
-            replays = self._replay_until_tokens(num_tokens)
-        end_event.record()
-        torch.cuda.synchronize()
-        return replays, start_event.elapsed_time(end_event)
+        The stop test runs on the device, in the bookkeeping of the round that reaches the budget or confirms the
+        end-of-text token, so the host never has to see a round before queuing the next: ``ROUNDS_IN_FLIGHT``
+        replays stay queued, and the host only waits on the oldest. Replays queued behind the stopping round
+        find the done flag and commit nothing, so the output equals the one-round-at-a-time loop's."""
+        first_step = int(self.sequence_step.item())
+        queued: deque[torch.cuda.Event] = deque()
+        finished = False
+        while not finished:
+            while len(queued) < ROUNDS_IN_FLIGHT:
+                self.graph.replay()
+                marker = torch.cuda.Event()
+                marker.record()
+                queued.append(marker)
+            queued.popleft().synchronize()
+            finished = bool(self.poll_host[1])
+        while queued:
+            queued.popleft().synchronize()
+        return int(self.sequence_step.item()) - first_step
 
     @torch.inference_mode()
     def generate(self, prompt, num_tokens: int, *, seed: int = 0, stop_at_eos: bool = True) -> DecodeResult:
-        """Decode ``num_tokens`` tokens after ``prompt`` (text with a tokenizer, or token ids)."""
+        """Decode ``num_tokens`` tokens after ``prompt`` (text with a tokenizer, or token ids): prefill and first
+        token, round 0, then steady rounds until the budget or, with ``stop_at_eos``, the end-of-text token."""
         if self.graph is None:
             self.prepare()
         torch.cuda.synchronize()
-        started = time.perf_counter()
-        ids = self._prompt_ids(prompt)
-        length = ids.numel()
-        if length + num_tokens + 2 * self.width + self.block_size > self.max_seq:
-            raise ValueError(f"prompt ({length}) + tokens ({num_tokens}) exceeds max_model_len {self.max_seq} "
+        t_request = time.perf_counter()
+        ids = self._as_ids(prompt)
+        needed = ids.numel() + num_tokens + 2 * self.width + self.block_size
+        if needed > self.max_seq:
+            raise ValueError(f"prompt ({ids.numel()}) + tokens ({num_tokens}) exceeds max_model_len {self.max_seq} "
                              f"for width {self.width}")
+        eos = self.eos_token_id if stop_at_eos else None
         self._fill_aux(seed)
+        self.handle.set_stop(num_tokens, eos, min(num_tokens, EOS_WINDOW))
         self.handle.load_prompt(ids)
         self.handle.prefill()
         self.handle.round0()
-        replays, steady_ms = self._steady_loop(num_tokens, stop_at_eos)
-        seconds = time.perf_counter() - started
-        tokens = self.out[:num_tokens].tolist()
-        eos = self.eos_token_id
-        if stop_at_eos and eos is not None and eos in tokens:
-            tokens = tokens[: tokens.index(eos) + 1]
-        final_base = int(self.base_t.item())
-        text = self.tokenizer.decode(tokens) if self.tokenizer is not None else ""
-        return DecodeResult(token_ids=tokens, text=text, seconds=seconds, steady_rounds=replays,
-                            steady_ms=steady_ms, steady_tokens=final_base - 2)
+        t_steady, t_done = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_steady.record()
+        rounds = self._decode_rounds()
+        t_done.record()
+        torch.cuda.synchronize()
+        seconds = time.perf_counter() - t_request
+        produced = self.out[:num_tokens].tolist()
+        if eos is not None and eos in produced:
+            produced = produced[: produced.index(eos) + 1]
+        committed = int(self.base_t.item())  # round 0 leaves base at 2, so the steady rounds added committed - 2
+        return DecodeResult(token_ids=produced,
+                            text=self.tokenizer.decode(produced) if self.tokenizer is not None else "",
+                            seconds=seconds, steady_rounds=rounds, steady_ms=t_steady.elapsed_time(t_done),
+                            steady_tokens=committed - 2)
 
     def proposal_argmax(self, rows: int) -> list[int]:
         """Argmax token (first index on ties) of forward rows [0, rows) from the lm_head's per-tile partials of the

@@ -176,7 +176,10 @@ class PLMWeights:
         return out
 
     @classmethod
-    def from_export(cls, directory: str | Path, device: str | torch.device = "cuda") -> "PLMWeights":
+    def from_export(cls, directory: str | Path, device: str | torch.device = "cuda",
+                    dtype: str | None = None) -> "PLMWeights":
+        """Load an export in its own ``torch_dtype``, or converted to ``dtype`` when one is given (the conversion
+        is recorded in ``config.dtype``; nothing is reinterpreted)."""
         from safetensors import safe_open
 
         directory = Path(directory)
@@ -184,6 +187,8 @@ class PLMWeights:
         if "PLMForCausalLM" not in cfg.get("architectures", []):
             raise ValueError(f"{directory} is not a PLM export (architectures {cfg.get('architectures')})")
         c = PLMConfig.from_hf_config(cfg, name=directory.name)
+        if dtype is not None:
+            c.dtype = dtype
         dtype = DTYPES.get(c.dtype)
         if dtype is None:
             raise ValueError(f"model dtype {c.dtype} is not supported (bfloat16 or float16)")

@@ -54,7 +54,7 @@ class Bookkeeping(ctypes.Structure):
                 ("n_tiles", c_int32), ("rows", c_int32), ("out", c_void_p), ("out_cap", c_int64),
                 ("base", c_void_p), ("offset", c_void_p), ("anchor", c_void_p), ("pending", c_void_p),
                 ("round_sequence", c_void_p), ("seq_cap", c_int64), ("sequence_step", c_void_p),
-                ("prompt_len", c_int64)]
+                ("prompt_len", c_int64), ("stop", c_void_p)]
 
 
 class VerifyDesc(ctypes.Structure):
@@ -125,7 +125,7 @@ class StatePtrs(ctypes.Structure):
                 ("best_val", c_void_p), ("best_idx", c_void_p), ("verify", c_void_p), ("flags", c_void_p),
                 ("hidden_normed", c_void_p), ("kv_cache", c_void_p), ("table", c_void_p),
                 ("out_capacity", c_int64), ("seq_capacity", c_int64), ("aux_len", c_int64), ("plane_elems", c_int64),
-                ("width", c_int32), ("lm_tiles", c_int32), ("row_capacity", c_int32)]
+                ("width", c_int32), ("lm_tiles", c_int32), ("row_capacity", c_int32), ("stop", c_void_p)]
 
 
 _lib: ctypes.CDLL | None = None
@@ -152,6 +152,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_set_block_table": [c_void_p, POINTER(c_int32), c_int32],
     "plm_set_aux_stream": [c_void_p, c_void_p, c_int64, c_void_p],
     "plm_load_prompt": [c_void_p, c_void_p, c_int64, c_void_p],
+    "plm_set_stop": [c_void_p, c_int64, c_int64, c_int64, c_void_p],
     "plm_prefill": [c_void_p, c_void_p],
     "plm_round0": [c_void_p, c_void_p],
     "plm_round": [c_void_p, c_void_p],
@@ -336,6 +337,11 @@ class Handle:
     def load_prompt(self, ids, stream=None) -> None:
         check(library().plm_load_prompt(self.handle, ids.data_ptr(), ids.numel(), stream_handle(stream)),
               "plm_load_prompt")
+
+    def set_stop(self, max_tokens: int, eos_token: int | None = None, eos_window: int = 0, stream=None) -> None:
+        """The request's stop block (plm_set_stop): budget, end-of-text id (None: none) and its window."""
+        check(library().plm_set_stop(self.handle, int(max_tokens), -1 if eos_token is None else int(eos_token),
+                                     int(eos_window), stream_handle(stream)), "plm_set_stop")
 
     def prefill(self, stream=None) -> None:
         check(library().plm_prefill(self.handle, stream_handle(stream)), "plm_prefill")

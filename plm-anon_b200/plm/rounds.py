@@ -35,6 +35,13 @@ def is_plm_export(model: str) -> bool:
     return config.exists() and "PLMForCausalLM" in json.loads(config.read_text()).get("architectures", [])
 
 
+def export_dtype(model: str) -> str:
+    """The ``torch_dtype`` an export directory declares (float16 when it declares none, the reference's default,
+    plm/rounds.py:50)."""
+    config = json.loads((Path(model) / "config.json").read_text())
+    return str(config.get("torch_dtype", "float16"))
+
+
 def scheme_kind(scheme: str) -> str | None:
     config = json.loads((Path(scheme) / "config.json").read_text())
     return config.get("auxiliary_scheme", {}).get("kind")
@@ -42,13 +49,15 @@ def scheme_kind(scheme: str) -> str | None:
 
 @dataclass
 class RoundConfig:
-    """``model`` is an export directory or ``synthetic:<shape>[:seed=<n>]`` (e.g. ``synthetic:plm-1.3b``)."""
+    """``model`` is an export directory or ``synthetic:<shape>[:seed=<n>]`` (e.g. ``synthetic:plm-1.3b``).
+    ``dtype`` None keeps the export's own ``torch_dtype`` (bfloat16 for synthetic models); a dtype the native
+    kernels are not built for makes ``build`` raise ``NativeError``. Naming one converts the weights explicitly."""
     model: str
     setting: str = "posttrain"
     mode: str = "fast"
     match: str = "exact"
     k: int | None = None
-    dtype: str = "bfloat16"
+    dtype: str | None = None
     max_model_len: int = 4096
 
     def __post_init__(self) -> None:
@@ -60,6 +69,10 @@ class RoundConfig:
             raise ValueError(f"--mode {self.mode!r}: fast or default")
         if self.k is None:
             self.k = SETTINGS[self.setting].default_k[self.match]
+        if self.dtype is None and self.model.startswith("synthetic:"):
+            self.dtype = "bfloat16"
+        elif self.dtype is None and (Path(self.model) / "config.json").exists():
+            self.dtype = export_dtype(self.model)
 
     @property
     def accept(self) -> tuple[str, float | None]:
@@ -86,15 +99,17 @@ class RoundConfig:
                 if extra.startswith("seed="):
                     seed = int(extra[5:])
             return PLMWeights.random(shape_config(parts[1], dtype=self.dtype), seed=seed)
-        return PLMWeights.from_export(self.model)
+        return PLMWeights.from_export(self.model, dtype=self.dtype)
 
     def build(self, gpu_memory_utilization: float = 0.25, kv_cache_bytes: int = 1 << 30, block_size: int = 64):
         """The prepared RoundDecoder (plm/rounds.py:71-81). ``gpu_memory_utilization`` is accepted for drop-in
         compatibility; the KV pool is sized by ``kv_cache_bytes``."""
         from .decoder import RoundDecoder
+        from .native import NativeError
 
         if self.dtype != "bfloat16":
-            raise NotImplementedError(f"dtype {self.dtype}: the native kernels are built for bfloat16")
+            raise NativeError(f"dtype {self.dtype}: the native kernels are built for bfloat16; pass "
+                              "RoundConfig(dtype='bfloat16') to convert the weights")
         rule, threshold = self.accept
         tokenizer = None
         if not self.model.startswith("synthetic:"):

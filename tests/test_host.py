@@ -148,3 +148,23 @@ def test_generate_cli_surface(tmp_path):
     args.ar, args.fdv2 = False, True
     with pytest.raises(SystemExit):
         generate.build_generator(args)
+
+
+def test_float16_export_keeps_its_dtype(tmp_path):
+    """A float16 export loads as float16 (never relabelled as bfloat16); a dtype is converted only when asked for,
+    and RoundConfig takes the export's own dtype unless one is given."""
+    from plm.model import PLMWeights, shape_config
+    from plm.rounds import RoundConfig
+
+    cfg = shape_config("plm-tiny", vocab=1000, aux_vocab=64, dtype="float16")
+    w = PLMWeights.random(cfg, seed=1, device="cpu")
+    export = w.save_export(tmp_path / "fp16")
+    kept = PLMWeights.from_export(export, device="cpu")
+    assert kept.config.dtype == "float16" and kept.embed.dtype == torch.float16 and kept.qkv[0].dtype == torch.float16
+    assert torch.equal(kept.qkv[1], w.qkv[1])
+    converted = PLMWeights.from_export(export, device="cpu", dtype="bfloat16")
+    assert converted.config.dtype == "bfloat16" and converted.o[0].dtype == torch.bfloat16
+    assert torch.equal(converted.o[0], w.o[0].bfloat16())
+    assert RoundConfig(model=str(export)).dtype == "float16"
+    assert RoundConfig(model=str(export), dtype="bfloat16").dtype == "bfloat16"
+    assert RoundConfig(model="synthetic:plm-tiny").dtype == "bfloat16"
