@@ -1,16 +1,11 @@
 // Paged attention of the round's query rows under the round mask (replaces FlexAttention with the block mask of
 // plm/mask.py:23-29 as vLLM's backend calls it: vllm/v1/attention/backends/flex_attention.py:1070-1205).
 //
-// Grid (head, KV split, 128-row query tile), 4 warps; thread t owns query row t of the tile, which is TMEM lane t.
-// A CTA walks its keys in chunks of up to 128 (two 64-key tiles):
-//   - every thread gathers 16-byte pieces of the chunk's K and V rows through the block table with cp.async into
-//     shared memory, in the 128-byte-swizzled layout the tensor cores read (a double-buffered ring);
-//   - one thread issues S = Q K^T (tcgen05.mma, M = 128 query rows, N = the chunk's keys, K = head_dim) into TMEM;
-//   - each thread loads its row of S from TMEM, applies the scale and the mask, and forms the online softmax in
-//     base 2: P = 2^(S - m) rounded to bf16 is written to shared memory, the running sum l in fp32; when the row
-//     maximum grows, the row of O in TMEM is rescaled first;
-//   - one thread issues O += P V (tcgen05.mma, N = head_dim, K = the chunk's keys; V is read MN-major) into TMEM.
-// The KV splits of one (head, query tile) form a thread-block cluster whose unnormalised partials (O, m, l) are
+// Grid (head, KV split, 64-row query tile), 4 warps; warp w owns query rows [16w, 16w + 16) of the tile.
+// Keys are visited in tiles of 64: each tile's K and V rows are gathered page by page through the block table
+// with 16-byte cp.async into XOR-swizzled shared memory (double buffered), S = Q K^T and O += P V run on tensor
+// cores (mma.m16n8k16 bf16, fp32 accumulation; P is rounded to bf16 for the second product), and the softmax is
+// online in base 2. The KV splits of one (head, query tile) form a thread-block cluster whose partial results are
 // combined through distributed shared memory. Key kv is visible to row r (logical query offset + r) iff
 //     kv < offset + rows  and  (kv < offset  or  kv - offset <= depth[r]
 //                                 or  (kv - offset >= own_start[r]  and  kv <= offset + r)),
@@ -24,14 +19,28 @@ namespace plm {
 namespace {
 
 constexpr int kKeysPerTile = 64;
-constexpr int kTilesPerChunk = 2;
-constexpr int kChunkKeys = kKeysPerTile * kTilesPerChunk;
 constexpr int kAttnThreads = 128;
-constexpr int kQRowsPerCta = 128;
+constexpr int kQRowsPerCta = 64;
+constexpr int kStages = 3;           // K/V tiles in flight per CTA (two CTAs still share an SM)
 constexpr int kMaxPageSlice = 1024;  // block-table entries staged per CTA (keys per CTA <= 1023 pages)
-constexpr uint32_t kAttnTmemCols = 256;  // S: columns [0, 128); O: columns [128, 128 + head_dim)
-constexpr uint32_t kTmemO = 128;
 
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 // 2^x by the special-function unit (relative error ~2^-22; -inf gives +0): the softmax's exponentials.
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -43,60 +52,26 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Byte offset of (row, 16-byte chunk) in a swizzled tile with HD/8 chunks per row.
 template <int HD>
-struct AttnSmem {
-  static constexpr int KB = HD / 64;                    // 64-element k-blocks of a head row
-  static constexpr int Q_BYTES = KB * kQRowsPerCta * 128;
-  static constexpr int KV_BLOCK = kChunkKeys * 128;     // one k-block of a chunk's K (or V) rows
-  static constexpr int K_BYTES = KB * KV_BLOCK;
-  static constexpr int BUF_BYTES = 2 * K_BYTES;         // K then V
-  static constexpr int P_BYTES = kTilesPerChunk * kQRowsPerCta * 128;
-  static constexpr int Q_OFF = 0;
-  static constexpr int RING_OFF = Q_OFF + Q_BYTES;
-  static constexpr int P_OFF = RING_OFF + 2 * BUF_BYTES;
-  static constexpr int PAGES_OFF = P_OFF + P_BYTES;
-  static constexpr int BAR_OFF = PAGES_OFF + kMaxPageSlice * 4;
-  static constexpr int SMEM = 1024 + BAR_OFF + 64;
-  // the split combine reuses the ring: O partial [128][HD] fp32, then (m, l) [128][2], then the weights
-  static_assert(kQRowsPerCta * HD * 4 + kQRowsPerCta * 2 * 4 + kQRowsPerCta * 9 * 4 <= 2 * BUF_BYTES, "combine");
-  static_assert(SMEM <= 227 * 1024, "shared memory");
-  static_assert(Q_BYTES % 1024 == 0 && KV_BLOCK % 1024 == 0 && P_BYTES % 1024 == 0, "1024-byte swizzle atoms");
-};
-
-// Byte offset of 16-byte chunk c (of 8 per 128-byte row) of row `row` in a 128-byte-swizzled operand block.
-__device__ __forceinline__ uint32_t swz128(int row, int c) { return uint32_t(row * 128 + ((c ^ (row & 7)) << 4)); }
+__device__ __forceinline__ int swz(int row, int chunk) {
+  return row * (HD * 2) + ((chunk ^ (row & 7)) << 4);
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const AttnArgs a) {
-  using L = AttnSmem<HD>;
-  constexpr int PIECES = HD / 8;                       // 16-byte pieces of a head row
-  constexpr int RSTEP = kAttnThreads / PIECES;         // rows one pass of the CTA covers
-  constexpr int ITER = kKeysPerTile / RSTEP;           // rows per thread per 64-key tile
-  constexpr uint32_t IDESC_S = umma_idesc_f16(128, kChunkKeys, true);
-  constexpr uint32_t IDESC_S_HALF = umma_idesc_f16(128, kKeysPerTile, true);
-  constexpr uint32_t IDESC_O = umma_idesc_f16(128, HD, true) | kUmmaBMajorMN;
+  constexpr int CH = HD / 8;
+  constexpr int TILE_BYTES = kKeysPerTile * HD * 2;
+  constexpr int NT = kKeysPerTile / 8;  // key n-tiles per tile
+  constexpr int KS = HD / 16;           // k-steps over the head dim
+  extern __shared__ __align__(128) uint8_t smem[];
+  auto kbuf = [&](int slot) { return smem + (2 * slot) * TILE_BYTES; };  // ring slot: K tile, then V tile
+  auto vbuf = [&](int slot) { return smem + (2 * slot + 1) * TILE_BYTES; };
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* q_s = smem + L::Q_OFF;
-  uint8_t* p_s = smem + L::P_OFF;
-  int* pages = reinterpret_cast<int*>(smem + L::PAGES_OFF);
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* o_bar = s_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_bar + 1);
-  auto k_buf = [&](int b) { return smem + L::RING_OFF + b * L::BUF_BYTES; };
-  auto v_buf = [&](int b) { return smem + L::RING_OFF + b * L::BUF_BYTES + L::K_BYTES; };
-
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;
   const int head = blockIdx.x, split = blockIdx.y, qt = blockIdx.z;
   const int group = head / (a.num_heads / a.num_kv_heads);
-
-  if (tid == 0) {
-    mbar_init(s_bar, 1);
-    mbar_init(o_bar, 1);
-    fence_barrier_init();
-  }
-  if (warp == 0) tmem_alloc(tmem_slot, kAttnTmemCols);
 
   // Before the dependency wait: everything the previous kernel does not write. The offset comes from an earlier
   // kernel (the last round's commit, or a copy before a prefill), the block table and the layout are static, and
@@ -110,7 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   const int t0 = n_tiles - int(int64_t(a.splits - split) * n_tiles / a.splits);
   const int t1 = n_tiles - int(int64_t(a.splits - split - 1) * n_tiles / a.splits);
   const int n_local = t1 - t0;
-  const int n_chunks = (n_local + kTilesPerChunk - 1) / kTilesPerChunk;
+  int* pages = reinterpret_cast<int*>(smem + 2 * kStages * TILE_BYTES);
   const int64_t lp0 = (int64_t(t0) * kKeysPerTile) >> a.page_shift;
   const int n_pages = n_local > 0 ? int(((int64_t(t1) * kKeysPerTile - 1) >> a.page_shift) - lp0 + 1) : 0;
   const bool staged_pages = n_pages <= kMaxPageSlice;
@@ -118,26 +93,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     const int64_t lp = lp0 + i;
     pages[i] = lp < a.max_pages ? a.block_table[lp] : -1;
   }
-  const int row = qt * kQRowsPerCta + tid;  // this thread's query row
-  const bool live = row < a.rows;
-  const int dep = live ? a.depth[row] : -1, own = live ? a.own_start[row] : (1 << 30);
-  tc_fence_before();
+  const int r0 = qt * kQRowsPerCta + warp * 16 + gq, r1 = r0 + 8;
+  const int dep0 = r0 < a.rows ? a.depth[r0] : -1, own0 = r0 < a.rows ? a.own_start[r0] : (1 << 30);
+  const int dep1 = r1 < a.rows ? a.depth[r1] : -1, own1 = r1 < a.rows ? a.own_start[r1] : (1 << 30);
   __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t t_lane = uint32_t(warp * 32) << 16;  // this warp's TMEM lane slice
 
   const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
   const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache);
-  // Thread tid copies 16-byte piece tid % PIECES of tile rows tid / PIECES + u * RSTEP: its page lookups are issued
-  // together, then per-thread constant address arithmetic; a bad page is recorded once per tile.
-  const int my_piece = tid % PIECES, my_row0 = tid / PIECES;
-  const size_t head_off = size_t(group) * a.page_size * HD + size_t(my_piece) * 8;  // elements
+  // Thread tid always copies 16-byte chunk tid % CH of tile rows tid / CH + u * RSTEP: its page lookups are issued
+  // together, then 32-bit-cheap address arithmetic from per-thread constants; a bad page is recorded once per tile.
+  constexpr int ITER = (kKeysPerTile * CH) / kAttnThreads;
+  constexpr int RSTEP = kAttnThreads / CH;
+  const int my_chunk = tid % CH, my_row0 = tid / CH;
+  const size_t head_off = size_t(group) * a.page_size * HD + size_t(my_chunk) * 8;  // elements
   const size_t page_stride = size_t(a.num_kv_heads) * a.page_size * HD;            // elements per page
-  const uint32_t dst_piece = uint32_t((my_piece >> 3) * L::KV_BLOCK);
-  // Tile t (absolute) into half `half` of ring buffer `buf`; `context_only`: only when the whole tile lies below
-  // offset (issued before the dependency wait), else only when it does not (after it).
-  auto issue_tile = [&](int t, int buf, int half) {
+  auto issue = [&](int t, int buf) {  // tile t (absolute) into ring slot buf; one commit group per call
     const int64_t kv0 = int64_t(t) * kKeysPerTile + my_row0;
     int pg[ITER];
 #pragma unroll
@@ -149,230 +119,219 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     bool bad = false;
 #pragma unroll
     for (int u = 0; u < ITER; ++u) {
-      const int r = half * kKeysPerTile + my_row0 + u * RSTEP;  // key row inside the chunk
+      const int row = my_row0 + u * RSTEP;
       const bool valid = pg[u] >= 0 && pg[u] < a.num_pages;
       bad |= pg[u] != -2 && !valid;
       const size_t src =
           valid ? size_t(pg[u]) * page_stride + head_off + size_t((kv0 + u * RSTEP) & (a.page_size - 1)) * HD : 0;
-      const uint32_t dst = dst_piece + swz128(r, my_piece & 7);
-      cp_async_16(k_buf(buf) + dst, kc + src, valid);
-      cp_async_16(v_buf(buf) + dst, vc + src, valid);
+      cp_async_16(kbuf(buf) + swz<HD>(row, my_chunk), kc + src, valid);
+      cp_async_16(vbuf(buf) + swz<HD>(row, my_chunk), vc + src, valid);
     }
     if (bad) record_error(a.err, kErrBadIndex);
   };
-  auto tile_in_context = [&](int t) { return int64_t(t + 1) * kKeysPerTile <= offset; };
-  auto issue_chunk = [&](int c, int mode) {  // mode 0: context tiles only, 1: the others, 2: all
-    for (int h = 0; h < kTilesPerChunk; ++h) {
-      const int t = t0 + c * kTilesPerChunk + h;
-      if (t >= t1) break;
-      const bool ctx_tile = tile_in_context(t);
-      if (mode == 2 || (mode == 0) == ctx_tile) issue_tile(t, c & 1, h);
-    }
-  };
-  if (n_chunks > 0) issue_chunk(0, 0);
+  // Pipeline prologue: kStages - 1 commit groups. Tiles lying wholly in the context go out before the wait.
+  int64_t whole = offset / kKeysPerTile - t0;  // tiles of this CTA whose last key lies below offset
+  whole = whole < 0 ? 0 : (whole > n_local ? n_local : whole);
+  const int ctx_tiles = int(whole);
+  int issued = 0;
+  for (; issued < kStages - 1 && issued < ctx_tiles; ++issued) {
+    issue(t0 + issued, issued);
+    cp_async_commit();
+  }
 
   grid_dependency_wait();
   allow_dependents();
 
-  // Q rows of the tile (rows past a.rows zero-filled), then the rest of chunk 0: commit group 0. Chunk 1: group 1.
-  {
-    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
-    const size_t q_stride = size_t(a.num_heads) * HD;
-    for (int idx = tid; idx < kQRowsPerCta * PIECES; idx += kAttnThreads) {
-      const int r = idx / PIECES, pc = idx % PIECES;
-      const int gr = qt * kQRowsPerCta + r;
-      const bool ok = gr < a.rows;
-      const size_t src = ok ? size_t(gr) * q_stride + size_t(head) * HD + size_t(pc) * 8 : 0;
-      cp_async_16(q_s + (pc >> 3) * (kQRowsPerCta * 128) + swz128(r, pc & 7), q + src, ok);
-    }
-  }
-  if (n_chunks > 0) issue_chunk(0, 1);
-  cp_async_commit();
-  if (n_chunks > 1) issue_chunk(1, 2);
-  cp_async_commit();
-
-  const float scale = a.scale_log2;
-  float m_run = -INFINITY, l_run = 0.f;
-  for (int c = 0; c < n_chunks; ++c) {
-    const int buf = c & 1;
-    const int tiles = min(kTilesPerChunk, t1 - (t0 + c * kTilesPerChunk));
-    const int n_keys = tiles * kKeysPerTile;
-    const int64_t key0 = int64_t(t0 + c * kTilesPerChunk) * kKeysPerTile;
-    cp_async_wait<1>();          // chunk c (and Q) landed for this thread
-    fence_proxy_async_shared();  // ... and is visible to the tensor cores
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-      const uint32_t q_addr = smem_u32(q_s), k_addr = smem_u32(k_buf(buf));
-#pragma unroll
-      for (int kk = 0; kk < HD / 16; ++kk) {
-        const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (kQRowsPerCta * 128) + (kk & 3) * 32);
-        const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * L::KV_BLOCK + (kk & 3) * 32);
-        umma_f16(tmem, ad, bd, n_keys == kChunkKeys ? IDESC_S : IDESC_S_HALF, kk > 0 ? 1u : 0u);
-      }
-      umma_commit(s_bar);
-    }
-    __syncwarp();
-    mbar_wait(s_bar, uint32_t(c & 1), a.err, kErrTimeoutDone);
-    tc_fence_after();
-
-    // This thread's row of S: scale, mask, row maximum.
-    uint32_t sr[kChunkKeys];
-    tmem_ld_32cols_async(tmem + t_lane + 0, *reinterpret_cast<uint32_t(*)[32]>(sr));
-    tmem_ld_32cols_async(tmem + t_lane + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-    if (n_keys > kKeysPerTile) {
-      tmem_ld_32cols_async(tmem + t_lane + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-      tmem_ld_32cols_async(tmem + t_lane + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-    }
-    tmem_ld_wait();
-    const bool need_mask = key0 + n_keys > offset;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kChunkKeys; ++j) {  // in place: sr[j] becomes the scaled, masked score
-      const float v = __uint_as_float(sr[j]) * scale;
-      bool vis = live && j < n_keys;
-      if (need_mask && vis) {
-        const int64_t kv = key0 + j;
-        vis = kv < seq_len;
-        if (vis && kv >= offset) {
-          const int64_t rel = kv - offset;
-          vis = rel <= dep || (rel >= own && rel <= row);
-        }
-      }
-      const float sv = vis ? v : -INFINITY;
-      sr[j] = __float_as_uint(sv);
-      mx = fmaxf(mx, sv);
-    }
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = m_new == -INFINITY ? 1.f : ex2(m_run - m_new);
-    m_run = m_new;
-    // before P is overwritten, the previous chunk's P V must have read it
-    if (c > 0) {
-      mbar_wait(o_bar, uint32_t((c - 1) & 1), a.err, kErrTimeoutDone);
-      tc_fence_after();
-    }
-    // P = 2^(S - m) for this row, rounded to bf16, into the row's 128-byte rows of the P operand
-    float psum = 0.f;
-#pragma unroll
-    for (int j8 = 0; j8 < kChunkKeys / 8; ++j8) {
-      uint32_t w[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p0 = m_new == -INFINITY ? 0.f : ex2(__uint_as_float(sr[8 * j8 + 2 * e]) - m_new);
-        const float p1 = m_new == -INFINITY ? 0.f : ex2(__uint_as_float(sr[8 * j8 + 2 * e + 1]) - m_new);
-        psum += p0 + p1;
-        w[e] = pack_bf16(p0, p1);
-      }
-      if (j8 * 8 < n_keys)
-        *reinterpret_cast<uint4*>(p_s + (j8 >> 3) * (kQRowsPerCta * 128) + swz128(tid, j8 & 7)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    l_run = l_run * alpha + psum;
-    // Rescale this row of O when its maximum grew (the whole warp joins the TMEM round trip if any lane needs it).
-    if (c > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-      for (int c32 = 0; c32 < HD / 32; ++c32) {
-        uint32_t o[32];
-        tmem_ld_32cols_async(tmem + t_lane + kTmemO + c32 * 32, o);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-        tmem_st_32cols(tmem + t_lane + kTmemO + c32 * 32, o);
-      }
-    }
-    fence_proxy_async_shared();  // P is read by the tensor cores next
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-      const uint32_t p_addr = smem_u32(p_s), v_addr = smem_u32(v_buf(buf));
-      for (int kk = 0; kk < n_keys / 16; ++kk) {
-        const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (kQRowsPerCta * 128) + (kk & 3) * 32);
-        const uint64_t bd = umma_desc_sw128_mn(v_addr + kk * 16 * 128, L::KV_BLOCK, 1024);
-        umma_f16(tmem + kTmemO, ad, bd, IDESC_O, (c > 0 || kk > 0) ? 1u : 0u);
-      }
-      umma_commit(o_bar);
-    }
-    __syncwarp();
-    // The ring buffer of chunk c is free once its P V has completed: chunk c + 2 goes there.
-    if (c + 2 < n_chunks) {
-      mbar_wait(o_bar, uint32_t(c & 1), a.err, kErrTimeoutDone);
-      issue_chunk(c + 2, 2);
-    }
+  for (; issued < kStages - 1; ++issued) {
+    if (issued < n_local) issue(t0 + issued, issued);
     cp_async_commit();
   }
-  if (n_chunks > 0) mbar_wait(o_bar, uint32_t((n_chunks - 1) & 1), a.err, kErrTimeoutDone);
-  cp_async_wait<0>();
-  tc_fence_after();
 
-  // This thread's row of O (unnormalised) from TMEM.
-  float o[HD];
+  // ---- query fragments (A operand, rows r0 and r0 + 8 of this warp) ----
+  const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  const size_t q_stride = size_t(a.num_heads) * HD;
+  uint32_t qf[KS][4];
 #pragma unroll
-  for (int c32 = 0; c32 < HD / 32; ++c32) tmem_ld_32cols_async(tmem + t_lane + kTmemO + c32 * 32,
-                                                               *reinterpret_cast<uint32_t(*)[32]>(o + c32 * 32));
-  tmem_ld_wait();
-  if (n_chunks == 0) {
+  for (int kk = 0; kk < KS; ++kk) {
+    const int col = kk * 16 + 2 * tq;
+    auto ld = [&](int rr, int c) -> uint32_t {
+      if (rr >= a.rows) return 0u;
+      return *reinterpret_cast<const uint32_t*>(q + size_t(rr) * q_stride + size_t(head) * HD + c);
+    };
+    qf[kk][0] = ld(r0, col);
+    qf[kk][1] = ld(r1, col);
+    qf[kk][2] = ld(r0, col + 8);
+    qf[kk][3] = ld(r1, col + 8);
+  }
+
+  float o[HD / 8][4];
 #pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float scale = a.scale_log2;
+
+  for (int i = 0; i < n_local; ++i) {
+    const int t = t0 + i, buf = i % kStages;
+    cp_async_wait<kStages - 2>();  // tile i has landed (one group is committed per tile, empty ones included)
+    __syncthreads();               // ... for every thread, and slot (i - 1) % kStages is free again
+    if (i + kStages - 1 < n_local) issue(t + kStages - 1, (i + kStages - 1) % kStages);
+    cp_async_commit();
+    const uint8_t* kb = kbuf(buf);
+    const uint8_t* vb = vbuf(buf);
+
+    float s[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+      for (int jj = 0; jj < NT / 2; ++jj) {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = jj * 16 + (mi >> 1) * 8 + rr;
+        const int chunk = kk * 2 + (mi & 1);
+        uint32_t b[4];
+        ldmatrix_x4(b, kb + swz<HD>(row, chunk));
+        mma_bf16(s[2 * jj], qf[kk], b[0], b[1]);
+        mma_bf16(s[2 * jj + 1], qf[kk], b[2], b[3]);
+      }
+    }
+    // scale + mask
+    const int64_t kbase = int64_t(t) * kKeysPerTile;
+    const bool need_mask = kbase + kKeysPerTile > offset;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = s[j][e] * scale;
+        if (need_mask) {
+          const int64_t kv = kbase + j * 8 + 2 * tq + (e & 1);
+          const int rr = e < 2 ? r0 : r1;
+          const int dep = e < 2 ? dep0 : dep1, own = e < 2 ? own0 : own1;
+          bool vis = kv < seq_len;
+          if (vis && kv >= offset) {
+            const int64_t rel = kv - offset;
+            vis = rel <= dep || (rel >= own && rel <= rr);
+          }
+          if (!vis) v = -INFINITY;
+        }
+        s[j][e] = v;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float c0 = n0 == -INFINITY ? 1.f : ex2(m0 - n0);
+    const float c1 = n1 == -INFINITY ? 1.f : ex2(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      s[j][0] = n0 == -INFINITY ? 0.f : ex2(s[j][0] - n0);
+      s[j][1] = n0 == -INFINITY ? 0.f : ex2(s[j][1] - n0);
+      s[j][2] = n1 == -INFINITY ? 0.f : ex2(s[j][2] - n1);
+      s[j][3] = n1 == -INFINITY ? 0.f : ex2(s[j][3] - n1);
+      ps0 += s[j][0] + s[j][1];
+      ps1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * c0 + ps0;
+    l1 = l1 * c1 + ps1;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      o[j][0] *= c0;
+      o[j][1] *= c0;
+      o[j][2] *= c1;
+      o[j][3] *= c1;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < kKeysPerTile / 16; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int nn = 0; nn < HD / 16; ++nn) {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = kk * 16 + (mi & 1) * 8 + rr;
+        const int chunk = nn * 2 + (mi >> 1);
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, vb + swz<HD>(row, chunk));
+        mma_bf16(o[2 * nn], pa, b[0], b[1]);
+        mma_bf16(o[2 * nn + 1], pa, b[2], b[3]);
+      }
+    }
   }
-  tc_fence_before();
-  __syncthreads();  // every thread has its row: TMEM and the ring are free
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kAttnTmemCols);
-  }
+  cp_async_wait<0>();
+  __syncthreads();  // the ring is reused by the split combine below
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
   const size_t out_stride = size_t(a.num_heads) * HD;
-  // Eight consecutive output elements (one 16-byte chunk) of row `r`, columns col .. col + 7 of the head output:
-  // row-major, or inside the row tiles (the 16-byte chunk of its k-block).
+  // Element (row, col) of the output: row-major, or inside the row tiles (the 16-byte chunk of its k-block, then
+  // the position within the chunk; writers store at most one chunk's worth at a time).
   uint8_t* tiles = static_cast<uint8_t*>(a.row_tiles);
-  auto out_chunk = [&](int r, int col) -> uint4* {
-    if (tiles != nullptr) return reinterpret_cast<uint4*>(tiles) + row_tile_chunk(col >> 6, r, (col >> 3) & 7, a.tile_rows);
-    return reinterpret_cast<uint4*>(out + size_t(r) * out_stride + col);
+  auto out_at = [&](int row, int col) -> __nv_bfloat16* {
+    if (tiles != nullptr)
+      return reinterpret_cast<__nv_bfloat16*>(tiles + row_tile_chunk(col >> 6, row, (col >> 3) & 7, a.tile_rows) * 16) +
+             (col & 7);
+    return out + size_t(row) * out_stride + col;
   };
   if (a.splits == 1) {
-    if (live) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
-      for (int j = 0; j < HD / 8; ++j)
-        *out_chunk(row, head * HD + 8 * j) =
-            make_uint4(pack_bf16(o[8 * j] * inv, o[8 * j + 1] * inv), pack_bf16(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
-                       pack_bf16(o[8 * j + 4] * inv, o[8 * j + 5] * inv), pack_bf16(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+    for (int j = 0; j < HD / 8; ++j) {
+      const int col = head * HD + j * 8 + 2 * tq;
+      if (r0 < a.rows)
+        *reinterpret_cast<__nv_bfloat162*>(out_at(r0, col)) = __floats2bfloat162_rn(o[j][0] * inv0, o[j][1] * inv0);
+      if (r1 < a.rows)
+        *reinterpret_cast<__nv_bfloat162*>(out_at(r1, col)) = __floats2bfloat162_rn(o[j][2] * inv1, o[j][3] * inv1);
     }
     return;
   }
 
   // ---- split partials, combined over the cluster of the (head, query tile) ----
-  // Each CTA leaves its unnormalised partial (O, m, l) in its own shared memory (the ring is free now); after a
-  // cluster barrier rank q combines its share of the live rows over all ranks in rank order through distributed
-  // shared memory; a second barrier keeps every partial alive until all rows are combined.
-  float* po = reinterpret_cast<float*>(smem + L::RING_OFF);         // [128][HD]
-  float* pml = po + kQRowsPerCta * HD;                              // [128][2]
-  float* wts = pml + kQRowsPerCta * 2;                              // [rows of this rank][S + 1]
-  if (live) {
+  // Each CTA leaves its unnormalised partial (O, m, l) in its own shared memory (the K/V buffers are free now);
+  // after a cluster barrier rank r combines rows [r * 64 / S, (r + 1) * 64 / S) over all ranks in rank order through
+  // distributed shared memory; a second barrier keeps every partial alive until all rows are combined.
+  float* po = reinterpret_cast<float*>(smem);                              // [64][HD]
+  float* pml = reinterpret_cast<float*>(smem + kQRowsPerCta * HD * 4);     // [64][2]
+  float* wts = pml + kQRowsPerCta * 2;                                     // [64 / S rows][S] weights, then 1/L
+  const int lr0 = warp * 16 + gq, lr1 = lr0 + 8;
 #pragma unroll
-    for (int j = 0; j < HD / 4; ++j)
-      *reinterpret_cast<float4*>(po + tid * HD + 4 * j) = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-    *reinterpret_cast<float2*>(pml + tid * 2) = make_float2(m_run, l_run);
+  for (int j = 0; j < HD / 8; ++j) {
+    const int col = j * 8 + 2 * tq;
+    *reinterpret_cast<float2*>(po + lr0 * HD + col) = make_float2(o[j][0], o[j][1]);
+    *reinterpret_cast<float2*>(po + lr1 * HD + col) = make_float2(o[j][2], o[j][3]);
+  }
+  if (tq == 0) {
+    *reinterpret_cast<float2*>(pml + lr0 * 2) = make_float2(m0, l0);
+    *reinterpret_cast<float2*>(pml + lr1 * 2) = make_float2(m1, l1);
   }
   cluster_sync();
   const int S = a.splits;
   const uint32_t rank = cluster_rank();
-  const int live_rows = max(0, min(kQRowsPerCta, a.rows - qt * kQRowsPerCta));
-  const int rpc = (live_rows + S - 1) / S;
-  const int row_begin = min(live_rows, int(rank) * rpc);
-  const int my_rows = max(0, min(rpc, live_rows - row_begin));
-  if (tid < my_rows) {
-    const int r = row_begin + tid;
+  const int rpc = kQRowsPerCta / S;
+  const int row_begin = int(rank) * rpc;
+  if (tid < rpc) {
+    const int row = row_begin + tid;
     float ms[8], ls[8], mmax = -INFINITY;
 #pragma unroll
     for (int sp = 0; sp < 8; ++sp) {
       ms[sp] = -INFINITY;
       ls[sp] = 0.f;
       if (sp < S) {
-        const float2 ml = ld_dsmem_f32x2(cluster_map(pml + r * 2, uint32_t(sp)));
+        const float2 ml = ld_dsmem_f32x2(cluster_map(pml + row * 2, uint32_t(sp)));
         ms[sp] = ml.x;
         ls[sp] = ml.y;
         mmax = fmaxf(mmax, ml.x);
@@ -388,46 +347,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     wts[tid * (S + 1) + S] = lsum > 0.f ? 1.f / lsum : 0.f;
   }
   __syncthreads();
-  // 16-byte remote loads of eight output elements, every rank's piece in flight before any is summed
-  constexpr int Q8 = HD / 8;
-  for (int idx = tid; idx < my_rows * Q8; idx += kAttnThreads) {
-    const int lr = idx / Q8, c8 = (idx % Q8) * 8;
-    const uint32_t off = uint32_t((row_begin + lr) * HD + c8) * 4u;
-    float4 lo[8], hi[8];
+  // 16-byte remote loads, two of the thread's row chunks x every rank in flight at a time; rows past a.rows are
+  // skipped
+  constexpr int Q4 = HD / 4;  // float4 per row
+  const int live = max(0, min(rpc, a.rows - (qt * kQRowsPerCta + row_begin)));
+  for (int idx0 = tid; idx0 < live * Q4; idx0 += 2 * kAttnThreads) {
+    float4 part[2][8];
 #pragma unroll
-    for (int sp = 0; sp < 8; ++sp) {
-      if (sp < S) {
-        const uint32_t base = cluster_map(po, uint32_t(sp)) + off;
-        lo[sp] = ld_dsmem_f32x4(base);
-        hi[sp] = ld_dsmem_f32x4(base + 16);
-      }
-    }
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int u = 0; u < 2; ++u) {
+      const int idx = idx0 + u * kAttnThreads;
+      const int lr = idx / Q4, c = (idx % Q4) * 4;
+      const uint32_t off = uint32_t((row_begin + lr) * HD + c) * 4u;
 #pragma unroll
-    for (int sp = 0; sp < 8; ++sp) {
-      if (sp < S) {
-        const float w = wts[lr * (S + 1) + sp];
-        acc[0] += w * lo[sp].x;
-        acc[1] += w * lo[sp].y;
-        acc[2] += w * lo[sp].z;
-        acc[3] += w * lo[sp].w;
-        acc[4] += w * hi[sp].x;
-        acc[5] += w * hi[sp].y;
-        acc[6] += w * hi[sp].z;
-        acc[7] += w * hi[sp].w;
-      }
+      for (int sp = 0; sp < 8; ++sp)
+        part[u][sp] = (sp < S && idx < live * Q4) ? ld_dsmem_f32x4(cluster_map(po, uint32_t(sp)) + off)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const float inv = wts[lr * (S + 1) + S];
-    *out_chunk(qt * kQRowsPerCta + row_begin + lr, head * HD + c8) =
-        make_uint4(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv),
-                   pack_bf16(acc[4] * inv, acc[5] * inv), pack_bf16(acc[6] * inv, acc[7] * inv));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int idx = idx0 + u * kAttnThreads;
+      if (idx >= live * Q4) continue;
+      const int lr = idx / Q4, c = (idx % Q4) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        if (sp < S) {
+          const float w = wts[lr * (S + 1) + sp];
+          acc.x += w * part[u][sp].x;
+          acc.y += w * part[u][sp].y;
+          acc.z += w * part[u][sp].z;
+          acc.w += w * part[u][sp].w;
+        }
+      }
+      const int grow = qt * kQRowsPerCta + row_begin + lr;
+      const float inv = wts[lr * (S + 1) + S];
+      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out_at(grow, head * HD + c));
+      dst[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+      dst[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    }
   }
   cluster_sync();
 }
 
 template <int HD>
 int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool pdl) {
-  constexpr int SMEM = AttnSmem<HD>::SMEM;
+  constexpr int SMEM = 2 * kStages * kKeysPerTile * HD * 2 + kMaxPageSlice * 4;
   auto kernel = round_attention_kernel<HD>;
   const int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(attention smem)");
   if (st != PLM_OK) return st;
@@ -439,12 +403,10 @@ int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool p
 }  // namespace
 
 int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys) {
-  // One CTA per SM (shared memory and tensor memory): double the splits while the grid still fits in one wave and
-  // every split keeps at least two tiles.
   const int ctas = num_heads * q_tiles;
   const int max_tiles = int((max_keys + kKeysPerTile - 1) / kKeysPerTile);
   int splits = 1;
-  while (splits < 8 && ctas * 2 * splits <= num_sms && 2 * splits <= max_tiles / 2) splits *= 2;
+  while (splits < 8 && ctas * splits < 2 * num_sms && 2 * splits <= max_tiles) splits *= 2;
   return splits;
 }
 

@@ -250,57 +250,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// The same for a K x N operand stored MN-major (N contiguous): 128-byte rows hold 64 consecutive N elements of one
-// k, rows of successive k 128 bytes apart, 8-row groups `k_group_bytes` apart (the SBO field), and the next 64 N
-// elements `n_chunk_bytes` further on (the LBO field); 128-byte swizzle, 1024-byte aligned groups.
-__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t n_chunk_bytes,
-                                                       uint32_t k_group_bytes) {
-  uint64_t d = 0;
-  d |= uint64_t((smem_addr >> 4) & 0x3FFF);
-  d |= uint64_t((n_chunk_bytes >> 4) & 0x3FFF) << 16;
-  d |= uint64_t((k_group_bytes >> 4) & 0x3FFF) << 32;
-  d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
-  return d;
-}
-// Instruction-descriptor bit selecting an MN-major B operand.
-constexpr uint32_t kUmmaBMajorMN = 1u << 16;
-
-// Orders this thread's generic-proxy writes to shared memory (st.shared, cp.async) before later reads of it by
-// the async proxy (tcgen05.mma operands); a CTA barrier must follow before the MMA is issued.
-__device__ __forceinline__ void fence_proxy_async_shared() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Issues a 32 lanes x 32 columns TMEM load without waiting (tmem_ld_wait completes every load issued before it).
-__device__ __forceinline__ void tmem_ld_32cols_async(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 32 lanes x 32 columns of fp32 into TMEM (the store counterpart of tmem_ld_32cols), completed before returning.
-__device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
-      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
-      "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
 // 32 lanes x 32 columns of fp32 from TMEM: thread i of the warp receives lane (lane_base + i), columns
 // col .. col+31. The warp may only address the 32-lane slice (warp_id % 4) * 32.
 __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, float (&v)[32]) {

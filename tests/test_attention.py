@@ -52,6 +52,9 @@ def _reference(q, kc, vc, table, offset, depth, own, page, heads, kv_heads):
 @pytest.mark.parametrize("kind,k,ctx_len,page,heads,kv_heads,hd,splits", [
     ("steady", 7, 1024, 16, 16, 16, 128, 0),
     ("steady", 7, 4096, 16, 16, 16, 128, 0),
+    ("steady", 7, 32768, 16, 16, 16, 128, 0),   # the longest context of the configs[4] sweep
+    ("steady", 7, 4096, 64, 16, 16, 128, 0),    # the reference's page size (bench/engine.py:4)
+    ("steady", 7, 4096, 16, 20, 20, 128, 0),    # the 3B shape's 20 heads
     ("steady", 7, 1000, 32, 16, 16, 128, 1),
     ("steady", 4, 333, 64, 8, 8, 64, 0),
     ("steady", 6, 190, 16, 8, 8, 64, 2),
