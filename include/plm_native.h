@@ -23,6 +23,9 @@
  *                   165-169; vllm/v1/attention/backends/flex_attention.py:1070-1205).
  *   plm_kv_append   reshape_and_cache_flash (flex_attention.py:1047-1068) at the slots of plm/decoder.py:347.
  *   plm_add_rmsnorm vLLM RMSNorm with residual (fused_add_rms_norm) between the Llama sublayers.
+ *   plm_commit      the KV commit of a round: the reference's implicit commit (offset += nc + 1 with the verify
+ *                   rows already in place, plm/decoder.py:351-365) made explicit as a copy of the accepted verify
+ *                   rows from round scratch into the permanent pages, the KV move of eagle3/tree.py:263-279.
  *   plm_create / plm_round / plm_round0 / plm_prefill / plm_state
  *                   RoundDecoder (plm/decoder.py:85-467): construction and state (88-146), the steady round
  *                   (312-324), round 0 (275-310), the prefill (369-403); RoundConfig.build (plm/rounds.py:71-81)
@@ -38,7 +41,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 5
+#define PLM_ABI_VERSION 6
 
 enum plm_status {
   PLM_OK = 0,
@@ -135,6 +138,10 @@ typedef struct plm_bookkeeping {
    * confirms the end-of-text id at an output position below the window, sets it (the stop test of the reference's
    * host loop, plm/decoder.py:414-439). The first-token bookkeeping clears it. */
   int64_t* stop;
+  /* Nullable commit record, int64[2], written by steady and round-0 bookkeeping: the first logical KV index and the
+   * number of round rows to commit (nc + 1; 0 when the round committed nothing because the request had stopped).
+   * plm_commit reads it. */
+  int64_t* commit;
 } plm_bookkeeping;
 
 /* One verify decode per row: Voronoi assignment of the row's logits (plm/iterate.py:322-342 through
@@ -200,6 +207,21 @@ typedef struct plm_kv_append_desc {
   const int64_t* offset;
   int32_t rows, num_kv_heads, head_dim;
 } plm_kv_append_desc;
+
+/* Copies round rows commit[0] .. commit[0] + commit[1] - 1 (logical KV indices) of every layer's K and V from the
+ * round scratch into the paged cache through the block table: row j of the scratch goes to logical index
+ * commit[0] + j. The commit record is read on the device (the verify bookkeeping writes it), so the call can follow
+ * it in the same stream or graph. Rows past commit[1] and every other slot of the cache are left as they are. */
+typedef struct plm_commit_desc {
+  int32_t dtype;
+  const void* scratch;        /* [layers][2][scratch_rows][num_kv_heads][head_dim] */
+  int32_t scratch_rows;
+  void* kv_cache;             /* [layers][2][num_pages][num_kv_heads][page_size][head_dim] */
+  int64_t plane_elems;        /* num_pages * num_kv_heads * page_size * head_dim */
+  int32_t layers, num_kv_heads, head_dim, page_size, num_pages, max_pages;
+  const int32_t* block_table; /* [max_pages] */
+  const int64_t* commit;      /* device int64[2]: first logical index, rows */
+} plm_commit_desc;
 
 /* residual <- x + residual; normed <- RMSNorm(residual_fp32) * weight (vLLM fused_add_rms_norm). */
 typedef struct plm_add_rmsnorm_desc {
@@ -289,6 +311,8 @@ typedef struct plm_state_ptrs {
   int64_t out_capacity, seq_capacity, aux_len, plane_elems;
   int32_t width, lm_tiles, row_capacity;
   int64_t* stop;         /* [4] the request stop block (plm_bookkeeping.stop) */
+  void* round_kv;        /* [layers][2][width][kv_heads][head_dim]: K and V of the last round's rows (scratch) */
+  int64_t* commit;       /* [2] the last round's commit record (plm_bookkeeping.commit) */
 } plm_state_ptrs;
 
 /* ---- context ---- */
@@ -336,6 +360,7 @@ int plm_icdf_decode(plm_ctx* ctx, const plm_icdf_desc* desc, void* stream);
 int plm_attention(plm_ctx* ctx, const plm_attention_desc* desc, void* stream);
 int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* desc, void* stream);
 int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* desc, void* stream);
+int plm_commit(plm_ctx* ctx, const plm_commit_desc* desc, void* stream);
 
 /* ---- round engine ---- */
 int plm_create(const plm_model_desc* model, const plm_weight_ptrs* weights, const plm_round_desc* round,
@@ -352,7 +377,8 @@ int plm_set_stop(plm_handle* h, int64_t max_tokens, int64_t eos_token, int64_t e
 /* Causal prefill of the loaded prompt, then the first token and the request state of round 0. */
 int plm_prefill(plm_handle* h, void* stream);
 int plm_round0(plm_handle* h, void* stream);
-/* One steady round: forward of k + k^2 rows, lm_head, verify decode, acceptance, commit. Graph-capturable. */
+/* One steady round: forward of k + k^2 rows (their K and V into the round scratch), lm_head, verify decode,
+ * acceptance, and the KV commit of the accepted verify rows into the paged cache. Graph-capturable. */
 int plm_round(plm_handle* h, void* stream);
 /* One decoder layer's o_proj, post_attention_layernorm and mlp (vLLM llama.py:198-250 LlamaDecoderLayer.forward
  * after self_attn; plm/decoder.py:336 runs it inside the model forward) as the round runs it: the layer block over

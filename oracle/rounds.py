@@ -161,3 +161,17 @@ def first_token(state: RoundState, first: int, prompt_len: int) -> None:
 def argmax_first(values: np.ndarray) -> np.ndarray:
     """Row argmax with the first index on ties (torch.argmax's documented choice)."""
     return np.argmax(values, axis=-1)
+
+
+def commit_rows(cache: np.ndarray, scratch: np.ndarray, block_table: np.ndarray, page_size: int, first: int,
+                count: int) -> None:
+    """The KV commit of a round, in place: rows 0 .. count-1 of the round's K/V (``scratch``
+    [layers][2][rows][kv_heads][head_dim]) go to logical KV indices first .. first+count-1 of the paged ``cache``
+    [layers][2][pages][kv_heads][page_size][head_dim] through the block table. This is the reference's implicit
+    commit made explicit: plm/decoder.py:351-365 advances the offset over the verify rows 0 .. nc that the forward
+    already wrote in place, and eagle3/tree.py:263-279 moves accepted rows into their final slots the same way
+    (kv[dst // BS, :, dst % BS, :] = ...)."""
+    for j in range(count):
+        logical = first + j
+        page = int(block_table[logical // page_size])
+        cache[:, :, page, :, logical % page_size, :] = scratch[:, :, j, :, :]

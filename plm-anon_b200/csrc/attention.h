@@ -27,6 +27,10 @@ struct AttnArgs {
   void* row_tiles;             // non-null: the output written as row tiles of tile_rows rows instead (common.cuh)
   int tile_rows;
   int splits;                  // KV splits = cluster size, a power of two <= 8
+  // non-null: keys at logical indices >= offset (the forward's own rows) are read from these [rows][kv_heads]
+  // [head_dim] planes (the round scratch) instead of the paged cache
+  const void* scratch_k;
+  const void* scratch_v;
   int* err;
 };
 

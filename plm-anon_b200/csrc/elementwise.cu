@@ -42,7 +42,8 @@ __device__ __forceinline__ float block_sum_rows(float v, float* red) {
 //   Rows whose id lies in [V, V + num_aux_tokens) take auxiliary_vocabulary[min(cell, A - 1)] (mask_auxiliary if
 //   the cell is the sentinel A), all others embed_tokens[clamp(id, 0, V - 1)] (plm/decoder.py:264-268, 331-349;
 //   plm/auxiliary.py:50-54). The row's rotary position is offset + rel_positions[r] and its KV slot the physical
-//   slot of logical index offset + r through the block table (plm/decoder.py:340, 347).
+//   slot of logical index offset + r through the block table (plm/decoder.py:340, 347), or for a round's rows
+//   (round_scratch) row r of the round scratch, from which the commit copies the accepted rows into the pages.
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueArgs a) {
   __shared__ float red[32];
@@ -86,7 +87,9 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
     const int64_t logical = offset + r;
     const int64_t lp = logical / a.page_size;
     const int page = (logical >= 0 && lp < a.max_pages) ? a.block_table[lp] : -1;
-    if (page < 0 || page >= a.num_pages) {
+    if (a.round_scratch) {
+      a.slots[r] = r;  // a round's rows are candidates: their K/V wait in the round scratch for the commit
+    } else if (page < 0 || page >= a.num_pages) {
       record_error(a.err, kErrBadIndex);
       a.slots[r] = -1;
     } else {

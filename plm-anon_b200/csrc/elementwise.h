@@ -33,6 +33,7 @@ struct PrologueArgs {
   void* normed;                // [rows][hidden]
   int32_t* positions;          // [rows]
   int64_t* slots;              // [rows]
+  int round_scratch;           // nonzero: row r's K/V go to row r of the round scratch (slots[r] = r), not to a page
   int* counters;               // zeroed at the start of the forward (the layer blocks' phase counters; may be null)
   int n_counters;
   int* err;

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "attention.h"
+#include "commit.h"
 #include "elementwise.h"
 #include "mlp.h"
 #include "runtime.h"
@@ -70,6 +71,10 @@ struct plm_handle {
   void* kv = nullptr;
   size_t plane_elems = 0;
   int32_t* block_table = nullptr;
+  // a round's candidate rows: K/V of all W rows of the last round0 / steady forward, [layer][K|V][W][kv_heads][hd],
+  // and the commit record [first logical index, rows] the bookkeeping leaves for the commit kernel
+  void* round_kv = nullptr;
+  int64_t* commit = nullptr;
   // loop state
   int64_t *out = nullptr, *base = nullptr, *offset = nullptr, *anchor = nullptr, *pending = nullptr,
           *round_sequence = nullptr, *sequence_step = nullptr, *aux_buf = nullptr, *prompt = nullptr,
@@ -91,6 +96,10 @@ namespace {
 
 void* kv_plane(plm_handle* h, int layer, int which) {
   return static_cast<__nv_bfloat16*>(h->kv) + (size_t(layer) * 2 + which) * h->plane_elems;
+}
+void* round_plane(plm_handle* h, int layer, int which) {
+  return static_cast<__nv_bfloat16*>(h->round_kv) +
+         (size_t(layer) * 2 + which) * size_t(h->W) * h->m.num_kv_heads * h->m.head_dim;
 }
 
 int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMap** out) {
@@ -173,8 +182,11 @@ int layer_block_launch(plm_handle* h, int l, int rows, cudaStream_t s) {
 // The Llama forward of `rows` rows whose logical KV indices start at *offset_ptr (vLLM llama.py:253-314):
 // prologue (+ layer-0 input norm), then per layer qkv(+RoPE, KV scatter) -> attention -> o -> add+norm ->
 // gate_up(+SiLU) -> down -> add+norm (the next layer's input norm, or the final norm).
+// A round's forward (round0 or steady mode) writes its rows' K/V into the round scratch, and attention reads the
+// forward's own keys from there; a prefill writes straight into the pages (every prompt row is committed).
 int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const int64_t* relpos, const int64_t* relaux,
             const int32_t* depth, const int32_t* own, int attn_splits, int gather_row, cudaStream_t s) {
+  const bool round_rows = mode != kProloguePrefill;
   const plm_model_desc& m = h->m;
   const int hidden = m.hidden, hd = m.head_dim;
   const int q_size = m.num_heads * hd, kv_size = m.num_kv_heads * hd;
@@ -209,6 +221,7 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
   p.normed = h->x_norm;
   p.positions = h->positions;
   p.slots = h->slots;
+  p.round_scratch = round_rows ? 1 : 0;
   const bool layer_block = h->mlp.sched != nullptr && rows <= kMlpMaxRows;
   p.counters = h->block_ctr;
   p.n_counters = h->block_ctr != nullptr ? 4 * m.num_layers : 0;
@@ -220,16 +233,23 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     plm_gemm_epilogue e = {};
     e.kind = PLM_EPI_QKV_ROPE;
     e.q_out = h->q;
-    e.k_cache = kv_plane(h, l, 0);
-    e.v_cache = kv_plane(h, l, 1);
     e.positions = h->positions;
     e.slots = h->slots;
     e.cos_sin = h->cos_sin;
     e.num_heads = m.num_heads;
     e.num_kv_heads = m.num_kv_heads;
     e.head_dim = hd;
-    e.page_size = h->rd.page_size;
-    e.num_slots = int64_t(h->rd.num_pages) * h->rd.page_size;
+    if (round_rows) {  // the round scratch as a cache of one-row pages: slot r is row r
+      e.k_cache = round_plane(h, l, 0);
+      e.v_cache = round_plane(h, l, 1);
+      e.page_size = 1;
+      e.num_slots = h->W;
+    } else {
+      e.k_cache = kv_plane(h, l, 0);
+      e.v_cache = kv_plane(h, l, 1);
+      e.page_size = h->rd.page_size;
+      e.num_slots = int64_t(h->rd.num_pages) * h->rd.page_size;
+    }
     e.max_pos = m.max_pos;
     st = gemm(h, h->qkv[l], &h->map_qkv[l], q_size + 2 * kv_size, hidden, h->x_norm, rows, e, nullptr, 0, s);
     if (st != PLM_OK) return st;
@@ -257,6 +277,10 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
       a.out = h->attn;
     }
     a.splits = attn_splits;
+    if (round_rows) {
+      a.scratch_k = round_plane(h, l, 0);
+      a.scratch_v = round_plane(h, l, 1);
+    }
     st = attention_launch(h->ctx, a, s, true);
     if (st != PLM_OK) return st;
 
@@ -352,11 +376,31 @@ int verify(plm_handle* h, int n_rows, int mode, const int64_t* aux_base, cudaStr
   a.book.sequence_step = h->sequence_step;
   a.book.prompt_len = h->prompt_len;
   a.book.stop = h->stop;
+  a.book.commit = h->commit;
   a.counter = h->ctx->counters + (h->ctx->n_counters - 1);
   a.err = h->ctx->err;
   int st = verify_validate(a, n_rows);
   if (st != PLM_OK) return st;
   return verify_launch(a, h->m.dtype, n_rows, s, true);
+}
+
+// The accepted verify rows of the round just decided, from the round scratch into the pages (commit.cu).
+int commit_rows(plm_handle* h, cudaStream_t s) {
+  CommitArgs c = {};
+  c.scratch = h->round_kv;
+  c.scratch_rows = h->W;
+  c.kv_cache = h->kv;
+  c.plane_elems = int64_t(h->plane_elems);
+  c.layers = h->m.num_layers;
+  c.num_kv_heads = h->m.num_kv_heads;
+  c.head_dim = h->m.head_dim;
+  c.page_size = h->rd.page_size;
+  c.num_pages = h->rd.num_pages;
+  c.max_pages = h->rd.max_pages;
+  c.block_table = h->block_table;
+  c.commit = h->commit;
+  c.err = h->ctx->err;
+  return commit_launch(c, s, true);
 }
 
 int upload_layout(const std::vector<int64_t>& v, int64_t* dst) {
@@ -425,7 +469,8 @@ int plm_destroy(plm_handle* h) {
                   h->verify_logits, h->best_val, h->best_idx, h->verify, h->flags, h->st_relpos, h->st_relaux,
                   h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
-                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->stop, h->block_ctr,
+                  h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->stop, h->round_kv,
+                  h->commit, h->block_ctr,
                   h->block_tiles, h->attn_tiles, h->x_tiles, h->act_tiles};
   for (void* b : bufs) cudaFree(b);
   mlp_schedule_destroy(&h->mlp);
@@ -586,6 +631,11 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   h->plane_elems = size_t(rd->num_pages) * m->num_kv_heads * rd->page_size * hd;
   st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->kv), size_t(L) * 2 * h->plane_elems, "KV pool");
   if (st == PLM_OK) st = check_cuda(cudaMemset(h->kv, 0, size_t(L) * 2 * h->plane_elems * 2), "KV pool zero");
+  const size_t round_elems = size_t(L) * 2 * h->W * m->num_kv_heads * hd;
+  if (st == PLM_OK) st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->round_kv), round_elems, "round scratch");
+  if (st == PLM_OK) st = check_cuda(cudaMemset(h->round_kv, 0, round_elems * 2), "round scratch zero");
+  if (st == PLM_OK) st = dev_alloc(&h->commit, 2, "commit record");
+  if (st == PLM_OK) st = check_cuda(cudaMemset(h->commit, 0, 2 * sizeof(int64_t)), "commit record zero");
   if (st == PLM_OK) st = dev_alloc(&h->block_table, rd->max_pages, "block table");
   if (st == PLM_OK) {
     std::vector<int32_t> ident(rd->max_pages);
@@ -734,6 +784,7 @@ int plm_round0(plm_handle* h, void* stream) {
                    h->attn_splits_round, -1, s);
   if (st == PLM_OK) st = lm_head(h, h->x_norm, h->W, 1, s);
   if (st == PLM_OK) st = verify(h, 1, kBookRound0, h->base, s);
+  if (st == PLM_OK) st = commit_rows(h, s);
   return st;
 }
 
@@ -756,6 +807,7 @@ int plm_round(plm_handle* h, void* stream) {
                    h->attn_splits_round, -1, s);
   if (st == PLM_OK) st = lm_head(h, h->x_norm, h->W, h->rd.k, s);
   if (st == PLM_OK) st = verify(h, h->rd.k, kBookSteady, h->base, s);
+  if (st == PLM_OK) st = commit_rows(h, s);
   return st;
 }
 
@@ -786,6 +838,8 @@ int plm_state(plm_handle* h, plm_state_ptrs* p) {
   p->lm_tiles = h->lm_tiles;
   p->row_capacity = h->R;
   p->stop = h->stop;
+  p->round_kv = h->round_kv;
+  p->commit = h->commit;
   return PLM_OK;
 }
 

@@ -37,6 +37,7 @@ struct Bookkeeping {
   int64_t* sequence_step;
   int64_t prompt_len;        // first-token mode: the offset round 0 starts at
   int64_t* stop;             // nullable [kStopWords]: budget, end-of-text id, end-of-text window, done flag
+  int64_t* commit;           // nullable [2]: first logical KV index and count of the round rows to commit
 };
 
 struct VerifyArgs {

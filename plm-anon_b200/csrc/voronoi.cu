@@ -948,7 +948,10 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
   if (tid == 0) *a.counter = 0;
   const int K = b.k;
   // A request that has already stopped: the round was queued behind the one that ended it and commits nothing.
-  if (b.mode == kBookSteady && b.stop != nullptr && __ldcg(b.stop + kStopDone) != 0) return;
+  if (b.mode == kBookSteady && b.stop != nullptr && __ldcg(b.stop + kStopDone) != 0) {
+    if (tid == 0 && b.commit != nullptr) b.commit[1] = 0;
+    return;
+  }
 
   if (b.mode == kBookFirstToken) {
     for (int64_t i = tid; i < b.out_cap; i += kThreads) b.out[i] = -1;
@@ -1028,7 +1031,12 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
     for (int i = 0; i < K - 1; ++i) b.pending[i] = s->new_pending[i];
     *b.anchor = picked;
     *b.base = base + nc + 1;
-    *b.offset = *b.offset + nc + 1;
+    const int64_t committed = *b.offset;
+    if (b.commit != nullptr) {  // verify rows 0 .. nc go to logical indices offset .. offset + nc
+      b.commit[0] = committed;
+      b.commit[1] = nc + 1;
+    }
+    *b.offset = committed + nc + 1;
     if (b.mode == kBookSteady && b.stop != nullptr) {
       // The stop test of the reference's host loop (plm/decoder.py:414-439) on the tokens this round confirmed.
       const int64_t next = base + nc + 1;
@@ -1140,7 +1148,7 @@ extern "C" int plm_verify_decode(plm_ctx* ctx, const plm_verify_desc* d, void* s
   const plm_bookkeeping& b = d->book;
   a.book = Bookkeeping{b.mode,       b.k,     b.best_val, b.best_idx,       b.n_tiles, b.rows,
                        b.out,        b.out_cap, b.base,   b.offset,         b.anchor,  b.pending,
-                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len, b.stop};
+                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len, b.stop, b.commit};
   a.counter = ctx->counters + (ctx->n_counters - 1);
   a.err = ctx->err;
   int st = verify_validate(a, d->n_rows);
@@ -1266,7 +1274,7 @@ extern "C" int plm_verify_decode_static(const plm_verify_desc* d, int32_t* devic
   const plm_bookkeeping& b = d->book;
   a.book = Bookkeeping{b.mode,       b.k,     b.best_val, b.best_idx,       b.n_tiles, b.rows,
                        b.out,        b.out_cap, b.base,   b.offset,         b.anchor,  b.pending,
-                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len, b.stop};
+                       b.round_sequence, b.seq_cap, b.sequence_step, b.prompt_len, b.stop, b.commit};
   a.counter = reinterpret_cast<int*>(scratch);
   a.err = device_error != nullptr ? device_error : reinterpret_cast<int*>(scratch) + 1;
   st = verify_validate(a, d->n_rows);

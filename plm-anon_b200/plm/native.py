@@ -54,7 +54,7 @@ class Bookkeeping(ctypes.Structure):
                 ("n_tiles", c_int32), ("rows", c_int32), ("out", c_void_p), ("out_cap", c_int64),
                 ("base", c_void_p), ("offset", c_void_p), ("anchor", c_void_p), ("pending", c_void_p),
                 ("round_sequence", c_void_p), ("seq_cap", c_int64), ("sequence_step", c_void_p),
-                ("prompt_len", c_int64), ("stop", c_void_p)]
+                ("prompt_len", c_int64), ("stop", c_void_p), ("commit", c_void_p)]
 
 
 class VerifyDesc(ctypes.Structure):
@@ -88,6 +88,13 @@ class AddRmsNormDesc(ctypes.Structure):
                 ("weight", c_void_p), ("rows", c_int32), ("hidden", c_int32), ("eps", ctypes.c_float),
                 ("gather_row", c_int32), ("gathered", c_void_p), ("partials", c_void_p), ("n_partials", c_int32),
                 ("partial_stride", ctypes.c_int64)]
+
+
+class CommitDesc(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("scratch", c_void_p), ("scratch_rows", c_int32), ("kv_cache", c_void_p),
+                ("plane_elems", c_int64), ("layers", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32),
+                ("page_size", c_int32), ("num_pages", c_int32), ("max_pages", c_int32), ("block_table", c_void_p),
+                ("commit", c_void_p)]
 
 
 class ModelDesc(ctypes.Structure):
@@ -125,7 +132,8 @@ class StatePtrs(ctypes.Structure):
                 ("best_val", c_void_p), ("best_idx", c_void_p), ("verify", c_void_p), ("flags", c_void_p),
                 ("hidden_normed", c_void_p), ("kv_cache", c_void_p), ("table", c_void_p),
                 ("out_capacity", c_int64), ("seq_capacity", c_int64), ("aux_len", c_int64), ("plane_elems", c_int64),
-                ("width", c_int32), ("lm_tiles", c_int32), ("row_capacity", c_int32), ("stop", c_void_p)]
+                ("width", c_int32), ("lm_tiles", c_int32), ("row_capacity", c_int32), ("stop", c_void_p),
+                ("round_kv", c_void_p), ("commit", c_void_p)]
 
 
 _lib: ctypes.CDLL | None = None
@@ -144,6 +152,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_attention": [c_void_p, POINTER(AttentionDesc), c_void_p],
     "plm_kv_append": [c_void_p, POINTER(KvAppendDesc), c_void_p],
     "plm_add_rmsnorm": [c_void_p, POINTER(AddRmsNormDesc), c_void_p],
+    "plm_commit": [c_void_p, POINTER(CommitDesc), c_void_p],
     "plm_icdf_decode": [c_void_p, POINTER(IcdfDesc), c_void_p],
     "plm_block_schedule": [c_int32, c_int32, c_int32, c_int32, POINTER(c_int32), c_int32, POINTER(c_int32),
                            POINTER(c_int32)],
@@ -265,6 +274,11 @@ def kv_append(ctx: Context, desc: KvAppendDesc, stream=None) -> None:
 
 def add_rmsnorm(ctx: Context, desc: AddRmsNormDesc, stream=None) -> None:
     check(library().plm_add_rmsnorm(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_add_rmsnorm")
+
+
+def commit(ctx: Context, desc: CommitDesc, stream=None) -> None:
+    """Enqueue plm_commit: the rows the device commit record names, from round scratch into the paged cache."""
+    check(library().plm_commit(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_commit")
 
 
 def block_schedule(num_sms: int, hidden: int, intermediate: int, q_size: int) -> list[list[int]]:

@@ -16,6 +16,10 @@ running its own functions on the CPU:
                     meta GROUP=8, BLOCK=32; the compiled argmin replaced by its eager implementation);
   llama.npz         the Llama forward of Hugging Face transformers (LlamaForCausalLM, eager attention, fp32) over a
                     prompt plus one round under the round mask, pinning the oracle's paged forward;
+  drift.json        how far a bf16 run of Hugging Face's LlamaForCausalLM (the reference's model family, in bf16
+                    weights and bf16 arithmetic) lands from the oracle's forward (bf16 storage, fp32 sums) at the
+                    PLM-1.3B shape on seeded random weights: the spread between two correct bf16 implementations of
+                    the same model, which bounds the logit tolerance the GPU forward is held to;
   ptp.npz           the PTP scheme of the gated-LoRA model: LinearInterpolationAuxiliary.embed / decode_unmasked
                     (plm/auxiliary.py) and GatedLoraMethod.apply under gated_lora.rows_from (plm/gated_lora.py; its
                     GEMMs are vLLM's default unquantized GEMM, torch.nn.functional.linear, on the CPU).
@@ -79,6 +83,8 @@ def llama_weights(seed: int, layers: int, hidden: int, heads: int, kv_heads: int
 
 
 LLAMA = dict(seed=11, layers=2, hidden=256, heads=2, kv_heads=1, head_dim=128, inter=512, vocab=512)
+DRIFT = dict(seed=13, layers=24, hidden=2048, heads=16, kv_heads=16, head_dim=128, inter=8192, vocab=50257,
+             prompt=64)
 VORONOI_CASES = [  # seed, rows, vocab, aux, kind
     (100, 2, 50257, 1024, "fp32"), (101, 2, 50257, 1024, "bf16"), (102, 3, 3000, 256, "fp32"),
     (103, 2, 8000, 512, "bf16"),
@@ -380,6 +386,75 @@ def gen_llama(ref, out: Path):
                         prompt_len=prompt_len, **{f"cfg_{key}": value for key, value in c.items()})
 
 
+def _hf_llama(c: dict, w: dict, dtype: torch.dtype):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["inter"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["heads"], num_key_value_heads=c["kv_heads"],
+                      head_dim=c["head_dim"], rms_norm_eps=1e-5, max_position_embeddings=4096,
+                      tie_word_embeddings=False, attention_bias=False, mlp_bias=False)
+    cfg._attn_implementation = "eager"
+    model = LlamaForCausalLM(cfg).eval()
+    q_size, kv_size = c["heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+    with torch.no_grad():
+        model.model.embed_tokens.weight.copy_(w["embed"][: c["vocab"]])
+        model.lm_head.weight.copy_(w["lm_head"])
+        model.model.norm.weight.copy_(w["final_norm"])
+        for i, layer in enumerate(model.model.layers):
+            q, k, v = w["qkv"][i].split([q_size, kv_size, kv_size])
+            layer.self_attn.q_proj.weight.copy_(q)
+            layer.self_attn.k_proj.weight.copy_(k)
+            layer.self_attn.v_proj.weight.copy_(v)
+            layer.self_attn.o_proj.weight.copy_(w["o"][i])
+            gate, up = w["gate_up"][i].split([c["inter"], c["inter"]])
+            layer.mlp.gate_proj.weight.copy_(gate)
+            layer.mlp.up_proj.weight.copy_(up)
+            layer.mlp.down_proj.weight.copy_(w["down"][i])
+            layer.input_layernorm.weight.copy_(w["input_norm"][i])
+            layer.post_attention_layernorm.weight.copy_(w["post_norm"][i])
+    return model.to(dtype)
+
+
+def gen_drift(ref, out: Path):
+    """The bf16 drift of the reference's model family at the PLM-1.3B shape: HF LlamaForCausalLM with bf16 weights
+    run (a) in bf16 and (b) in fp32, against the oracle's forward of the same weights (bf16 storage, fp32 sums) and
+    the oracle with float64 sums, over a causal prompt. Stores the max abs differences of the final-norm logits."""
+    sys.path.insert(0, str(HERE.parent.parent))
+    from oracle import model as omodel
+    from oracle import rounds as orounds
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    c = DRIFT
+    w = llama_weights(c["seed"], c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                      c["vocab"])
+    w = {key: ([t.bfloat16().float() for t in v] if isinstance(v, list) else v.bfloat16().float())
+         for key, v in w.items()}
+    ids = torch.randint(0, c["vocab"], (c["prompt"],), generator=torch.Generator().manual_seed(c["seed"] + 1))
+    positions = torch.arange(c["prompt"])[None]
+    logits = {}
+    for name, dtype in (("hf_bf16", torch.bfloat16), ("hf_fp32", torch.float32)):
+        model = _hf_llama(c, w, dtype)
+        with torch.no_grad():
+            logits[name] = model(input_ids=ids[None], position_ids=positions).logits[0].float()
+        del model
+    shape = omodel.ModelShape(c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                              c["vocab"], 64, 1, 1e-5, 10000.0, 4096)
+    pages = -(-c["prompt"] // 16)
+    for name, acc in (("oracle", "float32"), ("oracle_f64", "float64")):
+        om = omodel.OracleModel(shape, w, "bfloat16", 16, pages, np.arange(pages), accumulate=acc)
+        _, _, depth, own = orounds.chunk_layout(c["prompt"])
+        embeds = om.embed_rows(ids.numpy(), np.full(c["prompt"], 64))
+        hidden = om.forward(embeds, np.arange(c["prompt"]), 0, depth, own)
+        logits[name] = om.logits(hidden)
+        del om
+    diff = lambda a, b: float((logits[a] - logits[b]).abs().max())  # noqa: E731
+    res = {"config": c, "logit_abs_max": float(logits["hf_fp32"].abs().max()),
+           "hf_bf16_vs_hf_fp32": diff("hf_bf16", "hf_fp32"), "hf_bf16_vs_oracle": diff("hf_bf16", "oracle"),
+           "hf_fp32_vs_oracle": diff("hf_fp32", "oracle"), "oracle_vs_oracle_f64": diff("oracle", "oracle_f64"),
+           "note": "max abs difference of the logits over all prompt rows; weights N(0, 0.02) rounded to bf16"}
+    (out / "drift.json").write_text(json.dumps(res, indent=1) + "\n")
+
+
 def gen_ptp(ref, out: Path):
     from plm import gated_lora
     from plm.auxiliary import LinearInterpolationAuxiliary
@@ -427,7 +502,7 @@ def main() -> None:
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     gens = {"layout": gen_layout, "quota": gen_quota, "accept": gen_accept, "epilogue": gen_epilogue,
-            "voronoi": gen_voronoi, "llama": gen_llama, "ptp": gen_ptp, "round0": gen_round0}
+            "voronoi": gen_voronoi, "llama": gen_llama, "ptp": gen_ptp, "round0": gen_round0, "drift": gen_drift}
     for name, fn in gens.items():
         if args.only is None or name in args.only:
             fn(args.reference, out)

@@ -235,3 +235,17 @@ def test_round0_matches_reference(case):
     assert state.base == int(d["base"]) and state.offset == int(d["offset"])
     assert state.anchor == int(d["anchor"][0])
     np.testing.assert_array_equal(state.pending, d["pending"])
+
+
+def test_bf16_drift_fixture_is_consistent():
+    """tests/golden/drift.json: the reference family's bf16 forward at the 1.3B shape drifts from the oracle by more
+    than 2e-2 and by a similar amount from its own fp32 forward, so the GPU's logit bound at that shape is the
+    reference's own spread, not a number this build chose."""
+    import json
+    from pathlib import Path
+
+    d = json.loads((Path(__file__).resolve().parent / "golden" / "drift.json").read_text())
+    assert d["config"]["layers"] == 24 and d["config"]["hidden"] == 2048 and d["config"]["vocab"] == 50257
+    assert d["hf_bf16_vs_oracle"] > 2e-2 and d["hf_bf16_vs_hf_fp32"] > 2e-2
+    assert 0.5 < d["hf_bf16_vs_oracle"] / d["hf_bf16_vs_hf_fp32"] < 2.0
+    assert d["oracle_vs_oracle_f64"] < d["hf_bf16_vs_oracle"]

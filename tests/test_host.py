@@ -168,3 +168,19 @@ def test_float16_export_keeps_its_dtype(tmp_path):
     assert RoundConfig(model=str(export)).dtype == "float16"
     assert RoundConfig(model=str(export), dtype="bfloat16").dtype == "bfloat16"
     assert RoundConfig(model="synthetic:plm-tiny").dtype == "bfloat16"
+
+
+def test_oracle_commit_moves_rows_through_the_block_table():
+    """oracle.rounds.commit_rows on a hand-checked case: rows go to logical first .. first + count - 1, each to
+    its page through the block table, in both planes of every layer, and nothing else changes."""
+    import numpy as np
+
+    from oracle import rounds as orounds
+
+    cache = np.zeros((2, 2, 3, 1, 4, 2), dtype=np.int16)  # layers, K|V, pages, kv heads, page size 4, head dim
+    scratch = np.arange(2 * 2 * 5 * 1 * 2, dtype=np.int16).reshape(2, 2, 5, 1, 2) + 1
+    orounds.commit_rows(cache, scratch, np.array([2, 0, 1]), 4, 3, 3)
+    np.testing.assert_array_equal(cache[:, :, 2, :, 3, :], scratch[:, :, 0])  # logical 3 -> page 2, slot 3
+    np.testing.assert_array_equal(cache[:, :, 0, :, 0, :], scratch[:, :, 1])  # logical 4 -> page 0, slot 0
+    np.testing.assert_array_equal(cache[:, :, 0, :, 1, :], scratch[:, :, 2])  # logical 5 -> page 0, slot 1
+    assert np.count_nonzero(cache) == np.count_nonzero(scratch[:, :, :3])

@@ -4,9 +4,12 @@ Teacher-forced parity, stage by stage (prefill, round 0, steady rounds): both si
 state, and the GPU's verify decode, acceptance and bookkeeping must equal the oracle's run on the GPU's own fp32
 logits, bit for bit (output tokens, base, offset, anchor, pending, accepted-count record).
 
-Logits must agree within bf16 tolerance: max abs error <= max(2e-2, 2 s), where s is the model's own sensitivity to
-rounding — the oracle's max abs change when it accumulates in float64 instead of float32, measured on the prefill
-(a 2-layer model has s < 1e-2; a random 24-layer bf16 stack amplifies any rounding-order difference to s ~ 0.13).
+Logits must agree within bf16 tolerance: max abs error <= 2e-2 (the north star's bound) for the small shapes. At the
+PLM-1.3B shape the bound is the reference family's own bf16 drift, pinned by tests/golden/drift.json: Hugging Face's
+LlamaForCausalLM run in bf16 on random 1.3B-shaped weights lands 0.20 from the oracle (0.18 from its own fp32 run),
+because a random 24-layer bf16 stack amplifies any rounding-order difference; the GPU forward, another bf16
+implementation, is held to no more than that. The model's own sensitivity s (the oracle's max abs change when it
+accumulates in float64) is reported beside it.
 The final-norm hidden rows use max(2e-2 + 2^-6 |ref|, 2.5 s_hidden): their elements reach |x| >= 4, where one bf16
 ulp is 0.031, and a bf16 rounding that flips in one layer (the GPU forms its fp32 sums in other orders than the
 oracle: k-split partials, the layer block's unsplit gate_up) reaches the hidden rows through every later layer. The
@@ -18,6 +21,7 @@ from __future__ import annotations
 
 import json
 import os
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -31,6 +35,8 @@ pytestmark = pytest.mark.gpu
 
 TOL = 2e-2
 HREL = 2.0 ** -6
+# The bf16 drift of the reference's model family at the PLM-1.3B shape (tests/golden/make_golden.py gen_drift).
+DRIFT = json.loads((Path(__file__).resolve().parent / "golden" / "drift.json").read_text())
 
 
 def _argmax_partials(decoder, rows: int) -> np.ndarray:
@@ -121,7 +127,9 @@ def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides)
     sens_l = float(np.abs(logits_s - logits_o).max())
     sens_h = float((hidden_s - hidden_o).abs().max())
     report["sensitivity logits"], report["sensitivity hidden"] = [sens_l], [sens_h]
-    fl, fh = 2 * sens_l, 2.5 * sens_h
+    pinned = shape == "plm-1.3b" and cfg.num_layers == DRIFT["config"]["layers"]
+    fl = DRIFT["hf_bf16_vs_oracle"] if pinned else 0.0  # logits: 2e-2, or the pinned drift at the 1.3B shape
+    fh = 2.5 * sens_h
     gpu_logits = decoder.verify_logits[0].cpu().numpy()
     _close("prefill logits", gpu_logits, logits_o[0], report, floor=fl)
     _close("prefill hidden", decoder.hidden_normed[P - 1].float().cpu().numpy(), hidden_o[0].numpy(), report, HREL, fh)
