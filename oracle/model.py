@@ -61,14 +61,18 @@ class OracleModel:
 
     def __init__(self, shape: ModelShape, weights: dict, dtype: str, page_size: int, num_pages: int,
                  block_table: np.ndarray, cos_sin: torch.Tensor | None = None, accumulate: str = "float32",
-                 ptp: "optp.PTPScheme | None" = None, adapters: "list[dict] | None" = None):
+                 ptp: "optp.PTPScheme | None" = None, adapters: "list[dict] | None" = None,
+                 device: str | torch.device = "cpu"):
         """``accumulate="float64"`` runs every matmul and attention product in double precision (then rounds to
         float32): the same model with another summation order, to measure how far rounding alone moves the output.
         ``ptp``: the linear-interpolation scheme replaces the logit-Voronoi auxiliary inputs; ``adapters``: per layer,
-        projection name ("qkv", "o", "gate_up", "down") -> ``optp.Adapter``, applied on the gated rows."""
+        projection name ("qkv", "o", "gate_up", "down") -> ``optp.Adapter``, applied on the gated rows. ``device``:
+        where the torch arithmetic runs (the CPU by default; a checker on a GPU box may put it on a GPU, with TF32
+        off, to follow long free-running decodes)."""
         self.s, self.dtype, self.tdtype = shape, dtype, TORCH_DTYPES[dtype]
         self.acc = torch.float64 if accumulate == "float64" else torch.float32
-        f = lambda t: t.detach().to("cpu", torch.float32)  # noqa: E731
+        self.device = torch.device(device)
+        f = lambda t: t.detach().to(self.device, torch.float32)  # noqa: E731
         self.embed = f(weights["embed"])
         self.lm_head = f(weights["lm_head"])[: shape.vocab]
         self.final_norm = f(weights["final_norm"])
@@ -81,7 +85,8 @@ class OracleModel:
         self.cos_sin = f(cos_sin)
         self.page_size, self.num_pages = page_size, num_pages
         self.block_table = np.asarray(block_table, dtype=np.int64)
-        self.kv = torch.zeros(shape.num_layers, 2, num_pages, shape.num_kv_heads, page_size, shape.head_dim)
+        self.kv = torch.zeros(shape.num_layers, 2, num_pages, shape.num_kv_heads, page_size, shape.head_dim,
+                              device=self.device)
         self.ptp = ptp
         self.adapters = adapters if adapters is not None else [{} for _ in range(shape.num_layers)]
 
@@ -108,13 +113,13 @@ class OracleModel:
         """plm/decoder.py:264-268 with LogitVoronoiAuxiliary.embed (plm/auxiliary.py:50-54), or with the PTP
         scheme's blend cast to the model dtype."""
         V, A = self.s.vocab, self.s.aux_vocab
-        ids = torch.as_tensor(ids, dtype=torch.int64)
+        ids = torch.as_tensor(ids, dtype=torch.int64, device=self.device)
         aux_mask = (ids >= V) & (ids < V + self.s.num_aux_tokens)
         token = self.embed[ids.masked_fill(aux_mask, 0).clamp(0, V - 1)]
         if self.ptp is not None:
             blend = optp.linear_interpolation_embed(np.asarray(aux_values, dtype=np.float32), self.ptp.embedding)
-            return torch.where(aux_mask[:, None], self._r(torch.from_numpy(blend)), token)
-        values = torch.as_tensor(aux_values, dtype=torch.int64)
+            return torch.where(aux_mask[:, None], self._r(torch.from_numpy(blend).to(self.device)), token)
+        values = torch.as_tensor(aux_values, dtype=torch.int64, device=self.device)
         vectors = self.aux_vocab[values.clamp(max=A - 1).clamp(min=0)]
         vectors = torch.where((values == A)[:, None], self.mask_aux[None, :], vectors)
         return torch.where(aux_mask[:, None], vectors, token)
@@ -133,13 +138,15 @@ class OracleModel:
         rows, hd = embeds.shape[0], s.head_dim
         half = hd // 2
         q_size, kv_size = s.num_heads * hd, s.num_kv_heads * hd
-        pos = torch.as_tensor(positions, dtype=torch.int64)
+        dev = self.device
+        pos = torch.as_tensor(positions, dtype=torch.int64, device=dev)
         cos, sin = self.cos_sin[pos, :half][:, None, :], self.cos_sin[pos, half:][:, None, :]
         n_keys = offset + rows
-        mask = torch.as_tensor(orounds.visible(np.asarray(depth), np.asarray(own_start), offset, n_keys))
+        mask = torch.as_tensor(orounds.visible(np.asarray(depth), np.asarray(own_start), offset, n_keys), device=dev)
         logical = np.arange(n_keys, dtype=np.int64)
-        key_pages, key_slots = (torch.as_tensor(a) for a in self.slots(logical))
-        row_pages, row_slots = (torch.as_tensor(a) for a in self.slots(offset + np.arange(rows, dtype=np.int64)))
+        key_pages, key_slots = (torch.as_tensor(a, device=dev) for a in self.slots(logical))
+        row_pages, row_slots = (torch.as_tensor(a, device=dev)
+                                for a in self.slots(offset + np.arange(rows, dtype=np.int64)))
         group = s.num_heads // s.num_kv_heads
 
         residual = embeds.clone()
@@ -222,21 +229,21 @@ class RoundOracle:
             embeds = self.model.embed_rows(prompt[start:start + rows], np.full(rows, sentinel))
             hidden = self.model.forward(embeds, start + np.arange(rows), start, depth, own)
         last = hidden[n - 1 - start: n - start]
-        return last, self.model.logits(last).numpy()
+        return last, self.model.logits(last).cpu().numpy()
 
     def round0_forward(self):
         st, layout = self.state, self.r0
         ids, values, positions, _ = orounds.round0_prologue(st, layout, self.model.s.vocab, self.sentinel, self.aux)
         hidden = self.model.forward(self.model.embed_rows(ids, values), positions, st.offset, layout[2], layout[3],
                                     gated_from=1)
-        return hidden, self.model.logits(hidden).numpy()
+        return hidden, self.model.logits(hidden).cpu().numpy()
 
     def round_forward(self):
         st, layout = self.state, self.steady
         ids, values, positions, _ = orounds.prologue(st, layout, self.model.s.vocab, self.sentinel, self.aux)
         hidden = self.model.forward(self.model.embed_rows(ids, values), positions, st.offset, layout[2], layout[3],
                                     gated_from=self.k)
-        return hidden, self.model.logits(hidden).numpy()
+        return hidden, self.model.logits(hidden).cpu().numpy()
 
     # ---- commits (acceptance / bookkeeping on given logits) ----
     def commit_first(self, logits_row: np.ndarray, prompt_len: int) -> int:
@@ -250,16 +257,23 @@ class RoundOracle:
         orounds.round0_epilogue(self.state, verify0, proposal_argmax)
         return verify0
 
-    def commit_round(self, verify_logits: np.ndarray, proposal_argmax: np.ndarray) -> int:
-        """``verify_logits``: the k verify rows; ``proposal_argmax``: argmax of the k^2 proposal rows."""
+    def commit_round(self, verify_logits: np.ndarray, proposal_argmax: np.ndarray, lazy: bool = False) -> int:
+        """``verify_logits``: the k verify rows; ``proposal_argmax``: argmax of the k^2 proposal rows. ``lazy``
+        decodes the verify rows in order only up to the first one that rejects its proposal: the rows after it
+        never reach the output or the state (plm/decoder.py:351-365 reads verify[nc] and the proposals before
+        it), so the round's result is the same and the decode costs nc + 1 rows instead of k."""
         st, k = self.state, self.k
-        verify = np.asarray([self.decode(verify_logits[d], self.aux[st.base + d]) for d in range(k)], dtype=np.int64)
+        verify = np.full(k, -1, dtype=np.int64)
         rule = np.zeros(k, dtype=bool)
-        for d in range(k - 1):
-            if self.rule == "floor":
-                rule[d] = ov.floor_accepts(verify_logits[d], int(st.pending[d]), self.threshold)
-            else:
-                rule[d] = ov.nucleus_accepts(verify_logits[d], int(st.pending[d]), self.threshold)
+        for d in range(k):
+            verify[d] = self.decode(verify_logits[d], self.aux[st.base + d])
+            if d < k - 1:
+                if self.rule == "floor":
+                    rule[d] = ov.floor_accepts(verify_logits[d], int(st.pending[d]), self.threshold)
+                else:
+                    rule[d] = ov.nucleus_accepts(verify_logits[d], int(st.pending[d]), self.threshold)
+                if lazy and not (verify[d] == st.pending[d] or rule[d]):
+                    break
         return orounds.epilogue(st, verify, rule, proposal_argmax)
 
     # ---- whole steps on the oracle's own logits ----
@@ -273,7 +287,7 @@ class RoundOracle:
         self.last_hidden, self.last_logits = hidden, logits
         self.commit_round0(logits[:1], orounds.argmax_first(logits[1:]))
 
-    def round(self) -> int:
+    def round(self, lazy: bool = False) -> int:
         hidden, logits = self.round_forward()
         self.last_hidden, self.last_logits = hidden, logits
-        return self.commit_round(logits[: self.k], orounds.argmax_first(logits[self.k:]))
+        return self.commit_round(logits[: self.k], orounds.argmax_first(logits[self.k:]), lazy=lazy)

@@ -102,6 +102,7 @@ def _close(name, gpu, ref, report, rel=0.0, floor=0.0):
     ("plm-tiny", 4, 16, "nucleus", 0.94, {"num_kv_heads": 1, "head_dim": 128, "aux_vocab": 512}),
     ("plm-80m", 6, 16, "nucleus", None, {"num_layers": 2}),
     ("plm-1.3b", 7, 16, "nucleus", None, {}),
+    ("plm-3b", 7, 16, "nucleus", 0.94, {"num_layers": 2}),  # the 3B width, relaxed posttrain
     ("plm-tiny", 1, 16, "nucleus", None, {}),  # k = 1: the AR-Voronoi comparator (plm/voronoi_ar.py)
     ("plm-80m", 7, 16, "nucleus", None, {"num_layers": 2, "separate_mlp": True}),  # gate_up and down as two launches
     # a 200-row prefill runs the separate launches (wider than the layer block's 128 rows), then the rounds run the
