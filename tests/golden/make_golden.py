@@ -83,8 +83,12 @@ def llama_weights(seed: int, layers: int, hidden: int, heads: int, kv_heads: int
 
 
 LLAMA = dict(seed=11, layers=2, hidden=256, heads=2, kv_heads=1, head_dim=128, inter=512, vocab=512)
-DRIFT = dict(seed=13, layers=24, hidden=2048, heads=16, kv_heads=16, head_dim=128, inter=8192, vocab=50257,
-             prompt=64)
+DRIFT = {  # name -> shape; the tests look a case up by (shape name, layers)
+    "plm-1.3b": dict(seed=13, layers=24, hidden=2048, heads=16, kv_heads=16, head_dim=128, inter=8192, vocab=50257,
+                     prompt=64),
+    "plm-3b_2layers": dict(seed=14, layers=2, hidden=2560, heads=20, kv_heads=20, head_dim=128, inter=10240,
+                           vocab=50257, prompt=64),
+}
 VORONOI_CASES = [  # seed, rows, vocab, aux, kind
     (100, 2, 50257, 1024, "fp32"), (101, 2, 50257, 1024, "bf16"), (102, 3, 3000, 256, "fp32"),
     (103, 2, 8000, 512, "bf16"),
@@ -416,41 +420,44 @@ def _hf_llama(c: dict, w: dict, dtype: torch.dtype):
 
 
 def gen_drift(ref, out: Path):
-    """The bf16 drift of the reference's model family at the PLM-1.3B shape: HF LlamaForCausalLM with bf16 weights
-    run (a) in bf16 and (b) in fp32, against the oracle's forward of the same weights (bf16 storage, fp32 sums) and
-    the oracle with float64 sums, over a causal prompt. Stores the max abs differences of the final-norm logits."""
+    """The bf16 drift of the reference's model family at the benchmark shapes: HF LlamaForCausalLM with bf16
+    weights run (a) in bf16 and (b) in fp32, against the oracle's forward of the same weights (bf16 storage, fp32
+    sums) and the oracle with float64 sums, over a causal prompt. Stores the max abs differences of the logits."""
     sys.path.insert(0, str(HERE.parent.parent))
     from oracle import model as omodel
     from oracle import rounds as orounds
 
     torch.set_num_threads(os.cpu_count() or 1)
-    c = DRIFT
-    w = llama_weights(c["seed"], c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
-                      c["vocab"])
-    w = {key: ([t.bfloat16().float() for t in v] if isinstance(v, list) else v.bfloat16().float())
-         for key, v in w.items()}
-    ids = torch.randint(0, c["vocab"], (c["prompt"],), generator=torch.Generator().manual_seed(c["seed"] + 1))
-    positions = torch.arange(c["prompt"])[None]
-    logits = {}
-    for name, dtype in (("hf_bf16", torch.bfloat16), ("hf_fp32", torch.float32)):
-        model = _hf_llama(c, w, dtype)
-        with torch.no_grad():
-            logits[name] = model(input_ids=ids[None], position_ids=positions).logits[0].float()
-        del model
-    shape = omodel.ModelShape(c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
-                              c["vocab"], 64, 1, 1e-5, 10000.0, 4096)
-    pages = -(-c["prompt"] // 16)
-    for name, acc in (("oracle", "float32"), ("oracle_f64", "float64")):
-        om = omodel.OracleModel(shape, w, "bfloat16", 16, pages, np.arange(pages), accumulate=acc)
-        _, _, depth, own = orounds.chunk_layout(c["prompt"])
-        embeds = om.embed_rows(ids.numpy(), np.full(c["prompt"], 64))
-        hidden = om.forward(embeds, np.arange(c["prompt"]), 0, depth, own)
-        logits[name] = om.logits(hidden)
-        del om
-    diff = lambda a, b: float((logits[a] - logits[b]).abs().max())  # noqa: E731
-    res = {"config": c, "logit_abs_max": float(logits["hf_fp32"].abs().max()),
-           "hf_bf16_vs_hf_fp32": diff("hf_bf16", "hf_fp32"), "hf_bf16_vs_oracle": diff("hf_bf16", "oracle"),
-           "hf_fp32_vs_oracle": diff("hf_fp32", "oracle"), "oracle_vs_oracle_f64": diff("oracle", "oracle_f64"),
+    cases = {}
+    for name, c in DRIFT.items():
+        w = llama_weights(c["seed"], c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                          c["vocab"])
+        w = {key: ([t.bfloat16().float() for t in v] if isinstance(v, list) else v.bfloat16().float())
+             for key, v in w.items()}
+        ids = torch.randint(0, c["vocab"], (c["prompt"],), generator=torch.Generator().manual_seed(c["seed"] + 1))
+        positions = torch.arange(c["prompt"])[None]
+        logits = {}
+        for kind, dtype in (("hf_bf16", torch.bfloat16), ("hf_fp32", torch.float32)):
+            model = _hf_llama(c, w, dtype)
+            with torch.no_grad():
+                logits[kind] = model(input_ids=ids[None], position_ids=positions).logits[0].float()
+            del model
+        shape = omodel.ModelShape(c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"],
+                                  c["vocab"], 64, 1, 1e-5, 10000.0, 4096)
+        pages = -(-c["prompt"] // 16)
+        for kind, acc in (("oracle", "float32"), ("oracle_f64", "float64")):
+            om = omodel.OracleModel(shape, w, "bfloat16", 16, pages, np.arange(pages), accumulate=acc)
+            _, _, depth, own = orounds.chunk_layout(c["prompt"])
+            embeds = om.embed_rows(ids.numpy(), np.full(c["prompt"], 64))
+            hidden = om.forward(embeds, np.arange(c["prompt"]), 0, depth, own)
+            logits[kind] = om.logits(hidden)
+            del om
+        diff = lambda a, b: float((logits[a] - logits[b]).abs().max())  # noqa: E731
+        cases[name] = {"config": c, "logit_abs_max": float(logits["hf_fp32"].abs().max()),
+                       "hf_bf16_vs_hf_fp32": diff("hf_bf16", "hf_fp32"),
+                       "hf_bf16_vs_oracle": diff("hf_bf16", "oracle"), "hf_fp32_vs_oracle": diff("hf_fp32", "oracle"),
+                       "oracle_vs_oracle_f64": diff("oracle", "oracle_f64")}
+    res = {"cases": cases,
            "note": "max abs difference of the logits over all prompt rows; weights N(0, 0.02) rounded to bf16"}
     (out / "drift.json").write_text(json.dumps(res, indent=1) + "\n")
 
