@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 6
+#define PLM_ABI_VERSION 7
 
 enum plm_status {
   PLM_OK = 0,
@@ -99,6 +99,12 @@ typedef struct plm_gemm_epilogue {
   void* table;
   int32_t aux;
   int32_t a0;
+  /* PLM_EPI_QKV_ROPE, PLM_EPI_SILU_MUL (nullable): fp32 corrections corr[(r - corr_from) * corr_ld + n] added to
+   * output n of rows r >= corr_from before the epilogue's rotary embedding or SiLU, as y = round(round(y) + corr):
+   * a gated-LoRA adapter's output on the gated rows (plm/gated_lora.py:45-57) */
+  const float* corr;
+  int32_t corr_from;
+  int32_t corr_ld;
 } plm_gemm_epilogue;
 
 typedef struct plm_gemm_desc {
@@ -239,6 +245,11 @@ typedef struct plm_add_rmsnorm_desc {
   const float* partials;
   int32_t n_partials;
   int64_t partial_stride;
+  /* Nullable: x[r] = round(x[r] + corr[(r - corr_from) * corr_ld + i]) for rows r >= corr_from before the residual
+   * add (a gated-LoRA adapter's output on the gated rows, plm/gated_lora.py:45-57) */
+  const float* corr;
+  int32_t corr_from;
+  int32_t corr_ld;
 } plm_add_rmsnorm_desc;
 
 /* ---- round engine (one handle = one request stream on one GPU, batch 1) ---- */
@@ -257,6 +268,28 @@ typedef struct plm_model_desc {
   double epsilon, refocus, endpoint;
 } plm_model_desc;
 
+/* The PTP scheme of the reference's gated-LoRA distilled model (plm/auxiliary.py:78-113, plm/gated_lora.py:35-90):
+ * auxiliary rows blend rows of a float32 table at the request's uniforms, verify rows decode by inverse CDF over
+ * the top_k probabilities, and each projection with adapters adds x A^T B^T on a round's gated rows (row 1 on in
+ * round 0, row k on in a steady round, none in the prefill). Per layer and projection (nullable arrays, nullable
+ * entries): A stacks the shards' down-projections [shards * rank][in]; B stacks their up-projections in output order
+ * [out][rank], shard s of the output (q, k, v for qkv; gate, up for gate_up) reading rank slice s of x A^T. A handle
+ * with adapters runs the MLP as separate launches. */
+typedef struct plm_ptp_desc {
+  const float* embedding; /* [num_embeddings][hidden] float32 */
+  int32_t num_embeddings;
+  int32_t top_k;          /* inverse-CDF bins, 1..256 */
+  int32_t rank;           /* adapter rank (a multiple of 64; 0: no adapters) */
+  const void* const* qkv_a;
+  const void* const* qkv_b;
+  const void* const* o_a;
+  const void* const* o_b;
+  const void* const* gate_up_a;
+  const void* const* gate_up_b;
+  const void* const* down_a;
+  const void* const* down_b;
+} plm_ptp_desc;
+
 /* Borrowed device pointers; they must stay valid for the handle's lifetime. */
 typedef struct plm_weight_ptrs {
   const void* embed;      /* [>= vocab][hidden] */
@@ -272,6 +305,7 @@ typedef struct plm_weight_ptrs {
   const void* const* input_norm;
   const void* const* post_norm;
   const void* table;      /* optional [vocab][aux_vocab] Voronoi table; NULL: built at creation */
+  const plm_ptp_desc* ptp; /* NULL: the logit-Voronoi scheme of every PLM; else the PTP scheme (copied at creation) */
 } plm_weight_ptrs;
 
 typedef struct plm_round_desc {
@@ -368,6 +402,9 @@ int plm_create(const plm_model_desc* model, const plm_weight_ptrs* weights, cons
 int plm_destroy(plm_handle* h);
 int plm_set_block_table(plm_handle* h, const int32_t* table_host, int32_t n);
 int plm_set_aux_stream(plm_handle* h, const int64_t* cells, int64_t n, void* stream);
+/* The PTP scheme's auxiliary stream: n uniforms in [0, 1) (LinearInterpolationAuxiliary.sample_prior,
+ * plm/auxiliary.py:92-94; the stream _fill_aux draws, plm/decoder.py:407-412). */
+int plm_set_aux_uniforms(plm_handle* h, const float* u, int64_t n, void* stream);
 int plm_load_prompt(plm_handle* h, const int64_t* ids, int64_t n, void* stream);
 /* Sets the request's stop block on `stream` (done flag cleared): steady rounds stop committing once base reaches
  * max_tokens, or once a round confirms eos_token (>= 0; -1 disables the test) at an output position below

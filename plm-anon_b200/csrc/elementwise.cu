@@ -48,6 +48,7 @@ template <typename T>
 __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueArgs a) {
   __shared__ float red[32];
   __shared__ int64_t s_id, s_cell;
+  __shared__ float s_u;
   const int r = blockIdx.x, tid = threadIdx.x;
   grid_dependency_wait();
   allow_dependents();
@@ -69,11 +70,14 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
       if (r == 0) id = *a.anchor;
       else if (a.mode == kPrologueSteady && r < a.k) id = a.pending[r - 1];
       const int64_t rel_aux = a.rel_aux[r];
+      s_u = 0.f;  // the PTP scheme's value of rows without an auxiliary value (plm/decoder.py:107-108)
       if (rel_aux >= 0) {
         const int64_t index = *a.base + rel_aux;
         if (index < 0 || index >= a.aux_len) {
           record_error(a.err, kErrBadIndex);
           cell = 0;
+        } else if (a.ptp_embedding != nullptr) {
+          s_u = a.aux_u[index];
         } else {
           cell = a.aux_buf[index];
         }
@@ -118,7 +122,31 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
   T* __restrict__ nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
   const T* __restrict__ w = reinterpret_cast<const T*>(a.norm_weight);
   uint4 e[kMaxVecs], wv[kMaxVecs];
-  load_row<T>(src, a.hidden, e);
+  if (aux_row && a.ptp_embedding != nullptr) {
+    // LinearInterpolationAuxiliary.embed (plm/auxiliary.py:96-102): u scaled to [0, n - 1], the two neighbouring
+    // float32 rows weighted by the fraction, each step rounded on its own (no fused multiply-add), then cast to the
+    // model dtype (plm/decoder.py:264-268).
+    const int last = a.ptp_rows - 1;
+    const float scaled = __fmul_rn(s_u, float(last));
+    const float below = floorf(scaled);
+    const int lo = max(0, min(last, int(below)));
+    const int hi = min(lo + 1, last);
+    const float frac = __fsub_rn(scaled, below);
+    const float keep = __fsub_rn(1.0f, frac);
+    const float* rlo = a.ptp_embedding + size_t(lo) * a.hidden;
+    const float* rhi = a.ptp_embedding + size_t(hi) * a.hidden;
+#pragma unroll
+    for (int j = 0; j < kMaxVecs; ++j) {
+      const int c = tid + j * kRowThreads;
+      if (c * kVec >= a.hidden) continue;
+      T* ev = reinterpret_cast<T*>(&e[j]);
+#pragma unroll
+      for (int q = 0; q < kVec; ++q)
+        ev[q] = from_f32<T>(__fadd_rn(__fmul_rn(rlo[c * kVec + q], keep), __fmul_rn(rhi[c * kVec + q], frac)));
+    }
+  } else {
+    load_row<T>(src, a.hidden, e);
+  }
   load_row<T>(w, a.hidden, wv);
   float ss = 0.f;
 #pragma unroll
@@ -201,6 +229,20 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs
     }
   } else {
     load_row<T>(x, a.hidden, xv);
+  }
+  if (a.corr != nullptr && r >= a.corr_from) {
+    // a gated-LoRA adapter's output on this row, added to the projection's rounded output and rounded again
+    const float* __restrict__ cr = a.corr + size_t(r - a.corr_from) * a.corr_ld;
+#pragma unroll
+    for (int j = 0; j < kMaxVecs; ++j) {
+      const int c = tid + j * kRowThreads;
+      if (c * kVec >= a.hidden) continue;
+      const float4 lo = reinterpret_cast<const float4*>(cr)[2 * c], hi = reinterpret_cast<const float4*>(cr)[2 * c + 1];
+      const float add[kVec] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      T* xo = reinterpret_cast<T*>(&xv[j]);
+#pragma unroll
+      for (int q = 0; q < kVec; ++q) xo[q] = from_f32<T>(to_f32<T>(xo[q]) + add[q]);
+    }
   }
   float v[kMaxVecs][kVec];
   float ss = 0.f;
@@ -314,8 +356,14 @@ extern "C" int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* d, void
       (d->n_partials < 1 || d->n_partials > kMaxNormPartials || d->partial_stride < int64_t(d->rows) * d->hidden))
     return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: %d partials with stride %lld", d->n_partials,
                 (long long)d->partial_stride);
+  if (d->corr != nullptr && (d->corr_from < 0 || d->corr_ld < d->hidden || d->corr_ld % 4 != 0 || d->hidden % 8 != 0))
+    return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: corrections from row %d with stride %d", d->corr_from,
+                d->corr_ld);
   AddNormArgs a = {d->x,      d->residual,   d->normed,       d->weight,       d->hidden,
                    d->eps,    d->gather_row, d->gathered,     d->partials,     d->n_partials,
                    d->partial_stride};
+  a.corr = d->corr;
+  a.corr_from = d->corr_from;
+  a.corr_ld = d->corr_ld;
   return add_norm_launch(a, d->rows, static_cast<cudaStream_t>(stream), true);
 }

@@ -34,6 +34,11 @@ struct PrologueArgs {
   int32_t* positions;          // [rows]
   int64_t* slots;              // [rows]
   int round_scratch;           // nonzero: row r's K/V go to row r of the round scratch (slots[r] = r), not to a page
+  // The PTP scheme (nullable): auxiliary rows blend rows of this float32 table [ptp_rows][hidden] at the request's
+  // uniform aux_u[base + rel_aux] instead of taking an auxiliary-vocabulary row
+  const float* ptp_embedding;
+  int ptp_rows;
+  const float* aux_u;
   int* counters;               // zeroed at the start of the forward (the layer blocks' phase counters; may be null)
   int n_counters;
   int* err;
@@ -53,6 +58,9 @@ struct AddNormArgs {
   int64_t partial_stride = 0;       // floats between slices
   void* row_tiles = nullptr;        // non-null: the normed rows also as row tiles of `tile_rows` rows (common.cuh)
   int tile_rows = 0;
+  const float* corr = nullptr;      // non-null: x[r] = round(x[r] + corr[r - corr_from]) for rows r >= corr_from
+  int corr_from = 0;
+  int corr_ld = 0;
 };
 
 struct KvAppendArgs {

@@ -50,6 +50,9 @@ GemmArgs make_args(plm_ctx* ctx, const plm_gemm_desc& d, int tiles, int splits, 
                       e.num_heads, e.num_kv_heads, e.head_dim, e.page_size, e.num_slots, e.max_pos};
   a.logits = LogitsEpilogue{e.verify_logits, e.best_val, e.best_idx, e.n_verify, e.vocab};
   a.table = TableEpilogue{e.table, e.aux, e.a0};
+  a.corr = e.corr;
+  a.corr_from = e.corr_from;
+  a.corr_ld = e.corr_ld;
   return a;
 }
 

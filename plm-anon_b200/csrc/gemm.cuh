@@ -80,6 +80,9 @@ struct GemmArgs {
   QkvEpilogue qkv;
   LogitsEpilogue logits;
   TableEpilogue table;
+  const float* corr;  // kEpiQkvRope / kEpiSiluMul: fp32 corrections of rows >= corr_from (gated-LoRA adapters)
+  int corr_from;
+  int corr_ld;
 };
 
 constexpr int kGemmBK = 64;
@@ -342,8 +345,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int j0 = tile * 64;
     for (int idx = tid; idx < ncols * 64; idx += kGemmThreads) {
       const int lc = idx >> 6, f = idx & 63;
-      const float g = round_to<T>(red[lc * kStagePad + f]);
-      const float u = round_to<T>(red[lc * kStagePad + 64 + f]);
+      float g = round_to<T>(red[lc * kStagePad + f]);
+      float u = round_to<T>(red[lc * kStagePad + 64 + f]);
+      const int c = c_begin + lc;
+      if (args.corr != nullptr && c >= args.corr_from) {  // the adapter's output joins before the activation
+        const float* cr = args.corr + size_t(c - args.corr_from) * args.corr_ld;
+        g = round_to<T>(g + cr[j0 + f]);
+        u = round_to<T>(u + cr[args.gate_offset + j0 + f]);
+      }
       const float act = g / (1.0f + expf(-g)) * u;
       out[size_t(c_begin + lc) * args.ldo + j0 + f] = from_f32<T>(act);
     }
@@ -369,7 +378,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the last tile may run past n_out when (heads + 2 kv_heads) * head_dim is not a multiple of 128
     for (int lc = 0; lc < (F < args.n_out ? ncols : 0); ++lc) {
       const int c = c_begin + lc;
-      const float x = round_to<T>(red[lc * kStagePad + f]);
+      const float* cr = (args.corr != nullptr && c >= args.corr_from)
+                            ? args.corr + size_t(c - args.corr_from) * args.corr_ld : nullptr;
+      float x = round_to<T>(red[lc * kStagePad + f]);
+      if (cr != nullptr) x = round_to<T>(x + cr[F]);  // the adapter's output joins before the rotary embedding
       float y = x;
       if (rope) {
         const int pos = __ldg(q.positions + c);
@@ -377,7 +389,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           record_error(args.err, kErrBadIndex);
           continue;
         }
-        const float xp = round_to<T>(red[lc * kStagePad + fp]);
+        float xp = round_to<T>(red[lc * kStagePad + fp]);
+        if (cr != nullptr) xp = round_to<T>(xp + cr[tile * 128 + fp]);
         const float cv = to_f32<T>(__ldg(cs_tab + size_t(pos) * hd + dh));
         const float sv = to_f32<T>(__ldg(cs_tab + size_t(pos) * hd + half + dh));
         y = d < half ? x * cv - xp * sv : x * cv + xp * sv;

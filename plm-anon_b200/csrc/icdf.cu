@@ -14,6 +14,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "icdf.h"
 #include "runtime.h"
 
 namespace plm {
@@ -21,19 +22,7 @@ namespace {
 
 constexpr int kIcdfThreads = 1024;
 constexpr int kIcdfWarps = kIcdfThreads / 32;
-constexpr int kIcdfMaxVocab = 53248;  // 208 KB of float32 probabilities
-constexpr int kIcdfMaxTopK = 256;
 
-struct IcdfArgs {
-  const float* logits;
-  int64_t ld;
-  const float* u;
-  int n_rows, vocab, top_k;
-  int64_t* tokens;
-  int32_t* ids_out;
-  float* edges_out;
-  int* err;
-};
 
 __device__ __forceinline__ float block_max(float v, float* red) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -159,7 +148,14 @@ __global__ void __launch_bounds__(kIcdfThreads, 1) icdf_decode_kernel(const Icdf
     const int k = taken < K ? taken : K;
     float total = 0.f;
     for (int j = 0; j < k; ++j) total += chosen_p[j];
-    const float u = a.u[row];
+    float u = 0.f;
+    if (a.u_base == nullptr) {
+      u = a.u[row];
+    } else {  // the round's uniforms: the request's stream from the round's first output position
+      const int64_t index = *a.u_base + row;
+      if (index < 0 || index >= a.u_len) record_error(a.err, kErrBadIndex);
+      else u = a.u[index];
+    }
     double run = 0.0;
     int bin = -1;
     for (int j = 0; j < k; ++j) {
@@ -175,6 +171,16 @@ __global__ void __launch_bounds__(kIcdfThreads, 1) icdf_decode_kernel(const Icdf
 }
 
 }  // namespace
+
+int icdf_launch(const IcdfArgs& a, cudaStream_t stream, bool pdl) {
+  const int smem = a.vocab * int(sizeof(float));
+  int st = raise_smem_limit(reinterpret_cast<const void*>(icdf_decode_kernel), smem,
+                            "cudaFuncSetAttribute(icdf smem)");
+  if (st != PLM_OK) return st;
+  return check_cuda(launch(icdf_decode_kernel, dim3(a.n_rows), dim3(kIcdfThreads), size_t(smem), stream, pdl, a),
+                    "icdf_decode_kernel");
+}
+
 }  // namespace plm
 
 using namespace plm;
@@ -188,13 +194,7 @@ extern "C" int plm_icdf_decode(plm_ctx* ctx, const plm_icdf_desc* d, void* strea
   if (d->top_k < 1 || d->top_k > kIcdfMaxTopK || d->top_k > d->vocab)
     return fail(PLM_ERR_UNSUPPORTED, "plm_icdf_decode: top_k %d (1..%d, at most the vocabulary)", d->top_k,
                 kIcdfMaxTopK);
-  const int smem = d->vocab * int(sizeof(float));
-  int st = raise_smem_limit(reinterpret_cast<const void*>(icdf_decode_kernel), smem,
-                            "cudaFuncSetAttribute(icdf smem)");
-  if (st != PLM_OK) return st;
   IcdfArgs a = {d->logits, d->ld, d->u, d->n_rows, d->vocab, d->top_k, d->tokens, d->ids_out, d->edges_out,
-                ctx->err};
-  return check_cuda(launch(icdf_decode_kernel, dim3(d->n_rows), dim3(kIcdfThreads), size_t(smem),
-                           static_cast<cudaStream_t>(stream), true, a),
-                    "icdf_decode_kernel");
+                nullptr, 0, ctx->err};
+  return icdf_launch(a, static_cast<cudaStream_t>(stream), true);
 }

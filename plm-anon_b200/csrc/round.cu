@@ -9,6 +9,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <array>
 #include <cstring>
 #include <map>
 #include <vector>
@@ -16,6 +17,7 @@
 #include "attention.h"
 #include "commit.h"
 #include "elementwise.h"
+#include "icdf.h"
 #include "mlp.h"
 #include "runtime.h"
 #include "verify.h"
@@ -89,6 +91,21 @@ struct plm_handle {
   void* block_tiles = nullptr;  // per layer: packed o, gate_up, down (pack.cu)
   void *attn_tiles = nullptr, *x_tiles = nullptr, *act_tiles = nullptr;  // row operands as row tiles (common.cuh)
   size_t block_o_bytes = 0, block_gate_up_bytes = 0, block_layer_bytes = 0;
+  // The PTP scheme of the gated-LoRA model (ptp_embedding null: the logit-Voronoi scheme of every PLM)
+  const float* ptp_embedding = nullptr;
+  int ptp_rows = 0, ptp_top_k = 0, lora_rank = 0;
+  float* aux_u = nullptr;  // [aux_len] the request's uniforms
+  // per layer and projection (qkv, o, gate_up, down): the adapter's shards, each a down map (rank rows of the stacked
+  // A) and an up map (its output rows of B); empty when the projection has no adapter
+  struct LoraShard {
+    const void* a = nullptr;
+    const void* b = nullptr;
+    CUtensorMap map_a, map_b;
+    int out0 = 0, width = 0;  // the shard's output columns
+  };
+  std::vector<std::array<std::vector<LoraShard>, 4>> lora;
+  void* lora_hidden = nullptr;  // [3][R][rank] model dtype: x A_s^T of the gated rows, per shard
+  float* lora_corr = nullptr;   // [R][widest output] fp32: the adapter's output of the gated rows
 };
 
 namespace plm {
@@ -102,7 +119,7 @@ void* round_plane(plm_handle* h, int layer, int which) {
          (size_t(layer) * 2 + which) * size_t(h->W) * h->m.num_kv_heads * h->m.head_dim;
 }
 
-int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMap** out) {
+int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMap** out, int x_rows = 0) {
   const int ntok = gemm_token_tile(rows);
   if (ntok < 0) return fail(PLM_ERR_UNSUPPORTED, "row map: %d rows", rows);
   auto key = std::make_pair(buffer, ntok);
@@ -113,7 +130,7 @@ int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMa
     d.x = buffer;
     d.k = k;
     d.rows = rows;
-    d.x_rows = buffer == h->gathered ? 16 : h->R;
+    d.x_rows = x_rows > 0 ? x_rows : buffer == h->gathered ? 16 : h->R;
     CUtensorMap map;
     int st = gemm_row_map(&map, d);
     if (st != PLM_OK) return st;
@@ -124,21 +141,21 @@ int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMa
 }
 
 int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, const void* x, int rows,
-         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s, int splits = 0) {
+         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s, int splits = 0, int x_rows = 0) {
   plm_gemm_desc d = {};
   d.dtype = h->m.dtype;
   d.w = w;
   d.n_out = n_out;
   d.k = k;
   d.x = x;
-  d.x_rows = x == h->gathered ? 16 : h->R;
+  d.x_rows = x_rows > 0 ? x_rows : x == h->gathered ? 16 : h->R;
   d.rows = rows;
   d.out = out;
   d.ldo = ldo;
   d.splits = splits;
   d.epi = epi;
   const CUtensorMap* mx = nullptr;
-  int st = row_map(h, x, k, rows, &mx);
+  int st = row_map(h, x, k, rows, &mx, x_rows);
   if (st != PLM_OK) return st;
   return gemm_launch(h->ctx, d, mw, mx, s, true);
 }
@@ -182,11 +199,43 @@ int layer_block_launch(plm_handle* h, int l, int rows, cudaStream_t s) {
 // The Llama forward of `rows` rows whose logical KV indices start at *offset_ptr (vLLM llama.py:253-314):
 // prologue (+ layer-0 input norm), then per layer qkv(+RoPE, KV scatter) -> attention -> o -> add+norm ->
 // gate_up(+SiLU) -> down -> add+norm (the next layer's input norm, or the final norm).
+// The gated-LoRA correction of projection `proj` (0 qkv, 1 o, 2 gate_up, 3 down) of layer `l` on rows
+// [from, rows) of `x` ([R][k] model dtype): per shard s, hidden_s = round(x A_s^T) into the hidden slices, then
+// hidden_s B_s^T in fp32 into the shard's columns of lora_corr (row r - from, stride n_total)
+// (plm/gated_lora.py:45-57). The projection's own epilogue (or the norm after it) adds it. Returns the stride,
+// or 0 when the projection has no adapter (nothing launched).
+int lora_correction(plm_handle* h, int l, int proj, const void* x, int k, int from, int rows, int n_total,
+                    cudaStream_t s, int* corr_ld) {
+  *corr_ld = 0;
+  if (h->ptp_embedding == nullptr || h->lora_rank == 0 || from >= rows || h->lora[l][proj].empty()) return PLM_OK;
+  const int g_rows = rows - from;
+  const int rank = h->lora_rank;
+  const void* xg = static_cast<const __nv_bfloat16*>(x) + size_t(from) * k;
+  int st = PLM_OK;
+  const std::vector<plm_handle::LoraShard>& shards = h->lora[l][proj];
+  for (size_t sh = 0; sh < shards.size() && st == PLM_OK; ++sh) {
+    const plm_handle::LoraShard& z = shards[sh];
+    void* hidden = static_cast<__nv_bfloat16*>(h->lora_hidden) + sh * size_t(h->R) * rank;
+    plm_gemm_epilogue store = {};
+    store.kind = PLM_EPI_STORE;
+    st = gemm(h, z.a, &z.map_a, rank, k, xg, g_rows, store, hidden, rank, s, 0, h->R - from);
+    plm_gemm_epilogue part = {};
+    part.kind = PLM_EPI_PARTIAL;
+    if (st == PLM_OK)
+      st = gemm(h, z.b, &z.map_b, z.width, rank, hidden, g_rows, part, h->lora_corr + z.out0, n_total, s, 1);
+  }
+  if (st == PLM_OK) *corr_ld = n_total;
+  return st;
+}
+
 // A round's forward (round0 or steady mode) writes its rows' K/V into the round scratch, and attention reads the
 // forward's own keys from there; a prefill writes straight into the pages (every prompt row is committed).
 int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const int64_t* relpos, const int64_t* relaux,
             const int32_t* depth, const int32_t* own, int attn_splits, int gather_row, cudaStream_t s) {
   const bool round_rows = mode != kProloguePrefill;
+  // the first row a gated-LoRA adapter acts on: row k of a steady round, row 1 of round 0, none in a prefill
+  // (plm/decoder.py:298, 317, 381)
+  const int gated_from = mode == kPrologueSteady ? h->rd.k : mode == kPrologueRound0 ? 1 : rows;
   const plm_model_desc& m = h->m;
   const int hidden = m.hidden, hd = m.head_dim;
   const int q_size = m.num_heads * hd, kv_size = m.num_kv_heads * hd;
@@ -222,6 +271,9 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
   p.positions = h->positions;
   p.slots = h->slots;
   p.round_scratch = round_rows ? 1 : 0;
+  p.ptp_embedding = h->ptp_embedding;
+  p.ptp_rows = h->ptp_rows;
+  p.aux_u = h->aux_u;
   const bool layer_block = h->mlp.sched != nullptr && rows <= kMlpMaxRows;
   p.counters = h->block_ctr;
   p.n_counters = h->block_ctr != nullptr ? 4 * m.num_layers : 0;
@@ -251,6 +303,12 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
       e.num_slots = int64_t(h->rd.num_pages) * h->rd.page_size;
     }
     e.max_pos = m.max_pos;
+    st = lora_correction(h, l, 0, h->x_norm, hidden, gated_from, rows, q_size + 2 * kv_size, s, &e.corr_ld);
+    if (st != PLM_OK) return st;
+    if (e.corr_ld > 0) {
+      e.corr = h->lora_corr;
+      e.corr_from = gated_from;
+    }
     st = gemm(h, h->qkv[l], &h->map_qkv[l], q_size + 2 * kv_size, hidden, h->x_norm, rows, e, nullptr, 0, s);
     if (st != PLM_OK) return st;
 
@@ -288,24 +346,40 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     plm_gemm_epilogue part = {};
     part.kind = PLM_EPI_PARTIAL;
     const int64_t slice = int64_t(rows) * hidden;
-    int s_d = 0;
+    int s_d = 0, down_ld = 0;
     if (layer_block) {  // o, its norm, gate_up and down in one launch
       st = layer_block_launch(h, l, rows, s);
       if (st != PLM_OK) return st;
       s_d = h->mlp.down_splits;
     } else {
+      int ld = 0;
+      st = lora_correction(h, l, 1, h->attn, q_size, gated_from, rows, hidden, s, &ld);
+      if (st != PLM_OK) return st;
       const int s_o = gemm_partial_splits(h->ctx, hidden, q_size, rows);
       st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, part, h->partials, hidden, s, s_o);
       if (st != PLM_OK) return st;
       AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
                         h->partials, s_o, slice};
+      if (ld > 0) {
+        n1.corr = h->lora_corr;
+        n1.corr_from = gated_from;
+        n1.corr_ld = ld;
+      }
       st = add_norm_launch(n1, rows, s, true);
       if (st != PLM_OK) return st;
       plm_gemm_epilogue silu = {};
       silu.kind = PLM_EPI_SILU_MUL;
       silu.gate_offset = m.intermediate;
+      st = lora_correction(h, l, 2, h->x_norm, hidden, gated_from, rows, 2 * m.intermediate, s, &silu.corr_ld);
+      if (st != PLM_OK) return st;
+      if (silu.corr_ld > 0) {
+        silu.corr = h->lora_corr;
+        silu.corr_from = gated_from;
+      }
       st = gemm(h, h->gate_up[l], &h->map_gate_up[l], 2 * m.intermediate, hidden, h->x_norm, rows, silu, h->act,
                 m.intermediate, s);
+      if (st != PLM_OK) return st;
+      st = lora_correction(h, l, 3, h->act, m.intermediate, gated_from, rows, hidden, s, &down_ld);
       if (st != PLM_OK) return st;
       s_d = gemm_partial_splits(h->ctx, hidden, m.intermediate, rows);
       st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, part, h->partials, hidden, s,
@@ -316,6 +390,11 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     AddNormArgs n2 = {nullptr,  h->residual,           h->x_norm, last ? h->final_norm : h->in_norm[l + 1],
                       hidden,   m.rms_eps,             last ? gather_row : -1, last ? h->gathered : nullptr,
                       h->partials, s_d, slice};
+    if (down_ld > 0) {
+      n2.corr = h->lora_corr;
+      n2.corr_from = gated_from;
+      n2.corr_ld = down_ld;
+    }
     st = add_norm_launch(n2, rows, s, true);
     if (st != PLM_OK) return st;
   }
@@ -335,6 +414,24 @@ int lm_head(plm_handle* h, const void* x, int rows, int n_verify, cudaStream_t s
 
 int verify(plm_handle* h, int n_rows, int mode, const int64_t* aux_base, cudaStream_t s) {
   VerifyArgs a = {};
+  if (h->ptp_embedding != nullptr) {
+    // The PTP scheme decodes by inverse CDF at the request's uniforms (plm/auxiliary.py:104-113); the verify kernel
+    // then adds only the relaxed rule's verdicts and the bookkeeping.
+    IcdfArgs ic = {};
+    ic.logits = h->verify_logits;
+    ic.ld = h->m.vocab;
+    ic.u = h->aux_u;
+    ic.n_rows = n_rows;
+    ic.vocab = h->m.vocab;
+    ic.top_k = h->ptp_top_k;
+    ic.tokens = h->verify;
+    ic.u_base = aux_base;
+    ic.u_len = h->rd.aux_len;
+    ic.err = h->ctx->err;
+    const int st = icdf_launch(ic, s, true);
+    if (st != PLM_OK) return st;
+    a.tokens_given = 1;
+  }
   a.logits = h->verify_logits;
   a.vocab = h->m.vocab;
   a.logits_stride = h->m.vocab;
@@ -442,15 +539,24 @@ int validate_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm
     return fail(PLM_ERR_INVALID, "plm_create: hidden / intermediate / head_dim must be multiples of 64");
   if ((m->num_heads * m->head_dim) % 64 != 0 || m->num_heads % m->num_kv_heads != 0)
     return fail(PLM_ERR_INVALID, "plm_create: heads %d / kv heads %d", m->num_heads, m->num_kv_heads);
-  if (m->vocab < m->top_m || m->aux_vocab < 32) return fail(PLM_ERR_INVALID, "plm_create: vocab / aux vocabulary");
+  const plm_ptp_desc* ptp = w->ptp;
+  if (ptp == nullptr && (m->vocab < m->top_m || m->aux_vocab < 32))
+    return fail(PLM_ERR_INVALID, "plm_create: vocab / aux vocabulary");
+  if (ptp != nullptr) {
+    if (!ptp->embedding || ptp->num_embeddings < 1 || ptp->top_k < 1 || ptp->top_k > kIcdfMaxTopK ||
+        ptp->top_k > m->vocab || m->vocab > kIcdfMaxVocab || ptp->rank < 0 || ptp->rank % 64 != 0 ||
+        ptp->rank > 256)
+      return fail(PLM_ERR_INVALID, "plm_create: PTP scheme (embeddings %d, top_k %d, rank %d, vocab %d)",
+                  ptp->num_embeddings, ptp->top_k, ptp->rank, m->vocab);
+  }
   if (r->k < 1 || r->k + r->k * r->k > 256 || r->k > 32)
     return fail(PLM_ERR_UNSUPPORTED, "plm_create: k=%d (round width must be <= 256)", r->k);
   if (r->page_size < 1 || r->num_pages < 1 || r->max_pages < 1)
     return fail(PLM_ERR_INVALID, "plm_create: paging");
   if (r->max_prefill < 1 || r->max_prefill > kMaxPrefillRows)
     return fail(PLM_ERR_INVALID, "plm_create: max_prefill %d (1..%d)", r->max_prefill, kMaxPrefillRows);
-  if (!w->embed || !w->lm_head || !w->final_norm || !w->aux_vocab || !w->mask_aux || !w->cos_sin || !w->qkv ||
-      !w->o || !w->gate_up || !w->down || !w->input_norm || !w->post_norm)
+  if (!w->embed || !w->lm_head || !w->final_norm || !w->cos_sin || !w->qkv || !w->o || !w->gate_up || !w->down ||
+      !w->input_norm || !w->post_norm || (ptp == nullptr && (!w->aux_vocab || !w->mask_aux)))
     return fail(PLM_ERR_INVALID, "plm_create: missing weight pointer");
   return PLM_OK;
 }
@@ -470,7 +576,7 @@ int plm_destroy(plm_handle* h) {
                   h->r0_relpos, h->r0_relaux, h->st_depth, h->st_own, h->r0_depth, h->r0_own, h->causal_depth,
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
                   h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->stop, h->round_kv,
-                  h->commit, h->block_ctr,
+                  h->commit, h->aux_u, h->lora_hidden, h->lora_corr, h->block_ctr,
                   h->block_tiles, h->attn_tiles, h->x_tiles, h->act_tiles};
   for (void* b : bufs) cudaFree(b);
   mlp_schedule_destroy(&h->mlp);
@@ -559,7 +665,49 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   if (st == PLM_OK) st = dev_alloc(&h->best_idx, size_t(h->lm_tiles) * h->W, "argmax partials");
   if (st == PLM_OK) st = dev_alloc(&h->verify, 32, "verify");
   if (st == PLM_OK) st = dev_alloc(&h->flags, 32, "flags");
-  if (st == PLM_OK && rd->separate_mlp == 0 && hidden % 128 == 0 && I % 128 == 0 && q_size % 128 == 0 &&
+  // the PTP scheme: its table, the uniform stream and the adapters' maps and buffers
+  const bool adapters = w->ptp != nullptr && w->ptp->rank > 0;
+  if (st == PLM_OK && w->ptp != nullptr) {
+    const plm_ptp_desc& pd = *w->ptp;
+    h->ptp_embedding = pd.embedding;
+    h->ptp_rows = pd.num_embeddings;
+    h->ptp_top_k = pd.top_k;
+    h->lora_rank = pd.rank;
+    st = dev_alloc(&h->aux_u, size_t(h->rd.aux_len), "uniform stream");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->aux_u, 0, size_t(h->rd.aux_len) * 4), "uniform stream");
+    h->lora.assign(L, {});
+    const void* const* const As[4] = {pd.qkv_a, pd.o_a, pd.gate_up_a, pd.down_a};
+    const void* const* const Bs[4] = {pd.qkv_b, pd.o_b, pd.gate_up_b, pd.down_b};
+    const int ins[4] = {hidden, q_size, hidden, I};
+    const std::vector<int> outs[4] = {{q_size, kv_size, kv_size}, {hidden}, {I, I}, {hidden}};
+    for (int l = 0; l < L && adapters && st == PLM_OK; ++l) {
+      for (int pj = 0; pj < 4 && st == PLM_OK; ++pj) {
+        if (As[pj] == nullptr || Bs[pj] == nullptr || As[pj][l] == nullptr || Bs[pj][l] == nullptr) continue;
+        int out0 = 0;
+        for (size_t sh = 0; sh < outs[pj].size() && st == PLM_OK; ++sh) {
+          plm_handle::LoraShard z;
+          z.a = static_cast<const __nv_bfloat16*>(As[pj][l]) + sh * size_t(pd.rank) * ins[pj];
+          z.b = static_cast<const __nv_bfloat16*>(Bs[pj][l]) + size_t(out0) * pd.rank;
+          z.out0 = out0;
+          z.width = outs[pj][sh];
+          plm_gemm_desc d = {};
+          d.dtype = m->dtype;
+          d.w = z.a, d.n_out = pd.rank, d.k = ins[pj], d.epi.kind = PLM_EPI_STORE;
+          st = gemm_weight_map(&z.map_a, d);
+          d.w = z.b, d.n_out = z.width, d.k = pd.rank, d.epi.kind = PLM_EPI_PARTIAL;
+          if (st == PLM_OK) st = gemm_weight_map(&z.map_b, d);
+          h->lora[l][pj].push_back(z);
+          out0 += z.width;
+        }
+      }
+    }
+    const size_t widest_out = size_t(std::max({q_size + 2 * kv_size, 2 * I, hidden}));
+    if (st == PLM_OK && adapters)
+      st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->lora_hidden), size_t(3) * R * pd.rank, "adapter rows");
+    if (st == PLM_OK && adapters) st = dev_alloc(&h->lora_corr, R * widest_out, "adapter corrections");
+  }
+  // The layer block fuses o, its norm, gate_up and down; a model with adapters runs them as separate launches.
+  if (st == PLM_OK && rd->separate_mlp == 0 && !adapters && hidden % 128 == 0 && I % 128 == 0 && q_size % 128 == 0 &&
       hidden <= 4096) {
     st = mlp_schedule_create(h->ctx->num_sms, hidden, I, q_size, &h->mlp);
     // row tiles of up to kMlpMaxRows rows, zeroed once (rows past a forward's count are read but never stored)
@@ -683,7 +831,7 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
                                           int64_t(rd->max_pages) * rd->page_size);
 
   // the Voronoi cost table -(aux_vocab . lm_head^T)^T, [vocab][A] (plm/auxiliary.py:56-65)
-  if (w->table != nullptr) {
+  if (w->table != nullptr || w->ptp != nullptr) {  // the PTP scheme decodes without a cost table
     h->table = const_cast<void*>(w->table);
   } else {
     st = dev_alloc(reinterpret_cast<__nv_bfloat16**>(&h->table), size_t(m->vocab) * m->aux_vocab, "Voronoi table");
@@ -725,6 +873,13 @@ int plm_set_aux_stream(plm_handle* h, const int64_t* cells, int64_t n, void* str
   if (!h || !cells || n < 1 || n > h->rd.aux_len) return fail(PLM_ERR_INVALID, "plm_set_aux_stream: n=%lld", (long long)n);
   return check_cuda(cudaMemcpyAsync(h->aux_buf, cells, size_t(n) * 8, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
                     "aux stream copy");
+}
+
+int plm_set_aux_uniforms(plm_handle* h, const float* u, int64_t n, void* stream) {
+  if (!h || !u || n < 1 || n > h->rd.aux_len) return fail(PLM_ERR_INVALID, "plm_set_aux_uniforms: n=%lld", (long long)n);
+  if (h->aux_u == nullptr) return fail(PLM_ERR_INVALID, "plm_set_aux_uniforms: the handle's scheme has no uniforms");
+  return check_cuda(cudaMemcpyAsync(h->aux_u, u, size_t(n) * 4, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
+                    "uniform stream copy");
 }
 
 int plm_load_prompt(plm_handle* h, const int64_t* ids, int64_t n, void* stream) {

@@ -65,6 +65,8 @@ struct VerifyArgs {
   float* dbg_stats;          // [n_rows][4] max, sum of exp, normaliser, unit
   int32_t* dbg_sigma;        // [n_rows] shortlist index of the decoded token
   int64_t* dbg_phase_ns;     // [n_rows][kPhaseSlots] ns from kernel start to the end of each phase (nullable)
+  int tokens_given;          // nonzero: verify[] already holds the rows' tokens (inverse-CDF decode); only the
+                             // relaxed rule's verdicts and the bookkeeping run
   Bookkeeping book;
   int* counter;              // arrival counter (zero between launches)
   int* err;

@@ -405,6 +405,11 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
   }
   phase(1);
 
+  // With tokens_given the rows' tokens were decoded before this launch (the PTP scheme's inverse CDF): only the
+  // relaxed rule's verdicts and the bookkeeping remain.
+  if (a.tokens_given) {
+    if (rank == 0 && tid == 0 && a.flags != nullptr) a.flags[r] = flag;
+  } else {
   // ---------------- 2a. exact top-M: per slice, then merged over the cluster ----------------
   // Prefilter: a histogram of the keys' top 11 bits finds the bin holding the slice's want-th largest key; the
   // elements at or above that bin (usually a few hundred) are compacted into all_key / all_idx and the exact top-want
@@ -933,6 +938,8 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
     if (a.dbg_bias != nullptr) a.dbg_bias[r * M + tid] = s->bias[tid];
   }
 
+  }  // !a.tokens_given
+
   // ---------------- 5. bookkeeping by the last cluster ----------------
   const Bookkeeping& b = a.book;
   if (b.mode == kBookNone || rank != 0) return;
@@ -1077,6 +1084,11 @@ int verify_launch(const VerifyArgs& a, int dtype, int n_rows, cudaStream_t strea
 
 int verify_validate(const VerifyArgs& a, int n_rows) {
   if (n_rows < 1 || n_rows > 32) return fail(PLM_ERR_INVALID, "verify decode: %d rows (1..32)", n_rows);
+  if (a.tokens_given) {  // rule verdicts and bookkeeping only: no Voronoi table, cells or shortlist
+    if (a.logits == nullptr || a.verify == nullptr) return fail(PLM_ERR_INVALID, "verify decode: null operand");
+    if (a.vocab < 1 || a.vocab > kCluster * kMaxSlice)
+      return fail(PLM_ERR_UNSUPPORTED, "verify decode: vocab %d (1..%d)", a.vocab, kCluster * kMaxSlice);
+  } else {
   if (a.logits == nullptr || a.table == nullptr || a.verify == nullptr || a.aux_buf == nullptr)
     return fail(PLM_ERR_INVALID, "verify decode: null operand");
   if (a.top_m < 1 || a.top_m > kMaxTopM || (a.top_m & (a.top_m - 1)) != 0)
@@ -1088,6 +1100,7 @@ int verify_validate(const VerifyArgs& a, int n_rows) {
                 kCluster * kMaxOwned);
   if (a.shortlist > a.top_m) return fail(PLM_ERR_INVALID, "verify decode: shortlist > top_m");
   if (a.rounds < 0 || a.rounds > 4 || a.sweeps < 0) return fail(PLM_ERR_INVALID, "verify decode: rounds/sweeps");
+  }
   if (a.n_accept > 0 && a.pending == nullptr) return fail(PLM_ERR_INVALID, "verify decode: pending missing");
   if (a.book.mode != kBookNone) {
     const Bookkeeping& b = a.book;

@@ -86,19 +86,23 @@ class RoundDecoder:
             aux_vocab=c.aux_vocab, num_aux_tokens=c.num_aux_tokens, rms_eps=c.rms_eps,
             max_pos=self.cos_sin.shape[0], top_m=c.top_m, shortlist=min(c.shortlist, c.top_m), rounds=c.rounds,
             sweeps=c.sweeps, epsilon=0.15, refocus=0.35, endpoint=0.0087)
+        self.ptp = weights.ptp_embedding is not None
+        ptp_desc = self._ptp_desc(weights) if self.ptp else None
         ptrs = native.WeightPtrs(
             embed=weights.embed.data_ptr(), lm_head=weights.lm_head.data_ptr(),
             final_norm=weights.final_norm.data_ptr(), aux_vocab=weights.aux_vocab.data_ptr(),
             mask_aux=weights.mask_aux.data_ptr(), cos_sin=self.cos_sin.data_ptr(),
             qkv=self._layer_arrays[0], o=self._layer_arrays[1], gate_up=self._layer_arrays[2],
-            down=self._layer_arrays[3], input_norm=self._layer_arrays[4], post_norm=self._layer_arrays[5], table=None)
+            down=self._layer_arrays[3], input_norm=self._layer_arrays[4], post_norm=self._layer_arrays[5], table=None,
+            ptp=None if ptp_desc is None else native.pointer(ptp_desc))
         rule = native.RULE_FLOOR if accept_rule == "floor" else native.RULE_NUCLEUS
         round_desc = native.RoundDesc(
             k=k, rule=rule, threshold=-1.0 if threshold is None else float(threshold), page_size=block_size,
             num_pages=self.num_pages, max_pages=self.max_pages, out_capacity=self.max_seq,
             seq_capacity=self.sequence_capacity, aux_len=AUX_STREAM_LENGTH, max_prefill=max_prefill,
             separate_mlp=1 if separate_mlp else 0)
-        self.handle = native.Handle(model, ptrs, round_desc, keepalive=(weights, self.cos_sin, self._layer_arrays))
+        self.handle = native.Handle(model, ptrs, round_desc,
+                                    keepalive=(weights, self.cos_sin, self._layer_arrays, ptp_desc))
         if block_table is not None:
             self.handle.set_block_table(block_table)
         st = self.handle.state()
@@ -115,7 +119,7 @@ class RoundDecoder:
         self.hidden_normed = native.device_view(st.hidden_normed, (st.row_capacity, c.hidden), torch.bfloat16)
         self.kv_cache = native.device_view(
             st.kv_cache, (c.num_layers, 2, self.num_pages, c.num_kv_heads, block_size, c.head_dim), torch.bfloat16)
-        self.table = native.device_view(st.table, (c.vocab, c.aux_vocab), torch.bfloat16)
+        self.table = None if self.ptp else native.device_view(st.table, (c.vocab, c.aux_vocab), torch.bfloat16)
         self.stop_block = native.device_view(st.stop, (4,), torch.int64)
         # [base, done] of the newest finished round, copied by every replay into pinned host memory
         self.poll_host = torch.zeros(2, dtype=torch.long).pin_memory()
@@ -149,15 +153,35 @@ class RoundDecoder:
         self.poll_host[0].copy_(self.base_t, non_blocking=True)
         self.poll_host[1].copy_(self.stop_block[3], non_blocking=True)
 
+    def _ptp_desc(self, weights: PLMWeights) -> native.PtpDesc:
+        """The PTP scheme for plm_create: the interpolation table and, per projection, arrays of per-layer A and B
+        pointers (null where a layer's projection has no adapter)."""
+        adapters = weights.adapters or []
+        rank = adapters[0][next(iter(adapters[0]))][1].shape[1] if adapters and adapters[0] else 0
+        arrays = {}
+        for name in ("qkv", "o", "gate_up", "down"):
+            for i, part in enumerate(("a", "b")):
+                ptrs = [layer[name][i].data_ptr() if name in layer else None for layer in adapters]
+                arrays[f"{name}_{part}"] = (native.c_void_p * len(ptrs))(*ptrs) if any(ptrs) else None
+        self._ptp_arrays = arrays
+        return native.PtpDesc(embedding=weights.ptp_embedding.data_ptr(), num_embeddings=weights.ptp_embedding.shape[0],
+                              top_k=weights.ptp_top_k, rank=rank, **arrays)
+
     def _fill_aux(self, seed: int) -> None:
-        """Per request: A-ary auxiliary cells from a CUDA generator seeded with ``seed`` (the stream of
-        plm/decoder.py:407-412, drawn as LogitVoronoiAuxiliary.sample_prior does, plm/auxiliary.py:46-48). A seed
-        already in the handle is not drawn again."""
+        """Per request: the auxiliary stream from a CUDA generator seeded with ``seed`` (plm/decoder.py:407-412), as
+        the scheme's sample_prior draws it: A-ary cells for the logit-Voronoi scheme (plm/auxiliary.py:46-48),
+        uniforms in [0, 1) for the PTP scheme (plm/auxiliary.py:92-94). A seed already in the handle is not drawn
+        again."""
         if seed == self.aux_seed:
             return
-        cells = torch.randint(self.config.aux_vocab, (AUX_STREAM_LENGTH,), dtype=torch.long, device="cuda",
-                              generator=torch.Generator(device="cuda").manual_seed(seed))
-        self.handle.set_aux_stream(cells)
+        generator = torch.Generator(device="cuda").manual_seed(seed)
+        if self.ptp:
+            cells = torch.rand(AUX_STREAM_LENGTH, dtype=torch.float32, device="cuda", generator=generator)
+            self.handle.set_aux_uniforms(cells)
+        else:
+            cells = torch.randint(self.config.aux_vocab, (AUX_STREAM_LENGTH,), dtype=torch.long, device="cuda",
+                                  generator=generator)
+            self.handle.set_aux_stream(cells)
         torch.cuda.current_stream().synchronize()  # ``cells`` must outlive the copy
         self.aux_seed = seed
 

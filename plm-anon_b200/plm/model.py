@@ -114,6 +114,12 @@ class PLMWeights:
     down: list = field(default_factory=list)
     input_norm: list = field(default_factory=list)
     post_norm: list = field(default_factory=list)
+    # The PTP scheme of the gated-LoRA model (plm/auxiliary.py:78-113, plm/gated_lora.py:35-90); None: the
+    # logit-Voronoi scheme of every PLM. adapters: per layer, projection name -> (A [shards * rank][in],
+    # B [out][rank] with the shards' up-projections stacked in output order).
+    ptp_embedding: torch.Tensor | None = None
+    ptp_top_k: int = 128
+    adapters: list | None = None
 
     @property
     def device(self) -> torch.device:
@@ -142,6 +148,36 @@ class PLMWeights:
             w.input_norm.append(mat(c.hidden, mean=1.0))
             w.post_norm.append(mat(c.hidden, mean=1.0))
         return w
+
+    def with_ptp(self, rank: int = 64, num_embeddings: int = 3, top_k: int = 128, seed: int = 0,
+                 projections=("qkv", "o", "gate_up", "down")) -> "PLMWeights":
+        """The same base model as a synthetic PTP model: a float32 interpolation table [num_embeddings, hidden] and
+        rank-``rank`` adapters on ``projections`` of every layer, all N(0, 0.02) from a seeded generator."""
+        c = self.config
+        g = torch.Generator(device=self.device).manual_seed(seed)
+
+        def mat(*shape, dtype):
+            t = torch.empty(*shape, device=self.device, dtype=torch.float32)
+            t.normal_(0.0, 0.02, generator=g)
+            return t.to(dtype)
+
+        q_size, kv_size = c.num_heads * c.head_dim, c.num_kv_heads * c.head_dim
+        shapes = {"qkv": (3, c.hidden, q_size + 2 * kv_size), "o": (1, q_size, c.hidden),
+                  "gate_up": (2, c.hidden, 2 * c.intermediate), "down": (1, c.intermediate, c.hidden)}
+        dtype = self.embed.dtype
+        self.ptp_embedding = mat(num_embeddings, c.hidden, dtype=torch.float32)
+        self.ptp_top_k = top_k
+        self.adapters = [{name: (mat(shapes[name][0] * rank, shapes[name][1], dtype=dtype),
+                                 mat(shapes[name][2], rank, dtype=dtype)) for name in projections}
+                         for _ in range(c.num_layers)]
+        return self
+
+    def adapter_shards(self, layer: int, name: str) -> list[int]:
+        """Output widths of a projection's shards, in output order (q, k, v; gate, up)."""
+        c = self.config
+        q_size, kv_size = c.num_heads * c.head_dim, c.num_kv_heads * c.head_dim
+        return {"qkv": [q_size, kv_size, kv_size], "o": [c.hidden], "gate_up": [c.intermediate, c.intermediate],
+                "down": [c.hidden]}[name]
 
     def named(self) -> dict:
         """Tensors by name for the CPU oracle (lists per layer)."""

@@ -7,7 +7,7 @@ into it without an sm_100a GPU, raises ``NativeError``. There is no fallback.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_int32, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_int32, c_int64, c_size_t, c_void_p, pointer
 from pathlib import Path
 
 LIBRARY = Path(__file__).resolve().with_name("libplm_native.so")
@@ -36,7 +36,8 @@ class GemmEpilogue(ctypes.Structure):
                 ("num_slots", c_int64), ("max_pos", c_int32),
                 ("verify_logits", c_void_p), ("best_val", c_void_p), ("best_idx", c_void_p),
                 ("n_verify", c_int32), ("vocab", c_int32),
-                ("table", c_void_p), ("aux", c_int32), ("a0", c_int32)]
+                ("table", c_void_p), ("aux", c_int32), ("a0", c_int32),
+                ("corr", c_void_p), ("corr_from", c_int32), ("corr_ld", c_int32)]
 
 
 class GemmDesc(ctypes.Structure):
@@ -87,7 +88,7 @@ class AddRmsNormDesc(ctypes.Structure):
     _fields_ = [("dtype", c_int32), ("x", c_void_p), ("residual", c_void_p), ("normed", c_void_p),
                 ("weight", c_void_p), ("rows", c_int32), ("hidden", c_int32), ("eps", ctypes.c_float),
                 ("gather_row", c_int32), ("gathered", c_void_p), ("partials", c_void_p), ("n_partials", c_int32),
-                ("partial_stride", ctypes.c_int64)]
+                ("partial_stride", ctypes.c_int64), ("corr", c_void_p), ("corr_from", c_int32), ("corr_ld", c_int32)]
 
 
 class CommitDesc(ctypes.Structure):
@@ -111,11 +112,18 @@ class IcdfDesc(ctypes.Structure):
                 ("top_k", c_int32), ("tokens", c_void_p), ("ids_out", c_void_p), ("edges_out", c_void_p)]
 
 
+class PtpDesc(ctypes.Structure):
+    _fields_ = [("embedding", c_void_p), ("num_embeddings", c_int32), ("top_k", c_int32), ("rank", c_int32),
+                ("qkv_a", POINTER(c_void_p)), ("qkv_b", POINTER(c_void_p)), ("o_a", POINTER(c_void_p)),
+                ("o_b", POINTER(c_void_p)), ("gate_up_a", POINTER(c_void_p)), ("gate_up_b", POINTER(c_void_p)),
+                ("down_a", POINTER(c_void_p)), ("down_b", POINTER(c_void_p))]
+
+
 class WeightPtrs(ctypes.Structure):
     _fields_ = [("embed", c_void_p), ("lm_head", c_void_p), ("final_norm", c_void_p), ("aux_vocab", c_void_p),
                 ("mask_aux", c_void_p), ("cos_sin", c_void_p), ("qkv", POINTER(c_void_p)), ("o", POINTER(c_void_p)),
                 ("gate_up", POINTER(c_void_p)), ("down", POINTER(c_void_p)), ("input_norm", POINTER(c_void_p)),
-                ("post_norm", POINTER(c_void_p)), ("table", c_void_p)]
+                ("post_norm", POINTER(c_void_p)), ("table", c_void_p), ("ptp", POINTER(PtpDesc))]
 
 
 class RoundDesc(ctypes.Structure):
@@ -160,6 +168,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_destroy": [c_void_p],
     "plm_set_block_table": [c_void_p, POINTER(c_int32), c_int32],
     "plm_set_aux_stream": [c_void_p, c_void_p, c_int64, c_void_p],
+    "plm_set_aux_uniforms": [c_void_p, c_void_p, c_int64, c_void_p],
     "plm_load_prompt": [c_void_p, c_void_p, c_int64, c_void_p],
     "plm_set_stop": [c_void_p, c_int64, c_int64, c_int64, c_void_p],
     "plm_prefill": [c_void_p, c_void_p],
@@ -347,6 +356,11 @@ class Handle:
     def set_aux_stream(self, cells, stream=None) -> None:
         check(library().plm_set_aux_stream(self.handle, cells.data_ptr(), cells.numel(), stream_handle(stream)),
               "plm_set_aux_stream")
+
+    def set_aux_uniforms(self, u, stream=None) -> None:
+        """The PTP scheme's uniform stream (float32 device or pinned tensor)."""
+        check(library().plm_set_aux_uniforms(self.handle, u.data_ptr(), u.numel(), stream_handle(stream)),
+              "plm_set_aux_uniforms")
 
     def load_prompt(self, ids, stream=None) -> None:
         check(library().plm_load_prompt(self.handle, ids.data_ptr(), ids.numel(), stream_handle(stream)),

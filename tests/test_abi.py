@@ -30,17 +30,18 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} is declared but not exported"
     assert sorted(native.exported_symbols()) == declared, "ctypes signatures must cover exactly the header"
-    assert lib.plm_abi_version() == 6
+    assert lib.plm_abi_version() == 7
 
 
 STRUCTS = ["plm_gemm_epilogue", "plm_gemm_desc", "plm_bookkeeping", "plm_verify_desc", "plm_attention_desc",
            "plm_kv_append_desc", "plm_add_rmsnorm_desc", "plm_model_desc", "plm_weight_ptrs", "plm_round_desc",
-           "plm_state_ptrs", "plm_icdf_desc", "plm_commit_desc"]
+           "plm_state_ptrs", "plm_icdf_desc", "plm_commit_desc", "plm_ptp_desc"]
 MIRRORS = {"plm_gemm_epilogue": "GemmEpilogue", "plm_gemm_desc": "GemmDesc", "plm_bookkeeping": "Bookkeeping",
            "plm_verify_desc": "VerifyDesc", "plm_attention_desc": "AttentionDesc",
            "plm_kv_append_desc": "KvAppendDesc", "plm_add_rmsnorm_desc": "AddRmsNormDesc",
            "plm_model_desc": "ModelDesc", "plm_weight_ptrs": "WeightPtrs", "plm_round_desc": "RoundDesc",
-           "plm_state_ptrs": "StatePtrs", "plm_icdf_desc": "IcdfDesc", "plm_commit_desc": "CommitDesc"}
+           "plm_state_ptrs": "StatePtrs", "plm_icdf_desc": "IcdfDesc", "plm_commit_desc": "CommitDesc",
+           "plm_ptp_desc": "PtpDesc"}
 
 
 def test_ctypes_structs_match_c_layout(tmp_path):
