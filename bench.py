@@ -402,6 +402,78 @@ def run_reference(args) -> None:
     print(json.dumps(line))
 
 
+def write_reference_export(directory: Path, seed: int = 0) -> None:
+    """A synthetic PLM-1.3B export both engines load: seeded bf16 weights (lm_head padded to the embedding's rows,
+    as a vLLM Llama head expects) and a word-level tokenizer whose token i is the text "w<i>"."""
+    import torch
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config(SHAPE)
+    w = PLMWeights.random(cfg, seed=seed)
+    w.lm_head = torch.cat([w.lm_head, torch.zeros(cfg.vocab_rows - cfg.vocab, cfg.hidden, dtype=w.lm_head.dtype,
+                                                  device=w.lm_head.device)])
+    w.save_export(directory)
+    tok = Tokenizer(models.WordLevel(vocab={f"w{i}": i for i in range(cfg.vocab)}, unk_token="w0"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="w0", eos_token=f"w{cfg.vocab - 1}").save_pretrained(
+        directory)
+
+
+def run_reference_gpu(args) -> None:
+    """The reference's own round (baseline/_ref through vLLM, --mode default and fast) and this engine's, on the same
+    export, prompt and GPU: one request of a 256-token prompt and 512 new tokens each (after a warm-up request)."""
+    import tempfile
+
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "plm").exists():
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "the reference is not installed in baseline/_ref"}))
+        return
+    from plm.rounds import RoundConfig
+
+    seed, tokens = 0, TOKENS_E2E
+    with tempfile.TemporaryDirectory() as tmp:
+        export = Path(tmp) / "plm-1.3b"
+        write_reference_export(export)
+        results = {}
+        for mode in ("default", "fast"):
+            env = dict(os.environ, PYTHONPATH=str(ref))
+            proc = subprocess.run([sys.executable, str(ROOT / "plm-anon_b200" / "bench" / "reference_gpu.py"),
+                                   str(export), mode, str(seed), str(tokens)], capture_output=True, text=True, env=env,
+                                  timeout=1200)
+            lines = [line for line in proc.stdout.splitlines() if line.startswith("{")]
+            errors = [line for line in (proc.stderr + proc.stdout).splitlines()
+                      if ("Error" in line or "no tuned tile" in line) and "prime_rl" not in line]
+            results[mode] = json.loads(lines[-1]) if proc.returncode == 0 and lines else {
+                "failed": (errors or proc.stderr.strip().splitlines() or ["no output"])[-1][:400]}
+        decoder = RoundConfig(model=str(export), setting="posttrain", mode="fast", match="exact", k=7,
+                              dtype="bfloat16", max_model_len=2048).build(kv_cache_bytes=1 << 30, block_size=16)
+        ids = torch.randint(0, shape_config_vocab(), (256,), generator=torch.Generator().manual_seed(seed))
+        prompt = " ".join(f"w{int(i)}" for i in ids)
+        decoder.generate(prompt, 64, seed=0, stop_at_eos=False)
+        res = decoder.generate(prompt, tokens, seed=0, stop_at_eos=False)
+        decoder.check()
+        ours = {"steady_rounds": res.steady_rounds, "steady_ms": res.steady_ms,
+                "round_us": 1000.0 * res.steady_ms / max(res.steady_rounds, 1), "tokens": len(res.token_ids),
+                "seconds": res.seconds, "tokens_per_second": len(res.token_ids) / res.seconds}
+        decoder.close()
+    print(json.dumps({"impl": "reference-gpu", "unit": UNIT, "workload": "PLM-1.3B shape, k=7, exact match + Voronoi, "
+                      "256-token prompt, 512 new tokens, 16-token pages, one request after a warm-up request",
+                      "reference": results, "native": ours}))
+
+
+def shape_config_vocab() -> int:
+    from plm.model import shape_config
+
+    return shape_config(SHAPE).vocab
+
+
 # DRAM bytes (read + write) of the weight GEMMs of one round of the benchmark shape, from one ncu capture of each
 # GEMM shape at 56 rows: 24 x (qkv 25.47 + o 8.69 + gate_up 68.12 + down 34.64) MB + lm_head 209.7 MB. Used for the
 # separate-launch configuration.
@@ -529,7 +601,9 @@ def main() -> None:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--impl", default="native", choices=("native", "reference"))
+    parser.add_argument("--impl", default="native", choices=("native", "reference", "reference-gpu"),
+                        help="reference: the CPU round oracle (the reference has no CPU round path); reference-gpu: "
+                             "the reference's own vLLM round from baseline/_ref beside this engine's, on one GPU")
     parser.add_argument("--skip-cpu", action="store_true", help="omit the CPU oracle baseline")
     parser.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end requests (profiling runs)")
     parser.add_argument("--ctx", type=int, default=CTX, help="committed context of the timed rounds (tokens)")
@@ -542,6 +616,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu(args)
     else:
         run_native(args)
 
