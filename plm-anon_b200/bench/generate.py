@@ -39,8 +39,8 @@ def add_arguments(parser: argparse.ArgumentParser) -> None:
     parser.add_argument("--k", type=int, help="proposal length per round; default from --setting")
     parser.add_argument("--block-size", type=int, default=KV_BLOCK_SIZE, help="KV page size in tokens")
     parser.add_argument("--dtype", default="", choices=("", "bfloat16", "float16"),
-                        help="weights' dtype on the GPU; default: the export's own (the kernels take bfloat16, so a "
-                             "float16 export needs --dtype bfloat16 to convert it)")
+                        help="weights' dtype on the GPU; default: the export's own (the kernels run bfloat16 and "
+                             "float16; naming the other converts the weights)")
     parser.add_argument("--ar", action="store_true", help="autoregressive decoding: one Voronoi-decoded row per step")
     parser.add_argument("--ar-sampler", default="voronoi", choices=("voronoi", "icdf", "topk", "greedy"),
                         help="voronoi: the PLM's own decode rule on the seeded cells, token-identical to --match exact "

@@ -11,6 +11,8 @@
 //                                 or  (kv - offset >= own_start[r]  and  kv <= offset + r)),
 // which is RoundMaskView for a round (depth / own_start from round_layout) and plain causal attention for a
 // prefill chunk (depth[r] = r).
+#include <type_traits>
+
 #include "attention.h"
 #include "common.cuh"
 #include "runtime.h"
@@ -34,12 +36,22 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(smem_u32(p)));
 }
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// m16n8k16 tensor-core product with fp32 accumulation, operands in the model dtype T (bf16 or f16).
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
 }
 // 2^x by the special-function unit (relative error ~2^-22; -inf gives +0): the softmax's exponentials.
 __device__ __forceinline__ float ex2(float x) {
@@ -47,9 +59,11 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+// Two floats rounded to the model dtype, packed low element first.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const T l = from_f32<T>(lo), h = from_f32<T>(hi);
+  return uint32_t(*reinterpret_cast<const uint16_t*>(&l)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&h)) << 16);
 }
 
 // Byte offset of (row, 16-byte chunk) in a swizzled tile with HD/8 chunks per row.
@@ -58,7 +72,7 @@ __device__ __forceinline__ int swz(int row, int chunk) {
   return row * (HD * 2) + ((chunk ^ (row & 7)) << 4);
 }
 
-template <int HD>
+template <int HD, typename T>
 __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const AttnArgs a) {
   constexpr int CH = HD / 8;
   constexpr int TILE_BYTES = kKeysPerTile * HD * 2;
@@ -206,8 +220,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
         const int chunk = kk * 2 + (mi & 1);
         uint32_t b[4];
         ldmatrix_x4(b, kb + swz<HD>(row, chunk));
-        mma_bf16(s[2 * jj], qf[kk], b[0], b[1]);
-        mma_bf16(s[2 * jj + 1], qf[kk], b[2], b[3]);
+        mma_16816<T>(s[2 * jj], qf[kk], b[0], b[1]);
+        mma_16816<T>(s[2 * jj + 1], qf[kk], b[2], b[3]);
       }
     }
     // scale + mask
@@ -267,10 +281,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
 #pragma unroll
     for (int kk = 0; kk < kKeysPerTile / 16; ++kk) {
       uint32_t pa[4];
-      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
       for (int nn = 0; nn < HD / 16; ++nn) {
         const int mi = lane >> 3, rr = lane & 7;
@@ -278,8 +292,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
         const int chunk = nn * 2 + (mi >> 1);
         uint32_t b[4];
         ldmatrix_x4_trans(b, vb + swz<HD>(row, chunk));
-        mma_bf16(o[2 * nn], pa, b[0], b[1]);
-        mma_bf16(o[2 * nn + 1], pa, b[2], b[3]);
+        mma_16816<T>(o[2 * nn], pa, b[0], b[1]);
+        mma_16816<T>(o[2 * nn + 1], pa, b[2], b[3]);
       }
     }
   }
@@ -308,9 +322,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     for (int j = 0; j < HD / 8; ++j) {
       const int col = head * HD + j * 8 + 2 * tq;
       if (r0 < a.rows)
-        *reinterpret_cast<__nv_bfloat162*>(out_at(r0, col)) = __floats2bfloat162_rn(o[j][0] * inv0, o[j][1] * inv0);
+        *reinterpret_cast<uint32_t*>(out_at(r0, col)) = pack2<T>(o[j][0] * inv0, o[j][1] * inv0);
       if (r1 < a.rows)
-        *reinterpret_cast<__nv_bfloat162*>(out_at(r1, col)) = __floats2bfloat162_rn(o[j][2] * inv1, o[j][3] * inv1);
+        *reinterpret_cast<uint32_t*>(out_at(r1, col)) = pack2<T>(o[j][2] * inv1, o[j][3] * inv1);
     }
     return;
   }
@@ -396,18 +410,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
       }
       const int grow = qt * kQRowsPerCta + row_begin + lr;
       const float inv = wts[lr * (S + 1) + S];
-      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out_at(grow, head * HD + c));
-      dst[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-      dst[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(out_at(grow, head * HD + c));
+      dst[0] = pack2<T>(acc.x * inv, acc.y * inv);
+      dst[1] = pack2<T>(acc.z * inv, acc.w * inv);
     }
   }
   cluster_sync();
 }
 
-template <int HD>
+template <int HD, typename T>
 int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool pdl) {
   constexpr int SMEM = 2 * kStages * kKeysPerTile * HD * 2 + kMaxPageSlice * 4;
-  auto kernel = round_attention_kernel<HD>;
+  auto kernel = round_attention_kernel<HD, T>;
   const int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(attention smem)");
   if (st != PLM_OK) return st;
   return check_cuda(launch_ex(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl,
@@ -441,8 +455,11 @@ int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
   if (a.splits > 8 || (a.splits & (a.splits - 1)) != 0)
     return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits (a power of two <= 8)", a.splits);
   a.err = ctx->err;
-  return a.head_dim == 128 ? launch_attention<128>(a, q_tiles, stream, pdl)
-                           : launch_attention<64>(a, q_tiles, stream, pdl);
+  if (a.dtype == PLM_F16)
+    return a.head_dim == 128 ? launch_attention<128, __half>(a, q_tiles, stream, pdl)
+                             : launch_attention<64, __half>(a, q_tiles, stream, pdl);
+  return a.head_dim == 128 ? launch_attention<128, __nv_bfloat16>(a, q_tiles, stream, pdl)
+                           : launch_attention<64, __nv_bfloat16>(a, q_tiles, stream, pdl);
 }
 
 }  // namespace plm
@@ -451,8 +468,9 @@ using namespace plm;
 
 extern "C" int plm_attention(plm_ctx* ctx, const plm_attention_desc* d, void* stream) {
   if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_attention: null argument");
-  if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_attention: only bf16 is built");
+  if (d->dtype != PLM_BF16 && d->dtype != PLM_F16) return fail(PLM_ERR_INVALID, "plm_attention: dtype %d", d->dtype);
   AttnArgs a = {};
+  a.dtype = d->dtype;
   a.q = d->q;
   a.k_cache = d->k_cache;
   a.v_cache = d->v_cache;

@@ -9,6 +9,7 @@
 namespace plm {
 
 struct AttnArgs {
+  int dtype;                   // PLM_BF16 or PLM_F16: q, the caches and the output
   const void* q;               // [rows][num_heads][head_dim] (after RoPE)
   const void* k_cache;         // [num_pages][num_kv_heads][page_size][head_dim]
   const void* v_cache;

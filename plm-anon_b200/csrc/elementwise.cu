@@ -312,6 +312,9 @@ __global__ void kv_append_kernel(const KvAppendArgs a) {
 int prologue_launch(const PrologueArgs& a, int rows, cudaStream_t stream, bool pdl) {
   if (a.hidden > kRowThreads * kVec * kMaxVecs || a.hidden % kVec != 0)
     return fail(PLM_ERR_UNSUPPORTED, "prologue: hidden %d (a multiple of 8, at most 4096)", a.hidden);
+  if (a.dtype == PLM_F16)
+    return check_cuda(launch(embed_norm_kernel<__half>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
+                      "embed_norm_kernel");
   return check_cuda(launch(embed_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
                     "embed_norm_kernel");
 }
@@ -319,6 +322,9 @@ int prologue_launch(const PrologueArgs& a, int rows, cudaStream_t stream, bool p
 int add_norm_launch(const AddNormArgs& a, int rows, cudaStream_t stream, bool pdl) {
   if (a.hidden > kRowThreads * kVec * kMaxVecs || a.hidden % kVec != 0)
     return fail(PLM_ERR_UNSUPPORTED, "add_norm: hidden %d (a multiple of 8, at most 4096)", a.hidden);
+  if (a.dtype == PLM_F16)
+    return check_cuda(launch(add_norm_kernel<__half>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
+                      "add_norm_kernel");
   return check_cuda(launch(add_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
                     "add_norm_kernel");
 }
@@ -327,6 +333,9 @@ int kv_append_launch(const KvAppendArgs& a, cudaStream_t stream, bool pdl) {
   if (a.head_dim % 8 != 0) return fail(PLM_ERR_UNSUPPORTED, "kv_append: head_dim %d", a.head_dim);
   const int warps = a.rows * a.num_kv_heads;
   const int blocks = (warps * 32 + 255) / 256;
+  if (a.dtype == PLM_F16)
+    return check_cuda(launch(kv_append_kernel<__half>, dim3(blocks), dim3(256), 0, stream, pdl, a),
+                      "kv_append_kernel");
   return check_cuda(launch(kv_append_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream, pdl, a),
                     "kv_append_kernel");
 }
@@ -337,18 +346,18 @@ using namespace plm;
 
 extern "C" int plm_kv_append(plm_ctx* ctx, const plm_kv_append_desc* d, void* stream) {
   if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_kv_append: null argument");
-  if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_kv_append: only bf16 is built");
+  if (d->dtype != PLM_BF16 && d->dtype != PLM_F16) return fail(PLM_ERR_INVALID, "plm_kv_append: dtype %d", d->dtype);
   if (!d->k || !d->v || !d->k_cache || !d->v_cache || !d->block_table || !d->offset || d->rows < 1)
     return fail(PLM_ERR_INVALID, "plm_kv_append: null operand or no rows");
-  KvAppendArgs a = {d->k,         d->v,         d->k_cache,   d->v_cache,  d->block_table, d->max_pages,
-                    d->num_pages, d->page_size, d->offset,    d->rows,     d->num_kv_heads, d->head_dim,
-                    ctx->err};
+  KvAppendArgs a = {d->dtype,     d->k,         d->v,         d->k_cache,  d->v_cache,  d->block_table,
+                    d->max_pages, d->num_pages, d->page_size, d->offset,   d->rows,     d->num_kv_heads,
+                    d->head_dim,  ctx->err};
   return kv_append_launch(a, static_cast<cudaStream_t>(stream), true);
 }
 
 extern "C" int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* d, void* stream) {
   if (ctx == nullptr || d == nullptr) return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null argument");
-  if (d->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_add_rmsnorm: only bf16 is built");
+  if (d->dtype != PLM_BF16 && d->dtype != PLM_F16) return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: dtype %d", d->dtype);
   if (!d->residual || !d->normed || !d->weight || d->rows < 1 || d->hidden < 1)
     return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null operand");
   if (d->partials == nullptr && d->x == nullptr) return fail(PLM_ERR_INVALID, "plm_add_rmsnorm: null operand");
@@ -365,5 +374,6 @@ extern "C" int plm_add_rmsnorm(plm_ctx* ctx, const plm_add_rmsnorm_desc* d, void
   a.corr = d->corr;
   a.corr_from = d->corr_from;
   a.corr_ld = d->corr_ld;
+  a.dtype = d->dtype;
   return add_norm_launch(a, d->rows, static_cast<cudaStream_t>(stream), true);
 }

@@ -9,6 +9,7 @@ namespace plm {
 enum PrologueMode : int { kPrologueSteady = 0, kPrologueRound0 = 1, kProloguePrefill = 2 };
 
 struct PrologueArgs {
+  int dtype;                   // PLM_BF16 or PLM_F16: the model's storage dtype
   int mode;
   int k;
   int vocab, aux, num_aux_tokens, hidden;
@@ -61,9 +62,11 @@ struct AddNormArgs {
   const float* corr = nullptr;      // non-null: x[r] = round(x[r] + corr[r - corr_from]) for rows r >= corr_from
   int corr_from = 0;
   int corr_ld = 0;
+  int dtype = 0;                    // PLM_BF16 or PLM_F16
 };
 
 struct KvAppendArgs {
+  int dtype;      // PLM_BF16 or PLM_F16
   const void* k;  // [rows][num_kv_heads][head_dim]
   const void* v;
   void* k_cache;  // [num_pages][num_kv_heads][page_size][head_dim]

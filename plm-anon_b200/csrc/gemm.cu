@@ -118,7 +118,7 @@ int launch_dtype(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* mw, co
 }
 
 int validate(const plm_gemm_desc& d) {
-  if (d.dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: only bf16 is built");
+  if (d.dtype != PLM_BF16 && d.dtype != PLM_F16) return fail(PLM_ERR_INVALID, "plm_gemm: dtype %d", d.dtype);
   if (d.w == nullptr || d.x == nullptr) return fail(PLM_ERR_INVALID, "plm_gemm: null operand");
   if (d.k <= 0 || d.k % 64 != 0) return fail(PLM_ERR_INVALID, "plm_gemm: k=%d must be a positive multiple of 64", d.k);
   if (d.rows < 1 || d.rows > 256 || d.x_rows < d.rows)
@@ -214,6 +214,7 @@ int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, 
                 cudaStream_t stream, bool pdl) {
   int st = validate(d);
   if (st != PLM_OK) return st;
+  if (d.dtype == PLM_F16) return launch_dtype<__half>(ctx, d, map_w, map_x, stream, pdl);
   return launch_dtype<__nv_bfloat16>(ctx, d, map_w, map_x, stream, pdl);
 }
 

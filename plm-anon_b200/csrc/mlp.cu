@@ -74,7 +74,7 @@ __host__ __device__ constexpr int block_unit(int kind, int tile, int split) {
   return (kind << 28) | (tile << 12) | split;
 }
 
-template <int NTOK>
+template <typename T, int NTOK>
 __device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int et, float* red, volatile int* abort_flag);
 
 template <typename T, int NTOK>
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_block_kernel(const BlockPa
       const int code = p.sched[u];
       const int kind = (code >> 28) & 3, tile = (code >> 12) & 0xffff, split = code & 0xfff;
       if (kind == kUnitNorm) {
-        if (tile < rows) block_norm_row<NTOK>(p, tile, et, reinterpret_cast<float*>(gu), abort_flag);
+        if (tile < rows) block_norm_row<T, NTOK>(p, tile, et, reinterpret_cast<float*>(gu), abort_flag);
         continue;
       }
       const int buf = n & 1;
@@ -419,10 +419,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_block_kernel(const BlockPa
 // elementwise.cu, vLLM fused_add_rms_norm): x = the o partials summed in split order and rounded to bf16,
 // v = x + residual in fp32, residual <- bf16(v), normed = bf16(bf16(v * rstd) * w), written as row tiles for the
 // gate_up units. Run by the 256 epilogue threads once every o unit of the grid has signalled.
-template <int NTOK>
+template <typename T, int NTOK>
 __device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int et, float* red,
                                                volatile int* abort_flag) {
-  using T = __nv_bfloat16;
   constexpr int kThreads = kMlpEpiWarps * 32;
   if (et == 0) {
     const int target = p.o_units;
@@ -626,8 +625,23 @@ int launch_block(const MlpSchedule& s, const BlockParams& p, cudaStream_t stream
 
 }  // namespace
 
+template <typename T>
+int launch_block_rows(const MlpSchedule& s, const BlockParams& p, cudaStream_t stream, bool pdl) {
+  switch (gemm_token_tile(p.rows)) {  // the row tiles' height
+    case 16: return launch_block<T, 16>(s, p, stream, pdl);
+    case 32: return launch_block<T, 32>(s, p, stream, pdl);
+    case 48: return launch_block<T, 48>(s, p, stream, pdl);
+    case 64: return launch_block<T, 64>(s, p, stream, pdl);
+    case 80: return launch_block<T, 80>(s, p, stream, pdl);
+    case 96: return launch_block<T, 96>(s, p, stream, pdl);
+    case 112: return launch_block<T, 112>(s, p, stream, pdl);
+    case 128: return launch_block<T, 128>(s, p, stream, pdl);
+  }
+  return fail(PLM_ERR_UNSUPPORTED, "layer block: %d rows", p.rows);
+}
+
 int mlp_block_launch(const MlpSchedule& s, BlockParams p, int dtype, cudaStream_t stream, bool pdl) {
-  if (dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "layer block: only bf16 is built");
+  if (dtype != PLM_BF16 && dtype != PLM_F16) return fail(PLM_ERR_INVALID, "layer block: dtype %d", dtype);
   if (s.sched == nullptr || s.grid < 1) return fail(PLM_ERR_INVALID, "layer block: no schedule");
   if (p.rows < 1 || p.rows > kMlpMaxRows) return fail(PLM_ERR_UNSUPPORTED, "layer block: %d rows", p.rows);
   if ((p.hidden + 127) / 128 != s.down_tiles || p.intermediate / 64 != s.gate_tiles)
@@ -640,17 +654,8 @@ int mlp_block_launch(const MlpSchedule& s, BlockParams p, int dtype, cudaStream_
   p.o_splits = s.o_splits;
   p.down_splits = s.down_splits;
   p.o_units = s.o_tiles * s.o_splits;
-  switch (gemm_token_tile(p.rows)) {  // the row tiles' height
-    case 16: return launch_block<__nv_bfloat16, 16>(s, p, stream, pdl);
-    case 32: return launch_block<__nv_bfloat16, 32>(s, p, stream, pdl);
-    case 48: return launch_block<__nv_bfloat16, 48>(s, p, stream, pdl);
-    case 64: return launch_block<__nv_bfloat16, 64>(s, p, stream, pdl);
-    case 80: return launch_block<__nv_bfloat16, 80>(s, p, stream, pdl);
-    case 96: return launch_block<__nv_bfloat16, 96>(s, p, stream, pdl);
-    case 112: return launch_block<__nv_bfloat16, 112>(s, p, stream, pdl);
-    case 128: return launch_block<__nv_bfloat16, 128>(s, p, stream, pdl);
-  }
-  return fail(PLM_ERR_UNSUPPORTED, "layer block: %d rows", p.rows);
+  return dtype == PLM_F16 ? launch_block_rows<__half>(s, p, stream, pdl)
+                          : launch_block_rows<__nv_bfloat16>(s, p, stream, pdl);
 }
 
 }  // namespace plm

@@ -240,6 +240,7 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
   const int hidden = m.hidden, hd = m.head_dim;
   const int q_size = m.num_heads * hd, kv_size = m.num_kv_heads * hd;
   PrologueArgs p = {};
+  p.dtype = m.dtype;
   p.mode = mode;
   p.k = h->rd.k;
   p.vocab = m.vocab;
@@ -313,6 +314,7 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     if (st != PLM_OK) return st;
 
     AttnArgs a = {};
+    a.dtype = m.dtype;
     a.q = h->q;
     a.k_cache = kv_plane(h, l, 0);
     a.v_cache = kv_plane(h, l, 1);
@@ -360,6 +362,7 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
       if (st != PLM_OK) return st;
       AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
                         h->partials, s_o, slice};
+      n1.dtype = m.dtype;
       if (ld > 0) {
         n1.corr = h->lora_corr;
         n1.corr_from = gated_from;
@@ -390,6 +393,7 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
     AddNormArgs n2 = {nullptr,  h->residual,           h->x_norm, last ? h->final_norm : h->in_norm[l + 1],
                       hidden,   m.rms_eps,             last ? gather_row : -1, last ? h->gathered : nullptr,
                       h->partials, s_d, slice};
+    n2.dtype = m.dtype;
     if (down_ld > 0) {
       n2.corr = h->lora_corr;
       n2.corr_from = gated_from;
@@ -534,7 +538,7 @@ void round_layout(const std::vector<int>& blocks, std::vector<int64_t>& relpos, 
 }
 
 int validate_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_round_desc* r) {
-  if (m->dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "plm_create: only bf16 models are built");
+  if (m->dtype != PLM_BF16 && m->dtype != PLM_F16) return fail(PLM_ERR_INVALID, "plm_create: dtype %d", m->dtype);
   if (m->num_layers < 1 || m->hidden % 64 != 0 || m->intermediate % 64 != 0 || m->head_dim % 64 != 0)
     return fail(PLM_ERR_INVALID, "plm_create: hidden / intermediate / head_dim must be multiples of 64");
   if ((m->num_heads * m->head_dim) % 64 != 0 || m->num_heads % m->num_kv_heads != 0)

@@ -1072,7 +1072,15 @@ int launch_verify(const VerifyArgs& a, int n_rows, cudaStream_t stream, bool pdl
 }  // namespace
 
 int verify_launch(const VerifyArgs& a, int dtype, int n_rows, cudaStream_t stream, bool pdl) {
-  if (dtype != PLM_BF16) return fail(PLM_ERR_UNSUPPORTED, "verify decode: only bf16 tables are built");
+  if (dtype != PLM_BF16 && dtype != PLM_F16) return fail(PLM_ERR_INVALID, "verify decode: dtype %d", dtype);
+  if (dtype == PLM_F16) {
+    switch (a.shortlist) {
+      case 1: return launch_verify<__half, 1>(a, n_rows, stream, pdl);
+      case 2: return launch_verify<__half, 2>(a, n_rows, stream, pdl);
+      case 4: return launch_verify<__half, 4>(a, n_rows, stream, pdl);
+      case 8: return launch_verify<__half, 8>(a, n_rows, stream, pdl);
+    }
+  }
   switch (a.shortlist) {
     case 1: return launch_verify<__nv_bfloat16, 1>(a, n_rows, stream, pdl);
     case 2: return launch_verify<__nv_bfloat16, 2>(a, n_rows, stream, pdl);

@@ -60,11 +60,12 @@ class RoundDecoder:
         self.weights, self.config = weights, weights.config
         c = self.config
         stored = {t.dtype for t in [weights.embed, weights.lm_head, weights.aux_vocab, *weights.qkv, *weights.o,
-                                     *weights.gate_up, *weights.down]}
-        if stored != {torch.bfloat16}:
+                                     *weights.gate_up, *weights.down, *weights.input_norm, *weights.post_norm]}
+        if len(stored) != 1 or not stored <= {torch.bfloat16, torch.float16}:
             raise native.NativeError(f"RoundDecoder: weights stored as {sorted(map(str, stored))}; the sm_100a kernels "
-                                     "are built for bfloat16 only (convert explicitly, e.g. RoundConfig(dtype="
-                                     "'bfloat16') or PLMWeights.from_export(..., dtype='bfloat16'))")
+                                     "take one model dtype, bfloat16 or float16 (convert explicitly, e.g. "
+                                     "RoundConfig(dtype='bfloat16') or PLMWeights.from_export(..., dtype=...))")
+        self.dtype = stored.pop()
         self.k, self.width = k, k + k * k
         self.block_size = block_size
         self.accept_rule, self.threshold = accept_rule, threshold
@@ -81,7 +82,7 @@ class RoundDecoder:
         self._layer_arrays = [(native.c_void_p * c.num_layers)(*[t.data_ptr() for t in getattr(weights, name)])
                               for name in ("qkv", "o", "gate_up", "down", "input_norm", "post_norm")]
         model = native.ModelDesc(
-            dtype=native.PLM_BF16, num_layers=c.num_layers, hidden=c.hidden, num_heads=c.num_heads,
+            dtype=native.PLM_F16 if self.dtype == torch.float16 else native.PLM_BF16, num_layers=c.num_layers, hidden=c.hidden, num_heads=c.num_heads,
             num_kv_heads=c.num_kv_heads, head_dim=c.head_dim, intermediate=c.intermediate, vocab=c.vocab,
             aux_vocab=c.aux_vocab, num_aux_tokens=c.num_aux_tokens, rms_eps=c.rms_eps,
             max_pos=self.cos_sin.shape[0], top_m=c.top_m, shortlist=min(c.shortlist, c.top_m), rounds=c.rounds,
@@ -116,10 +117,10 @@ class RoundDecoder:
         self.sequence_step = native.device_view(st.sequence_step, (1,), torch.int64)
         self.aux_buf = native.device_view(st.aux_buf, (st.aux_len,), torch.int64)
         self.verify_logits = native.device_view(st.verify_logits, (k, c.vocab), torch.float32)
-        self.hidden_normed = native.device_view(st.hidden_normed, (st.row_capacity, c.hidden), torch.bfloat16)
+        self.hidden_normed = native.device_view(st.hidden_normed, (st.row_capacity, c.hidden), self.dtype)
         self.kv_cache = native.device_view(
-            st.kv_cache, (c.num_layers, 2, self.num_pages, c.num_kv_heads, block_size, c.head_dim), torch.bfloat16)
-        self.table = None if self.ptp else native.device_view(st.table, (c.vocab, c.aux_vocab), torch.bfloat16)
+            st.kv_cache, (c.num_layers, 2, self.num_pages, c.num_kv_heads, block_size, c.head_dim), self.dtype)
+        self.table = None if self.ptp else native.device_view(st.table, (c.vocab, c.aux_vocab), self.dtype)
         self.stop_block = native.device_view(st.stop, (4,), torch.int64)
         # [base, done] of the newest finished round, copied by every replay into pinned host memory
         self.poll_host = torch.zeros(2, dtype=torch.long).pin_memory()

@@ -326,7 +326,8 @@ def device_view(address: int, shape: tuple, dtype):
     """torch tensor aliasing ``shape`` elements of ``dtype`` at a device address (no copy, not owned)."""
     import torch
 
-    typestr = {torch.int64: "<i8", torch.int32: "<i4", torch.float32: "<f4", torch.bfloat16: "<V2"}[dtype]
+    typestr = {torch.int64: "<i8", torch.int32: "<i4", torch.float32: "<f4", torch.float16: "<f2",
+               torch.bfloat16: "<V2"}[dtype]
     if dtype == torch.bfloat16:
         raw = torch.as_tensor(_DeviceArray(address, shape, "<i2"), device="cuda")
         return raw.view(torch.bfloat16)

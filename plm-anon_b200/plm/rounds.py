@@ -50,8 +50,9 @@ def scheme_kind(scheme: str) -> str | None:
 @dataclass
 class RoundConfig:
     """``model`` is an export directory or ``synthetic:<shape>[:seed=<n>]`` (e.g. ``synthetic:plm-1.3b``).
-    ``dtype`` None keeps the export's own ``torch_dtype`` (bfloat16 for synthetic models); a dtype the native
-    kernels are not built for makes ``build`` raise ``NativeError``. Naming one converts the weights explicitly."""
+    ``dtype`` None keeps the export's own ``torch_dtype`` (bfloat16 for synthetic models); naming one converts the
+    weights explicitly. The kernels run bfloat16 and float16 (the reference's default, plm/rounds.py:50); any other
+    dtype makes ``build`` raise ``NativeError``."""
     model: str
     setting: str = "posttrain"
     mode: str = "fast"
@@ -107,9 +108,8 @@ class RoundConfig:
         from .decoder import RoundDecoder
         from .native import NativeError
 
-        if self.dtype != "bfloat16":
-            raise NativeError(f"dtype {self.dtype}: the native kernels are built for bfloat16; pass "
-                              "RoundConfig(dtype='bfloat16') to convert the weights")
+        if self.dtype not in ("bfloat16", "float16"):
+            raise NativeError(f"dtype {self.dtype}: the native kernels are built for bfloat16 and float16")
         rule, threshold = self.accept
         tokenizer = None
         if not self.model.startswith("synthetic:"):

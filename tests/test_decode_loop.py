@@ -78,10 +78,11 @@ def test_rounds_in_flight_match_one_at_a_time(k, num_tokens):
     decoder.close()
 
 
-def test_float16_export_is_never_reinterpreted(tmp_path):
-    """A float16 export (the reference's default dtype) fails loudly: build() raises NativeError, and so does a
-    RoundDecoder handed float16 tensors. Converting it explicitly (RoundConfig(dtype='bfloat16')) decodes the same
-    tokens as a model built from the same values rounded to bfloat16."""
+def test_float16_export_runs_in_float16(tmp_path):
+    """A float16 export (the reference's default dtype, plm/rounds.py:50) builds and decodes in float16: the handle's
+    model dtype is float16, and nothing is reinterpreted. Weights of mixed dtypes fail loudly. Converting the export
+    explicitly (RoundConfig(dtype='bfloat16')) decodes the same tokens as a model built from the same values
+    rounded to bfloat16."""
     from plm.decoder import RoundDecoder
     from plm.model import PLMWeights, shape_config
     from plm.native import NativeError
@@ -91,10 +92,18 @@ def test_float16_export_is_never_reinterpreted(tmp_path):
     weights = PLMWeights.random(cfg, seed=2)
     export = weights.save_export(tmp_path / "fp16")
     assert RoundConfig(model=str(export)).dtype == "float16"
+    native16 = RoundConfig(model=str(export), max_model_len=1024).build(kv_cache_bytes=64 << 20, block_size=16)
+    assert native16.dtype == torch.float16 and native16.handle.model.dtype == 1  # PLM_F16
+    prompt = list(range(10, 50))
+    t16 = native16.generate(prompt, 24, seed=1, stop_at_eos=False).token_ids
+    native16.check()
+    assert len(t16) == 24
+    native16.close()
+
+    mixed = PLMWeights.from_export(export)
+    mixed.o = [t.bfloat16() for t in mixed.o]
     with pytest.raises(NativeError):
-        RoundConfig(model=str(export)).build(kv_cache_bytes=64 << 20, block_size=16)
-    with pytest.raises(NativeError):
-        RoundDecoder(PLMWeights.from_export(export), 7, block_size=16, kv_cache_bytes=64 << 20)
+        RoundDecoder(mixed, 7, block_size=16, kv_cache_bytes=64 << 20)
 
     converted = RoundConfig(model=str(export), dtype="bfloat16", max_model_len=1024).build(kv_cache_bytes=64 << 20,
                                                                                           block_size=16)
@@ -104,7 +113,6 @@ def test_float16_export_is_never_reinterpreted(tmp_path):
     for name in ("embed", "lm_head", "final_norm", "aux_vocab", "mask_aux"):
         setattr(direct, name, getattr(direct, name).bfloat16())
     same = RoundDecoder(direct, 7, block_size=16, kv_cache_bytes=64 << 20, max_model_len=1024)
-    prompt = list(range(10, 50))
     a = converted.generate(prompt, 24, seed=1, stop_at_eos=False).token_ids
     b = same.generate(prompt, 24, seed=1, stop_at_eos=False).token_ids
     assert a == b and len(a) == 24

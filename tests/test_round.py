@@ -62,14 +62,14 @@ def _pair(shape: str, k: int, page: int, seed: int, rule="nucleus", threshold=No
                                 cfg.intermediate, cfg.vocab, cfg.aux_vocab, cfg.num_aux_tokens, cfg.rms_eps,
                                 cfg.rope_theta, decoder.cos_sin.shape[0])
     named = {key: ([t.cpu() for t in v] if isinstance(v, list) else v.cpu()) for key, v in weights.named().items()}
-    oracle_model = omodel.OracleModel(shape_o, named, "bfloat16", page, num_pages, table, cos_sin=decoder.cos_sin.cpu())
+    oracle_model = omodel.OracleModel(shape_o, named, cfg.dtype, page, num_pages, table, cos_sin=decoder.cos_sin.cpu())
     decoder._fill_aux(seed)
     aux = decoder.aux_buf.cpu().numpy().copy()
     table_np = decoder.table.float().cpu().numpy()
     oracle = omodel.RoundOracle(oracle_model, table_np, k, rule, threshold,
                                 ov.VoronoiConfig(cfg.top_m, cfg.shortlist, cfg.rounds, cfg.sweeps),
                                 capacity=decoder.out.numel(), aux_stream=aux)
-    oracle.sensitivity_model = omodel.OracleModel(shape_o, named, "bfloat16", page, num_pages, table,
+    oracle.sensitivity_model = omodel.OracleModel(shape_o, named, cfg.dtype, page, num_pages, table,
                                                   cos_sin=decoder.cos_sin.cpu(), accumulate="float64")
     return decoder, oracle, cfg
 
@@ -103,6 +103,8 @@ def _close(name, gpu, ref, report, rel=0.0, floor=0.0):
     ("plm-80m", 6, 16, "nucleus", None, {"num_layers": 2}),
     ("plm-1.3b", 7, 16, "nucleus", None, {}),
     ("plm-3b", 7, 16, "nucleus", 0.94, {"num_layers": 2}),  # the 3B width, relaxed posttrain
+    ("plm-tiny", 7, 16, "nucleus", None, {"dtype": "float16"}),  # the reference's dtype (plm/rounds.py:50)
+    ("plm-80m", 6, 16, "floor", 2e-3, {"num_layers": 2, "dtype": "float16", "separate_mlp": True}),
     ("plm-tiny", 1, 16, "nucleus", None, {}),  # k = 1: the AR-Voronoi comparator (plm/voronoi_ar.py)
     ("plm-80m", 7, 16, "nucleus", None, {"num_layers": 2, "separate_mlp": True}),  # gate_up and down as two launches
     # a 200-row prefill runs the separate launches (wider than the layer block's 128 rows), then the rounds run the
@@ -165,7 +167,7 @@ def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides)
     assert record == oracle.state.round_sequence
     out_dir = os.environ.get("PLM_PARITY_REPORT")
     if out_dir:
-        tag = f"_p{P}" if P != 64 else ""
+        tag = (f"_p{P}" if P != 64 else "") + ("_f16" if cfg.dtype == "float16" else "")
         with open(os.path.join(out_dir, f"parity_{shape}_k{k}_{rule}{tag}.json"), "w") as f:
             json.dump({key: max(v) for key, v in report.items()}, f)
 
