@@ -126,35 +126,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   const __nv_bfloat16* sk = reinterpret_cast<const __nv_bfloat16*>(a.scratch_k);
   const __nv_bfloat16* sv = reinterpret_cast<const __nv_bfloat16*>(a.scratch_v);
   const size_t scratch_off = size_t(group) * HD + size_t(my_chunk) * 8;
-  auto issue = [&](int t, int buf) {  // tile t (absolute) into ring slot buf; one commit group per call
+  // Tile t (absolute) into ring slot buf; one commit group per call. A tile wholly inside the context takes the
+  // branch-free path (every key through the block table); only the tiles holding the forward's own keys test each
+  // key against the offset.
+  auto issue = [&](int t, int buf) {
     const int64_t kv0 = int64_t(t) * kKeysPerTile + my_row0;
+    const bool context_tile = sk == nullptr || int64_t(t + 1) * kKeysPerTile <= offset;
     int pg[ITER];
 #pragma unroll
     for (int u = 0; u < ITER; ++u) {
       const int64_t kv = kv0 + u * RSTEP;
       const int64_t lp = kv >> a.page_shift;
-      pg[u] = kv >= seq_len                  ? -2
-              : (sk != nullptr && kv >= offset) ? -3
-              : staged_pages                   ? pages[lp - lp0]
-                                               : (lp < a.max_pages ? a.block_table[lp] : -1);
+      pg[u] = kv >= seq_len ? -2 : staged_pages ? pages[lp - lp0] : (lp < a.max_pages ? a.block_table[lp] : -1);
     }
     bool bad = false;
+    if (context_tile) {
 #pragma unroll
-    for (int u = 0; u < ITER; ++u) {
-      const int row = my_row0 + u * RSTEP;
-      const int64_t kv = kv0 + u * RSTEP;
-      if (pg[u] == -3) {
-        const size_t src = size_t(kv - offset) * size_t(a.num_kv_heads) * HD + scratch_off;
-        cp_async_16(kbuf(buf) + swz<HD>(row, my_chunk), sk + src, true);
-        cp_async_16(vbuf(buf) + swz<HD>(row, my_chunk), sv + src, true);
-        continue;
+      for (int u = 0; u < ITER; ++u) {
+        const int row = my_row0 + u * RSTEP;
+        const bool valid = pg[u] >= 0 && pg[u] < a.num_pages;
+        bad |= pg[u] != -2 && !valid;
+        const size_t src =
+            valid ? size_t(pg[u]) * page_stride + head_off + size_t((kv0 + u * RSTEP) & (a.page_size - 1)) * HD : 0;
+        cp_async_16(kbuf(buf) + swz<HD>(row, my_chunk), kc + src, valid);
+        cp_async_16(vbuf(buf) + swz<HD>(row, my_chunk), vc + src, valid);
       }
-      const bool valid = pg[u] >= 0 && pg[u] < a.num_pages;
-      bad |= pg[u] != -2 && !valid;
-      const size_t src =
-          valid ? size_t(pg[u]) * page_stride + head_off + size_t(kv & (a.page_size - 1)) * HD : 0;
-      cp_async_16(kbuf(buf) + swz<HD>(row, my_chunk), kc + src, valid);
-      cp_async_16(vbuf(buf) + swz<HD>(row, my_chunk), vc + src, valid);
+    } else {
+#pragma unroll
+      for (int u = 0; u < ITER; ++u) {
+        const int row = my_row0 + u * RSTEP;
+        const int64_t kv = kv0 + u * RSTEP;
+        const bool own = kv >= offset && kv < seq_len;
+        const bool valid = own || (pg[u] >= 0 && pg[u] < a.num_pages);
+        bad |= !own && pg[u] != -2 && !valid;
+        const __nv_bfloat16* ks =
+            own ? sk + size_t(kv - offset) * size_t(a.num_kv_heads) * HD + scratch_off
+                : kc + (valid ? size_t(pg[u]) * page_stride + head_off + size_t(kv & (a.page_size - 1)) * HD : 0);
+        const __nv_bfloat16* vs =
+            own ? sv + size_t(kv - offset) * size_t(a.num_kv_heads) * HD + scratch_off
+                : vc + (valid ? size_t(pg[u]) * page_stride + head_off + size_t(kv & (a.page_size - 1)) * HD : 0);
+        cp_async_16(kbuf(buf) + swz<HD>(row, my_chunk), ks, valid);
+        cp_async_16(vbuf(buf) + swz<HD>(row, my_chunk), vs, valid);
+      }
     }
     if (bad) record_error(a.err, kErrBadIndex);
   };
