@@ -237,28 +237,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
         mma_16816<T>(s[2 * jj + 1], qf[kk], b[2], b[3]);
       }
     }
-    // scale + mask
+    // Mask the tiles that reach the forward's own keys. Key kbase + c relative to the offset, in 32 bits: visible
+    // iff rel < rows and (a context key, or within the row's depth, or inside its own block up to its own
+    // position). Bitwise operators, so no branch per key.
     const int64_t kbase = int64_t(t) * kKeysPerTile;
-    const bool need_mask = kbase + kKeysPerTile > offset;
+    if (kbase + kKeysPerTile > offset) {
+      const int rel_base = int(kbase - offset) + 2 * tq;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int rel = rel_base + j * 8 + (e & 1);
+          const int rr = e < 2 ? r0 : r1;
+          const int dep = e < 2 ? dep0 : dep1, own = e < 2 ? own0 : own1;
+          const bool vis = (rel < a.rows) & ((rel < 0) | (rel <= dep) | ((rel >= own) & (rel <= rr)));
+          s[j][e] = vis ? s[j][e] : -INFINITY;
+        }
+      }
+    }
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float v = s[j][e] * scale;
-        if (need_mask) {
-          const int64_t kv = kbase + j * 8 + 2 * tq + (e & 1);
-          const int rr = e < 2 ? r0 : r1;
-          const int dep = e < 2 ? dep0 : dep1, own = e < 2 ? own0 : own1;
-          bool vis = kv < seq_len;
-          if (vis && kv >= offset) {
-            const int64_t rel = kv - offset;
-            vis = rel <= dep || (rel >= own && rel <= rr);
-          }
-          if (!vis) v = -INFINITY;
-        }
-        s[j][e] = v;
-      }
       mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
       mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
     }
@@ -267,17 +266,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float c0 = n0 == -INFINITY ? 1.f : ex2(m0 - n0);
-    const float c1 = n1 == -INFINITY ? 1.f : ex2(m1 - n1);
+    // Maxima are kept in raw score units and each exponent is ex2(s * scale - m * scale), one FMA. A row with no
+    // visible key yet keeps m = -inf: its exponents come out 0 and its correction 1.
+    const float ns0 = n0 == -INFINITY ? 0.f : n0 * scale, ns1 = n1 == -INFINITY ? 0.f : n1 * scale;
+    const float c0 = n0 == -INFINITY ? 1.f : ex2(fmaf(m0, scale, -ns0));
+    const float c1 = n1 == -INFINITY ? 1.f : ex2(fmaf(m1, scale, -ns1));
     m0 = n0;
     m1 = n1;
     float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-      s[j][0] = n0 == -INFINITY ? 0.f : ex2(s[j][0] - n0);
-      s[j][1] = n0 == -INFINITY ? 0.f : ex2(s[j][1] - n0);
-      s[j][2] = n1 == -INFINITY ? 0.f : ex2(s[j][2] - n1);
-      s[j][3] = n1 == -INFINITY ? 0.f : ex2(s[j][3] - n1);
+      s[j][0] = ex2(fmaf(s[j][0], scale, -ns0));
+      s[j][1] = ex2(fmaf(s[j][1], scale, -ns0));
+      s[j][2] = ex2(fmaf(s[j][2], scale, -ns1));
+      s[j][3] = ex2(fmaf(s[j][3], scale, -ns1));
       ps0 += s[j][0] + s[j][1];
       ps1 += s[j][2] + s[j][3];
     }
@@ -356,9 +358,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     *reinterpret_cast<float2*>(po + lr0 * HD + col) = make_float2(o[j][0], o[j][1]);
     *reinterpret_cast<float2*>(po + lr1 * HD + col) = make_float2(o[j][2], o[j][3]);
   }
-  if (tq == 0) {
-    *reinterpret_cast<float2*>(pml + lr0 * 2) = make_float2(m0, l0);
-    *reinterpret_cast<float2*>(pml + lr1 * 2) = make_float2(m1, l1);
+  if (tq == 0) {  // the combine works with maxima in log2 units
+    *reinterpret_cast<float2*>(pml + lr0 * 2) = make_float2(m0 * scale, l0);
+    *reinterpret_cast<float2*>(pml + lr1 * 2) = make_float2(m1 * scale, l1);
   }
   cluster_sync();
   const int S = a.splits;
