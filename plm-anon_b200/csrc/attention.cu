@@ -25,6 +25,7 @@ constexpr int kAttnThreads = 128;
 constexpr int kQRowsPerCta = 64;
 constexpr int kStages = 3;           // K/V tiles in flight per CTA (two CTAs still share an SM)
 constexpr int kMaxPageSlice = 1024;  // block-table entries staged per CTA (keys per CTA <= 1023 pages)
+constexpr int kClusterMax = 8;      // KV splits of one cluster; a launch with merge buffers has two per head
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -94,10 +95,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   const int64_t offset = *a.offset;
   const int64_t seq_len = offset + a.rows;
   const int n_tiles = int((seq_len + kKeysPerTile - 1) / kKeysPerTile);
+  // With two clusters per head (a.part set) the second one works only when every one of the 16 splits keeps at least
+  // four tiles; otherwise its CTAs leave at once and the first cluster's 8 splits cover all keys and combine
+  // through distributed shared memory.
+  const int S = a.part != nullptr && 4 * a.splits > n_tiles ? kClusterMax : a.splits;
+  if (split >= S) return;
   // Tiles spread evenly over the splits, the larger shares first: the last split holds the masked tiles of the
   // round's own keys, so it gets the smaller share.
-  const int t0 = n_tiles - int(int64_t(a.splits - split) * n_tiles / a.splits);
-  const int t1 = n_tiles - int(int64_t(a.splits - split - 1) * n_tiles / a.splits);
+  const int t0 = n_tiles - int(int64_t(S - split) * n_tiles / S);
+  const int t1 = n_tiles - int(int64_t(S - split - 1) * n_tiles / S);
   const int n_local = t1 - t0;
   int* pages = reinterpret_cast<int*>(smem + 2 * kStages * TILE_BYTES);
   const int64_t lp0 = (int64_t(t0) * kKeysPerTile) >> a.page_shift;
@@ -344,6 +350,89 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     return;
   }
 
+  if (S > kClusterMax) {
+    // ---- both clusters of the head active: split partials combined through global memory ----
+    // Each CTA stores its unnormalised partial (O, then (m, l) per row), signals a per-(head, query tile) counter and
+    // waits until all S splits have stored theirs (the host enables this only when every cluster of the launch is
+    // resident at once); split s then combines rows [s * 64 / S, (s + 1) * 64 / S) over the splits in split order,
+    // loading every split's (m, l) and 16 bytes of O together, and the last CTA done reading resets the counters.
+    constexpr int PSTRIDE = kQRowsPerCta * (HD + 2);
+    float* const head_part = a.part + size_t(head * int(gridDim.z) + qt) * S * PSTRIDE;
+    float* const mine = head_part + size_t(split) * PSTRIDE;
+    const int lr0 = warp * 16 + gq, lr1 = lr0 + 8;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      const int col = j * 8 + 2 * tq;
+      __stcg(reinterpret_cast<float2*>(mine + lr0 * HD + col), make_float2(o[j][0], o[j][1]));
+      __stcg(reinterpret_cast<float2*>(mine + lr1 * HD + col), make_float2(o[j][2], o[j][3]));
+    }
+    if (tq == 0) {  // maxima in log2 units
+      __stcg(reinterpret_cast<float2*>(mine + kQRowsPerCta * HD + lr0 * 2), make_float2(m0 * scale, l0));
+      __stcg(reinterpret_cast<float2*>(mine + kQRowsPerCta * HD + lr1 * 2), make_float2(m1 * scale, l1));
+    }
+    __syncthreads();
+    int* const ctr = a.arrive + 2 * (head * int(gridDim.z) + qt);
+    int* const flag = reinterpret_cast<int*>(smem);
+    if (tid == 0) {
+      signal_stored(ctr);
+      int ok = 1;
+      if (ld_acquire_gpu(ctr) < S) {
+        const uint64_t start = global_timer_ns();
+        while (ld_acquire_gpu(ctr) < S) {
+          if (global_timer_ns() - start > kWaitLimitNs) {
+            record_error(a.err, kErrTimeoutFlag);
+            ok = 0;
+            break;
+          }
+        }
+      }
+      *flag = ok;
+    }
+    __syncthreads();
+    if (*flag != 0) {
+      const int rpc = kQRowsPerCta / S;
+      const int row_begin = split * rpc;
+      constexpr int Q4 = HD / 4;
+      const int live = max(0, min(rpc, a.rows - (qt * kQRowsPerCta + row_begin)));
+      for (int idx = tid; idx < live * Q4; idx += kAttnThreads) {
+        const int lr = idx / Q4, c = (idx % Q4) * 4;
+        const float* ml = head_part + kQRowsPerCta * HD + (row_begin + lr) * 2;
+        const float* src = head_part + (row_begin + lr) * HD + c;
+        float2 mls[2 * kClusterMax];
+        float4 v[2 * kClusterMax];
+#pragma unroll
+        for (int sp = 0; sp < 2 * kClusterMax; ++sp) {
+          mls[sp] = __ldcg(reinterpret_cast<const float2*>(ml + size_t(sp) * PSTRIDE));
+          v[sp] = __ldcg(reinterpret_cast<const float4*>(src + size_t(sp) * PSTRIDE));
+        }
+        float mmax = -INFINITY;
+#pragma unroll
+        for (int sp = 0; sp < 2 * kClusterMax; ++sp) mmax = fmaxf(mmax, mls[sp].x);
+        float lsum = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < 2 * kClusterMax; ++sp) {
+          const float w = mls[sp].x != -INFINITY ? exp2f(mls[sp].x - mmax) : 0.f;
+          lsum += w * mls[sp].y;
+          acc.x += w * v[sp].x;
+          acc.y += w * v[sp].y;
+          acc.z += w * v[sp].z;
+          acc.w += w * v[sp].w;
+        }
+        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(out_at(qt * kQRowsPerCta + row_begin + lr, head * HD + c));
+        dst[0] = pack2<T>(acc.x * inv, acc.y * inv);
+        dst[1] = pack2<T>(acc.z * inv, acc.w * inv);
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && atomicAdd(ctr + 1, 1) == S - 1) {
+      ctr[0] = 0;
+      ctr[1] = 0;
+    }
+    return;
+  }
+
   // ---- split partials, combined over the cluster of the (head, query tile) ----
   // Each CTA leaves its unnormalised partial (O, m, l) in its own shared memory (the K/V buffers are free now);
   // after a cluster barrier rank r combines rows [r * 64 / S, (r + 1) * 64 / S) over all ranks in rank order through
@@ -363,15 +452,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     *reinterpret_cast<float2*>(pml + lr1 * 2) = make_float2(m1 * scale, l1);
   }
   cluster_sync();
-  const int S = a.splits;
   const uint32_t rank = cluster_rank();
   const int rpc = kQRowsPerCta / S;
   const int row_begin = int(rank) * rpc;
   if (tid < rpc) {
     const int row = row_begin + tid;
-    float ms[8], ls[8], mmax = -INFINITY;
+    float ms[kClusterMax], ls[kClusterMax], mmax = -INFINITY;
 #pragma unroll
-    for (int sp = 0; sp < 8; ++sp) {
+    for (int sp = 0; sp < kClusterMax; ++sp) {
       ms[sp] = -INFINITY;
       ls[sp] = 0.f;
       if (sp < S) {
@@ -383,7 +471,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
     }
     float lsum = 0.f;
 #pragma unroll
-    for (int sp = 0; sp < 8; ++sp) {
+    for (int sp = 0; sp < kClusterMax; ++sp) {
       const float w = (sp < S && ms[sp] != -INFINITY) ? exp2f(ms[sp] - mmax) : 0.f;
       if (sp < S) wts[tid * (S + 1) + sp] = w;
       lsum += w * ls[sp];
@@ -396,14 +484,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   constexpr int Q4 = HD / 4;  // float4 per row
   const int live = max(0, min(rpc, a.rows - (qt * kQRowsPerCta + row_begin)));
   for (int idx0 = tid; idx0 < live * Q4; idx0 += 2 * kAttnThreads) {
-    float4 part[2][8];
+    float4 part[2][kClusterMax];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int idx = idx0 + u * kAttnThreads;
       const int lr = idx / Q4, c = (idx % Q4) * 4;
       const uint32_t off = uint32_t((row_begin + lr) * HD + c) * 4u;
 #pragma unroll
-      for (int sp = 0; sp < 8; ++sp)
+      for (int sp = 0; sp < kClusterMax; ++sp)
         part[u][sp] = (sp < S && idx < live * Q4) ? ld_dsmem_f32x4(cluster_map(po, uint32_t(sp)) + off)
                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -414,7 +502,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
       const int lr = idx / Q4, c = (idx % Q4) * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int sp = 0; sp < 8; ++sp) {
+      for (int sp = 0; sp < kClusterMax; ++sp) {
         if (sp < S) {
           const float w = wts[lr * (S + 1) + sp];
           acc.x += w * part[u][sp].x;
@@ -440,19 +528,63 @@ int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool p
   const int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(attention smem)");
   if (st != PLM_OK) return st;
   return check_cuda(launch_ex(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl,
-                              a.splits, a),
+                              a.splits < kClusterMax ? a.splits : kClusterMax, a),
                     "round_attention_kernel");
 }
 
 }  // namespace
 
-int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys) {
+int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys, bool global_combine) {
   const int ctas = num_heads * q_tiles;
   const int max_tiles = int((max_keys + kKeysPerTile - 1) / kKeysPerTile);
   int splits = 1;
   while (splits < 8 && ctas * splits < 2 * num_sms && 2 * splits <= max_tiles) splits *= 2;
+  if (global_combine && splits == 8 && ctas * 16 <= 2 * num_sms && 4 * 16 <= max_tiles) splits = 16;
   return splits;
 }
+
+namespace {
+template <int HD, typename T>
+bool two_clusters_fit(int num_heads, int q_tiles) {
+  constexpr int SMEM = 2 * kStages * kKeysPerTile * HD * 2 + kMaxPageSlice * 4;
+  auto kernel = round_attention_kernel<HD, T>;
+  if (raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(attention smem)") != PLM_OK)
+    return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_heads, 2 * kClusterMax, q_tiles);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = kClusterMax;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return clusters >= num_heads * q_tiles * 2;
+}
+}  // namespace
+
+bool attention_two_clusters_fit(int num_heads, int q_tiles, int head_dim, int dtype) {
+  if (head_dim == 128)
+    return dtype == PLM_F16 ? two_clusters_fit<128, __half>(num_heads, q_tiles)
+                            : two_clusters_fit<128, __nv_bfloat16>(num_heads, q_tiles);
+  if (head_dim == 64)
+    return dtype == PLM_F16 ? two_clusters_fit<64, __half>(num_heads, q_tiles)
+                            : two_clusters_fit<64, __nv_bfloat16>(num_heads, q_tiles);
+  return false;
+}
+
+size_t attention_part_floats(int num_heads, int q_tiles, int head_dim) {
+  return size_t(num_heads) * q_tiles * 2 * kClusterMax * kQRowsPerCta * (head_dim + 2);
+}
+
+size_t attention_arrive_ints(int num_heads, int q_tiles) { return size_t(num_heads) * q_tiles * 2; }
 
 int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
   if (a.head_dim != 64 && a.head_dim != 128) return fail(PLM_ERR_UNSUPPORTED, "attention: head_dim %d", a.head_dim);
@@ -467,8 +599,10 @@ int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
     return fail(PLM_ERR_INVALID, "attention: null operand");
   const int q_tiles = (a.rows + kQRowsPerCta - 1) / kQRowsPerCta;
   if (a.splits < 1) a.splits = 1;
-  if (a.splits > 8 || (a.splits & (a.splits - 1)) != 0)
-    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits (a power of two <= 8)", a.splits);
+  if (a.part != nullptr ? a.splits != 2 * kClusterMax || a.arrive == nullptr
+                        : (a.splits & (a.splits - 1)) != 0 || a.splits > kClusterMax)
+    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits (a power of two <= %d, or %d with merge buffers)", a.splits,
+                kClusterMax, 2 * kClusterMax);
   a.err = ctx->err;
   if (a.dtype == PLM_F16)
     return a.head_dim == 128 ? launch_attention<128, __half>(a, q_tiles, stream, pdl)
@@ -504,5 +638,28 @@ extern "C" int plm_attention(plm_ctx* ctx, const plm_attention_desc* d, void* st
   a.out = d->out;
   const int q_tiles = (d->rows + kQRowsPerCta - 1) / kQRowsPerCta;
   a.splits = d->splits > 0 ? d->splits : attention_splits(d->num_heads, q_tiles, ctx->num_sms, d->max_keys);
+  if (a.splits == 2 * kClusterMax) {  // two clusters per head: the context's merge buffers, grown to this shape
+    if (!attention_two_clusters_fit(d->num_heads, q_tiles, d->head_dim, d->dtype))
+      return fail(PLM_ERR_UNSUPPORTED, "plm_attention: 16 splits need every cluster resident at once");
+    const size_t nf = attention_part_floats(d->num_heads, q_tiles, d->head_dim);
+    const size_t na = attention_arrive_ints(d->num_heads, q_tiles);
+    if (ctx->attn_part_floats < nf || ctx->attn_arrive_ints < na) {
+      int st = check_cuda(cudaDeviceSynchronize(), "plm_attention: synchronize before growing the merge buffers");
+      if (st != PLM_OK) return st;
+      cudaFree(ctx->attn_part);
+      cudaFree(ctx->attn_arrive);
+      ctx->attn_part = nullptr;
+      ctx->attn_arrive = nullptr;
+      ctx->attn_part_floats = ctx->attn_arrive_ints = 0;
+      st = check_cuda(cudaMalloc(&ctx->attn_part, nf * sizeof(float)), "plm_attention: merge buffers");
+      if (st == PLM_OK) st = check_cuda(cudaMalloc(&ctx->attn_arrive, na * sizeof(int)), "plm_attention: counters");
+      if (st == PLM_OK) st = check_cuda(cudaMemset(ctx->attn_arrive, 0, na * sizeof(int)), "plm_attention: counters");
+      if (st != PLM_OK) return st;
+      ctx->attn_part_floats = nf;
+      ctx->attn_arrive_ints = na;
+    }
+    a.part = ctx->attn_part;
+    a.arrive = ctx->attn_arrive;
+  }
   return attention_launch(ctx, a, static_cast<cudaStream_t>(stream), true);
 }

@@ -32,11 +32,24 @@ struct AttnArgs {
   // [head_dim] planes (the round scratch) instead of the paged cache
   const void* scratch_k;
   const void* scratch_v;
+  // non-null (with splits = 16): two clusters of 8 splits per (head, query tile). When the keys give all 16 splits four
+  // tiles each, every split stores its partial to `part` and waits (bounded) for the others, so every cluster of the
+  // launch must be resident at once (attention_two_clusters_fit); otherwise the second cluster leaves at once and the
+  // first combines through distributed shared memory. part holds [num_heads][q_tiles][16] x 64 rows x
+  // (head_dim + 2) floats, arrive [num_heads][q_tiles][2] counters that are zero between launches.
+  float* part;
+  int* arrive;
   int* err;
 };
 
-// Split count that fills about two CTAs per SM for `max_keys` keys.
-int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys);
+// Split count that fills about two CTAs per SM for `max_keys` keys: at most 8 (one cluster), or with
+// `global_combine` 16 (two clusters) when the keys can give every split four tiles.
+int attention_splits(int num_heads, int q_tiles, int num_sms, int64_t max_keys, bool global_combine = false);
+// Whether every cluster of a two-cluster launch (heads x q_tiles x 2 clusters of 8) is resident at once.
+bool attention_two_clusters_fit(int num_heads, int q_tiles, int head_dim, int dtype);
+// Sizes of the merge buffers of a two-cluster launch.
+size_t attention_part_floats(int num_heads, int q_tiles, int head_dim);
+size_t attention_arrive_ints(int num_heads, int q_tiles);
 int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl);
 
 }  // namespace plm

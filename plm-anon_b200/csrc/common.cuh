@@ -129,6 +129,14 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 __device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Acquire-release add returning the previous value: the release (after a fence) covers the stores the calling CTA
+// ordered before it with a barrier, the acquire the loads that follow it.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
 __device__ __forceinline__ void signal_stored(int* counter) {
   asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.s32 [%0], 1;" ::"l"(counter) : "memory");
 }

@@ -85,6 +85,8 @@ struct plm_handle {
   int64_t stop_host[4] = {};    // the values plm_set_stop last queued (the copy's host source stays valid)
   int64_t prompt_len = 0;
   int attn_splits_round = 1;
+  float* attn_part = nullptr;  // the round attention's split partials when its splits are combined in memory
+  int* attn_arrive = nullptr;
   // MLP block kernel: schedule, per-layer gate_up counters and the forward counter they are compared with
   plm::MlpSchedule mlp;
   int* block_ctr = nullptr;  // [layers][4] phase counters of the layer blocks, zeroed by every forward's prologue
@@ -337,6 +339,10 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
       a.out = h->attn;
     }
     a.splits = attn_splits;
+    if (attn_splits > 8) {  // the round's attention with two clusters of splits per head
+      a.part = h->attn_part;
+      a.arrive = h->attn_arrive;
+    }
     if (round_rows) {
       a.scratch_k = round_plane(h, l, 0);
       a.scratch_v = round_plane(h, l, 1);
@@ -581,7 +587,7 @@ int plm_destroy(plm_handle* h) {
                   h->causal_own, h->kv, h->block_table, h->out, h->base, h->offset, h->anchor, h->pending,
                   h->round_sequence, h->sequence_step, h->aux_buf, h->prompt, h->chunk_offsets, h->stop, h->round_kv,
                   h->commit, h->aux_u, h->lora_hidden, h->lora_corr, h->block_ctr,
-                  h->block_tiles, h->attn_tiles, h->x_tiles, h->act_tiles};
+                  h->block_tiles, h->attn_tiles, h->x_tiles, h->act_tiles, h->attn_part, h->attn_arrive};
   for (void* b : bufs) cudaFree(b);
   mlp_schedule_destroy(&h->mlp);
   if (h->own_table) cudaFree(h->table);
@@ -832,7 +838,18 @@ int plm_create(const plm_model_desc* m, const plm_weight_ptrs* w, const plm_roun
   }
   if (st != PLM_OK) return guard(st);
   h->attn_splits_round = attention_splits(m->num_heads, (h->W + 63) / 64, h->ctx->num_sms,
-                                          int64_t(rd->max_pages) * rd->page_size);
+                                          int64_t(rd->max_pages) * rd->page_size, true);
+  if (h->attn_splits_round > 8 &&
+      !attention_two_clusters_fit(m->num_heads, (h->W + 63) / 64, hd, m->dtype))  // both clusters must be resident
+    h->attn_splits_round = 8;
+  if (h->attn_splits_round > 8) {
+    const int q_tiles = (h->W + 63) / 64;
+    const size_t n_arrive = attention_arrive_ints(m->num_heads, q_tiles);
+    st = dev_alloc(&h->attn_part, attention_part_floats(m->num_heads, q_tiles, hd), "attention partials");
+    if (st == PLM_OK) st = dev_alloc(&h->attn_arrive, n_arrive, "attention counters");
+    if (st == PLM_OK) st = check_cuda(cudaMemset(h->attn_arrive, 0, n_arrive * sizeof(int)), "memset");
+    if (st != PLM_OK) return guard(st);
+  }
 
   // the Voronoi cost table -(aux_vocab . lm_head^T)^T, [vocab][A] (plm/auxiliary.py:56-65)
   if (w->table != nullptr || w->ptp != nullptr) {  // the PTP scheme decodes without a cost table

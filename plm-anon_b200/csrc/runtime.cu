@@ -155,6 +155,8 @@ int plm_ctx_destroy(plm_ctx* ctx) {
   if (ctx == nullptr) return PLM_OK;
   cudaFree(ctx->err);
   cudaFree(ctx->counters);
+  cudaFree(ctx->attn_part);
+  cudaFree(ctx->attn_arrive);
   delete ctx;
   return PLM_OK;
 }

@@ -20,6 +20,10 @@ struct plm_ctx {
   int* err = nullptr;           // device error word
   int* counters = nullptr;      // arrival counters, zero between launches
   int n_counters = 0;
+  float* attn_part = nullptr;   // plm_attention's two-cluster merge buffers, grown on demand
+  size_t attn_part_floats = 0;
+  int* attn_arrive = nullptr;   // zero between launches
+  size_t attn_arrive_ints = 0;
 };
 
 namespace plm {

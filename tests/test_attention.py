@@ -55,6 +55,11 @@ def _reference(q, kc, vc, table, offset, depth, own, page, heads, kv_heads):
     ("steady", 7, 32768, 16, 16, 16, 128, 0),   # the longest context of the configs[4] sweep
     ("steady", 7, 4096, 64, 16, 16, 128, 0),    # the reference's page size (bench/engine.py:4)
     ("steady", 7, 4096, 16, 20, 20, 128, 0),    # the 3B shape's 20 heads
+    # 16 splits: two clusters of 8 per head merged through memory (the second idle below 64 key tiles)
+    ("steady", 7, 4096, 16, 16, 16, 128, 16),
+    ("steady", 7, 32768, 16, 16, 16, 128, 16),
+    ("steady", 7, 1024, 16, 16, 16, 128, 16),
+    ("steady", 7, 8192, 32, 16, 4, 128, 16),
     ("steady", 7, 1000, 32, 16, 16, 128, 1),
     ("steady", 4, 333, 64, 8, 8, 64, 0),
     ("steady", 6, 190, 16, 8, 8, 64, 2),
@@ -121,6 +126,62 @@ def test_attention_split_invariance(ctx):
         outs[splits] = out
     for splits in (4, 8):
         assert (outs[splits].float() - outs[1].float()).abs().max().item() < 2e-2
+
+
+def test_attention_sixteen_splits_need_resident_clusters(ctx):
+    """16 splits wait for one another, so a launch whose clusters cannot all be resident at once (k = 8: 72 rows in
+    two query tiles, 64 clusters of 8) is refused up front instead of risking a wait."""
+    from plm import native
+
+    k, ctx_len, page, heads, hd = 8, 4096, 16, 16, 128
+    rows = k + k * k
+    depth, own = _layout("steady", k, rows)
+    max_pages = -(-(ctx_len + rows) // page)
+    kc, vc = _pool(max_pages, heads, page, hd, seed=11)
+    table = torch.arange(max_pages, dtype=torch.int32, device="cuda")
+    q = torch.randn(rows, heads, hd, device="cuda").bfloat16()
+    out = torch.zeros(rows, heads * hd, dtype=torch.bfloat16, device="cuda")
+    offset = torch.tensor([ctx_len], dtype=torch.int64, device="cuda")
+    depth_t = torch.as_tensor(depth, dtype=torch.int32, device="cuda")
+    own_t = torch.as_tensor(own, dtype=torch.int32, device="cuda")
+    desc = native.AttentionDesc(dtype=native.PLM_BF16, q=q.data_ptr(), k_cache=kc.data_ptr(), v_cache=vc.data_ptr(),
+                                block_table=table.data_ptr(), max_pages=max_pages, num_pages=max_pages,
+                                page_size=page, offset=offset.data_ptr(), rows=rows, depth=depth_t.data_ptr(),
+                                own_start=own_t.data_ptr(), num_heads=heads, num_kv_heads=heads, head_dim=hd,
+                                out=out.data_ptr(), splits=16, max_keys=ctx_len + rows)
+    with pytest.raises(native.NativeError, match="resident"):
+        native.attention(ctx, desc)
+
+
+def test_attention_two_cluster_merge_invariance(ctx):
+    """16 splits (two clusters merged through memory) agree with 8 within fp32 reassociation and repeat bit for
+    bit, launch after launch (the merge counters return to zero)."""
+    from plm import native
+
+    k, ctx_len, page, heads, hd = 7, 5000, 16, 16, 128
+    rows = k + k * k
+    depth, own = _layout("steady", k, rows)
+    max_pages = -(-(ctx_len + rows) // page)
+    kc, vc = _pool(max_pages, heads, page, hd, seed=10)
+    table = torch.arange(max_pages, dtype=torch.int32, device="cuda")
+    q = torch.randn(rows, heads, hd, device="cuda").bfloat16()
+    offset = torch.tensor([ctx_len], dtype=torch.int64, device="cuda")
+    depth_t = torch.as_tensor(depth, dtype=torch.int32, device="cuda")
+    own_t = torch.as_tensor(own, dtype=torch.int32, device="cuda")
+    outs = []
+    for splits in (8, 16, 16, 16):
+        out = torch.zeros(rows, heads * hd, dtype=torch.bfloat16, device="cuda")
+        desc = native.AttentionDesc(dtype=native.PLM_BF16, q=q.data_ptr(), k_cache=kc.data_ptr(),
+                                    v_cache=vc.data_ptr(), block_table=table.data_ptr(), max_pages=max_pages,
+                                    num_pages=max_pages, page_size=page, offset=offset.data_ptr(), rows=rows,
+                                    depth=depth_t.data_ptr(), own_start=own_t.data_ptr(), num_heads=heads,
+                                    num_kv_heads=heads, head_dim=hd, out=out.data_ptr(), splits=splits,
+                                    max_keys=ctx_len + rows)
+        native.attention(ctx, desc)
+        ctx.check()
+        outs.append(out)
+    assert torch.equal(outs[1], outs[2]) and torch.equal(outs[1], outs[3])
+    assert (outs[1].float() - outs[0].float()).abs().max().item() < 2e-2
 
 
 def test_attention_permutation_invariance(ctx):

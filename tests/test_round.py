@@ -110,6 +110,8 @@ def _close(name, gpu, ref, report, rel=0.0, floor=0.0):
     # a 200-row prefill runs the separate launches (wider than the layer block's 128 rows), then the rounds run the
     # layer block: its phase counters and row tiles must not depend on what the forward before did
     ("plm-tiny", 7, 16, "nucleus", None, {"prompt_len": 200}),
+    # a 4096-token capacity: the round attention runs 16 KV splits combined through global memory
+    ("plm-tiny", 7, 16, "nucleus", None, {"max_model_len": 4096}),
 ])
 def test_round_parity_teacher_forced(shape, k, page, rule, threshold, overrides):
     overrides = dict(overrides)
