@@ -527,8 +527,10 @@ int launch_attention(const AttnArgs& a, int q_tiles, cudaStream_t stream, bool p
   auto kernel = round_attention_kernel<HD, T>;
   const int st = raise_smem_limit(reinterpret_cast<const void*>(kernel), SMEM, "cudaFuncSetAttribute(attention smem)");
   if (st != PLM_OK) return st;
-  return check_cuda(launch_ex(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream, pdl,
-                              a.splits < kClusterMax ? a.splits : kClusterMax, a),
+  // Two clusters per head take the load-balancing placement: spread over distinct SMs, some of the 32 clusters
+  // started well after the others while the previous kernel still held SMs. One cluster per head stays spread.
+  return check_cuda(launch_cluster_pref(kernel, dim3(a.num_heads, a.splits, q_tiles), dim3(kAttnThreads), SMEM, stream,
+                                        pdl, 1, a.splits < kClusterMax ? a.splits : kClusterMax, a.part != nullptr, a),
                     "round_attention_kernel");
 }
 

@@ -44,16 +44,18 @@ int encode_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner,
 // than an earlier one return at once. Thread-safe.
 int raise_smem_limit(const void* kernel, int bytes, const char* what);
 
-// Launch with optional programmatic dependent launch and an optional cluster of cluster_x * cluster_y CTAs.
+// Launch with optional programmatic dependent launch and an optional cluster of cluster_x * cluster_y CTAs. With
+// `pack`, the hardware may place several CTAs of one cluster on an SM (load-balancing scheduling) instead of
+// spreading them over distinct SMs.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                           bool pdl, int cluster_x, int cluster_y, Args&&... args) {
+cudaError_t launch_cluster_pref(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                bool pdl, int cluster_x, int cluster_y, bool pack, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   int n = 0;
   if (pdl) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -66,10 +68,22 @@ cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size
     attr[n].val.clusterDim.y = unsigned(cluster_y);
     attr[n].val.clusterDim.z = 1;
     ++n;
+    if (pack) {
+      attr[n].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+      attr[n].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicyLoadBalancing;
+      ++n;
+    }
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           bool pdl, int cluster_x, int cluster_y, Args&&... args) {
+  return launch_cluster_pref(kernel, grid, block, smem, stream, pdl, cluster_x, cluster_y, false,
+                             std::forward<Args>(args)...);
 }
 
 // Cluster of `cluster_y` CTAs along y.
