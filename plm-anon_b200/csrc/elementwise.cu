@@ -159,6 +159,9 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
     }
   }
   ss = block_sum_rows(ss, red);
+  // The next kernel (the qkv projection's clusters) is let in only now: launched at this kernel's start, its
+  // clusters were placed while the layer block still held most SMs, and one launch in three ran half again as long.
+  allow_dependents();
   const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
 #pragma unroll
   for (int j = 0; j < kMaxVecs; ++j) {
@@ -181,7 +184,6 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs
   __shared__ float red[32];
   const int r = blockIdx.x, tid = threadIdx.x;
   grid_dependency_wait();
-  allow_dependents();
   const T* __restrict__ x = reinterpret_cast<const T*>(a.x) + size_t(r) * a.hidden;
   T* __restrict__ res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
   T* __restrict__ nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
@@ -262,6 +264,9 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs
     }
   }
   ss = block_sum_rows(ss, red);
+  // The next kernel (the qkv projection's clusters) is let in only now: launched at this kernel's start, its
+  // clusters were placed while the layer block still held most SMs, and one launch in three ran half again as long.
+  allow_dependents();
   const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
 #pragma unroll
   for (int j = 0; j < kMaxVecs; ++j) {
