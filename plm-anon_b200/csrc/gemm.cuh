@@ -108,9 +108,26 @@ constexpr int gemm_bar_offset() {
   return ((ring > staging ? ring : staging) + 7) & ~7;
 }
 
+// The QKV epilogue's per-column data: positions and slots in an area of their own (read while the MMAs run), the
+// rotary rows of those positions in the ring's space past the staging tile (copied once the ring is consumed), where
+// that space holds NTOK rows of head_dim <= 128.
+template <int NTOK>
+constexpr int gemm_rowdata_bytes() {
+  return (NTOK * 12 + 15) & ~15;
+}
+template <int NTOK>
+constexpr int gemm_staging_end() {
+  return ((NTOK <= 128 ? NTOK + NTOK / 2 : NTOK) * kStagePad * 4 + 15) & ~15;
+}
+template <int NTOK, int STAGES>
+constexpr bool gemm_rope_staged() {
+  return gemm_bar_offset<NTOK, STAGES>() - gemm_staging_end<NTOK>() >= NTOK * 128 * 2;
+}
+
 template <int NTOK, int STAGES>
 constexpr int gemm_smem_bytes() {
-  return gemm_bar_offset<NTOK, STAGES>() + 1024 /*alignment slack*/ + 256 /*barriers, flags*/;
+  return gemm_bar_offset<NTOK, STAGES>() + 1024 /*alignment slack*/ + 256 /*barriers, flags*/ +
+         gemm_rowdata_bytes<NTOK>();
 }
 
 template <typename T, int NTOK, int STAGES, int EPI>
@@ -241,6 +258,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   grid_dependency_wait();
 
+  // This CTA's token columns after the split reduction: [c_begin, c_end) of the tile.
+  const int S = args.splits;
+  const uint32_t rank = S > 1 ? cluster_rank() : 0;
+  const int cs = (args.rows + S - 1) / S;
+  const int c_begin = min(args.rows, int(rank) * cs), c_end = min(args.rows, c_begin + cs);
+  constexpr bool kRopeStaged = EPI == kEpiQkvRope && gemm_rope_staged<NTOK, STAGES>();
+  const bool rope_staged = kRopeStaged && args.qkv.head_dim <= 128;
+  int* const rd_pos = reinterpret_cast<int*>(smem + gemm_bar_offset<NTOK, STAGES>() + 256);  // [NTOK]
+  int64_t* const rd_slot = reinterpret_cast<int64_t*>(rd_pos + NTOK);                       // [NTOK]
+  T* const rd_cs = reinterpret_cast<T*>(smem + gemm_staging_end<NTOK>());                    // [NTOK][head_dim]
+  if (rope_staged && warp >= 2) {  // warps without a role fetch the columns' positions and slots meanwhile
+    for (int i = tid - 64; i < c_end - c_begin; i += kGemmThreads - 64) {
+      rd_pos[i] = __ldg(args.qkv.positions + c_begin + i);
+      rd_slot[i] = __ldg(args.qkv.slots + c_begin + i);
+    }
+  }
+
   // ---------------- accumulator -> this CTA's staging tile (fp32, [token][feature]) ----------------
   const bool mma_ok = warp_wait(done_bar, 0, kErrTimeoutDone);
   tc_fence_after();
@@ -265,6 +299,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (rope_staged && flags[0] == 0) {
+    // The rotary rows of the columns' positions, copied into the consumed ring while the split reduction runs.
+    const int hd = args.qkv.head_dim, chunks = hd / 8;
+    const T* cs_tab = reinterpret_cast<const T*>(args.qkv.cos_sin);
+    for (int idx = tid; idx < (c_end - c_begin) * chunks; idx += kGemmThreads) {
+      const int r = idx / chunks, ch = idx % chunks;
+      const int pos = rd_pos[r];
+      const bool valid = pos >= 0 && pos < args.qkv.max_pos;
+      cp_async_16(rd_cs + r * hd + ch * 8, cs_tab + (valid ? size_t(pos) * hd + ch * 8 : 0), valid);
+    }
+    cp_async_commit();
+  }
   if (flags[0] != 0 && tid == 0) {
     // Aborted: let every TMA copy this CTA issued but never consumed land before shared memory is reused.
     for (int i = flags[3]; i < flags[2]; ++i)
@@ -281,10 +327,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // The `splits` CTAs of a tile form one cluster. After the barrier, rank r sums the partial tiles of all ranks,
   // in rank order, for its slice of token columns [c_begin, c_end), reading peers' staging tiles through
   // distributed shared memory; a second barrier keeps every staging tile alive until all slices are read.
-  const int S = args.splits;
-  const uint32_t rank = S > 1 ? cluster_rank() : 0;
-  const int cs = (rows + S - 1) / S;
-  const int c_begin = min(rows, int(rank) * cs), c_end = min(rows, c_begin + cs);
   float* red = stage;
   if (S > 1) {
     red = stage + rows * kStagePad;
@@ -328,6 +370,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
   }
   if (!ok) return;
+  if (kRopeStaged) {
+    cp_async_wait<0>();
+    __syncthreads();
+  }
   // From here `red` holds the finished tile for token columns [c_begin, c_end), local column c - c_begin.
 
   // ---------------- fused epilogues ----------------
@@ -384,21 +430,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (cr != nullptr) x = round_to<T>(x + cr[F]);  // the adapter's output joins before the rotary embedding
       float y = x;
       if (rope) {
-        const int pos = __ldg(q.positions + c);
+        const int pos = rope_staged ? rd_pos[lc] : __ldg(q.positions + c);
         if (pos < 0 || pos >= q.max_pos) {
           record_error(args.err, kErrBadIndex);
           continue;
         }
         float xp = round_to<T>(red[lc * kStagePad + fp]);
         if (cr != nullptr) xp = round_to<T>(xp + cr[tile * 128 + fp]);
-        const float cv = to_f32<T>(__ldg(cs_tab + size_t(pos) * hd + dh));
-        const float sv = to_f32<T>(__ldg(cs_tab + size_t(pos) * hd + half + dh));
+        const T* cs_row = rope_staged ? rd_cs + lc * hd : cs_tab + size_t(pos) * hd;
+        const float cv = to_f32<T>(cs_row[dh]);
+        const float sv = to_f32<T>(cs_row[half + dh]);
         y = d < half ? x * cv - xp * sv : x * cv + xp * sv;
       }
       if (is_q) {
         reinterpret_cast<T*>(q.q_out)[size_t(c) * q_size + F] = from_f32<T>(y);
       } else {
-        const int64_t slot = __ldg(q.slots + c);
+        const int64_t slot = rope_staged ? rd_slot[lc] : __ldg(q.slots + c);
         if (slot < 0 || slot >= q.num_slots) {
           record_error(args.err, kErrBadIndex);
           continue;
