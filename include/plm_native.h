@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define PLM_ABI_VERSION 7
+#define PLM_ABI_VERSION 8
 
 enum plm_status {
   PLM_OK = 0,
@@ -425,6 +425,14 @@ int plm_round(plm_handle* h, void* stream);
  * updating the residual and the down partials. For measurement and tests; PLM_ERR_UNSUPPORTED when the handle was
  * created with separate_mlp. */
 int plm_layer_block(plm_handle* h, int32_t layer, int32_t rows, void* stream);
+
+/* Which of the caller's weight tensors the handle still reads after plm_create (a bit mask). PLM_WEIGHTS_IN_PLACE:
+ * qkv, lm_head, the norms and the embeddings, always. PLM_WEIGHTS_BLOCK: the o, gate_up and down projections, read
+ * only by a handle that runs them as separate launches (separate_mlp or gated-LoRA adapters); otherwise every launch
+ * reads the handle's packed copies, and the caller may free those three tensors once plm_create has returned. */
+#define PLM_WEIGHTS_IN_PLACE 1
+#define PLM_WEIGHTS_BLOCK 2
+int plm_borrowed_weights(plm_handle* h, int32_t* groups);
 /* The layer block's unit schedule for num_sms CTAs (host only: no device is touched). No counterpart in the
  * reference: it exposes how plm_layer_block spreads o / norm / gate_up / down work over the SMs, for tests and
  * inspection. units gets *n_units codes, CTA after CTA; offsets[c] .. offsets[c + 1] are CTA c's (offsets has

@@ -33,7 +33,7 @@ int tiles_for(int kind, int n_out, int gate_offset) {
   return kind == PLM_EPI_SILU_MUL ? gate_offset / 64 : (n_out + 127) / 128;
 }
 
-GemmArgs make_args(plm_ctx* ctx, const plm_gemm_desc& d, int tiles, int splits, int kb_per) {
+GemmArgs make_args(plm_ctx* ctx, const plm_gemm_desc& d, int tiles, int splits, int kb_per, const void* w_packed) {
   GemmArgs a = {};
   a.n_out = d.n_out;
   a.k = d.k;
@@ -53,12 +53,13 @@ GemmArgs make_args(plm_ctx* ctx, const plm_gemm_desc& d, int tiles, int splits, 
   a.corr = e.corr;
   a.corr_from = e.corr_from;
   a.corr_ld = e.corr_ld;
+  a.w_packed = static_cast<const uint8_t*>(w_packed);
   return a;
 }
 
 template <typename T, int NTOK, int EPI>
 int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,
-               cudaStream_t stream, bool pdl) {
+               cudaStream_t stream, bool pdl, const void* w_packed) {
   constexpr int STAGES = stages_for<NTOK, EPI>();
   constexpr int SMEM = gemm_smem_bytes<NTOK, STAGES>();
   auto kernel = skinny_gemm_kernel<T, NTOK, STAGES, EPI>;
@@ -79,7 +80,7 @@ int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, c
     if (NTOK > 128) splits = 1;  // the staging area holds no reduced slice for the widest tiles
   }
   const int kb_per = (total_kb + splits - 1) / splits;
-  GemmArgs args = make_args(ctx, d, tiles, splits, kb_per);
+  GemmArgs args = make_args(ctx, d, tiles, splits, kb_per, w_packed);
   return check_cuda(launch_ex(kernel, dim3(tiles, splits), dim3(kGemmThreads), SMEM, stream, pdl,
                               EPI == kEpiPartial ? 1 : splits, *map_w,
                               *map_x, args),
@@ -88,31 +89,31 @@ int launch_one(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, c
 
 template <typename T, int NTOK>
 int launch_epi(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* mw, const CUtensorMap* mx,
-               cudaStream_t s, bool pdl) {
+               cudaStream_t s, bool pdl, const void* wp) {
   switch (d.epi.kind) {
-    case PLM_EPI_STORE: return launch_one<T, NTOK, kEpiStore>(ctx, d, mw, mx, s, pdl);
-    case PLM_EPI_SILU_MUL: return launch_one<T, NTOK, kEpiSiluMul>(ctx, d, mw, mx, s, pdl);
-    case PLM_EPI_QKV_ROPE: return launch_one<T, NTOK, kEpiQkvRope>(ctx, d, mw, mx, s, pdl);
-    case PLM_EPI_LOGITS: return launch_one<T, NTOK, kEpiLogits>(ctx, d, mw, mx, s, pdl);
-    case PLM_EPI_TABLE: return launch_one<T, NTOK, kEpiTable>(ctx, d, mw, mx, s, pdl);
-    case PLM_EPI_PARTIAL: return launch_one<T, NTOK, kEpiPartial>(ctx, d, mw, mx, s, pdl);
+    case PLM_EPI_STORE: return launch_one<T, NTOK, kEpiStore>(ctx, d, mw, mx, s, pdl, wp);
+    case PLM_EPI_SILU_MUL: return launch_one<T, NTOK, kEpiSiluMul>(ctx, d, mw, mx, s, pdl, wp);
+    case PLM_EPI_QKV_ROPE: return launch_one<T, NTOK, kEpiQkvRope>(ctx, d, mw, mx, s, pdl, wp);
+    case PLM_EPI_LOGITS: return launch_one<T, NTOK, kEpiLogits>(ctx, d, mw, mx, s, pdl, wp);
+    case PLM_EPI_TABLE: return launch_one<T, NTOK, kEpiTable>(ctx, d, mw, mx, s, pdl, wp);
+    case PLM_EPI_PARTIAL: return launch_one<T, NTOK, kEpiPartial>(ctx, d, mw, mx, s, pdl, wp);
   }
   return fail(PLM_ERR_INVALID, "plm_gemm: unknown epilogue %d", d.epi.kind);
 }
 
 template <typename T>
 int launch_dtype(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* mw, const CUtensorMap* mx,
-                 cudaStream_t s, bool pdl) {
+                 cudaStream_t s, bool pdl, const void* wp) {
   switch (gemm_token_tile(d.rows)) {
-    case 16: return launch_epi<T, 16>(ctx, d, mw, mx, s, pdl);
-    case 32: return launch_epi<T, 32>(ctx, d, mw, mx, s, pdl);
-    case 48: return launch_epi<T, 48>(ctx, d, mw, mx, s, pdl);
-    case 64: return launch_epi<T, 64>(ctx, d, mw, mx, s, pdl);
-    case 80: return launch_epi<T, 80>(ctx, d, mw, mx, s, pdl);
-    case 96: return launch_epi<T, 96>(ctx, d, mw, mx, s, pdl);
-    case 112: return launch_epi<T, 112>(ctx, d, mw, mx, s, pdl);
-    case 128: return launch_epi<T, 128>(ctx, d, mw, mx, s, pdl);
-    case 256: return launch_epi<T, 256>(ctx, d, mw, mx, s, pdl);
+    case 16: return launch_epi<T, 16>(ctx, d, mw, mx, s, pdl, wp);
+    case 32: return launch_epi<T, 32>(ctx, d, mw, mx, s, pdl, wp);
+    case 48: return launch_epi<T, 48>(ctx, d, mw, mx, s, pdl, wp);
+    case 64: return launch_epi<T, 64>(ctx, d, mw, mx, s, pdl, wp);
+    case 80: return launch_epi<T, 80>(ctx, d, mw, mx, s, pdl, wp);
+    case 96: return launch_epi<T, 96>(ctx, d, mw, mx, s, pdl, wp);
+    case 112: return launch_epi<T, 112>(ctx, d, mw, mx, s, pdl, wp);
+    case 128: return launch_epi<T, 128>(ctx, d, mw, mx, s, pdl, wp);
+    case 256: return launch_epi<T, 256>(ctx, d, mw, mx, s, pdl, wp);
   }
   return fail(PLM_ERR_UNSUPPORTED, "plm_gemm: %d rows (1..256 supported)", d.rows);
 }
@@ -211,11 +212,14 @@ int gemm_partial_splits(plm_ctx* ctx, int n_out, int k, int rows) {
 }
 
 int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,
-                cudaStream_t stream, bool pdl) {
+                cudaStream_t stream, bool pdl, const void* w_packed) {
   int st = validate(d);
   if (st != PLM_OK) return st;
-  if (d.dtype == PLM_F16) return launch_dtype<__half>(ctx, d, map_w, map_x, stream, pdl);
-  return launch_dtype<__nv_bfloat16>(ctx, d, map_w, map_x, stream, pdl);
+  if (w_packed != nullptr && (d.epi.kind == PLM_EPI_LOGITS || d.epi.kind == PLM_EPI_TABLE ||
+                              (reinterpret_cast<uintptr_t>(w_packed) & 15) != 0))
+    return fail(PLM_ERR_INVALID, "gemm: packed weights for the projections only, 16-byte aligned");
+  if (d.dtype == PLM_F16) return launch_dtype<__half>(ctx, d, map_w, map_x, stream, pdl, w_packed);
+  return launch_dtype<__nv_bfloat16>(ctx, d, map_w, map_x, stream, pdl, w_packed);
 }
 
 }  // namespace plm

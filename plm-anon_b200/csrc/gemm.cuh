@@ -83,6 +83,9 @@ struct GemmArgs {
   const float* corr;  // kEpiQkvRope / kEpiSiluMul: fp32 corrections of rows >= corr_from (gated-LoRA adapters)
   int corr_from;
   int corr_ld;
+  // non-null: the weight as packed 128-row tiles (pack.cu: [tile][k-block] 16 KB shared-memory images), loaded with
+  // one untiled bulk copy per k-block instead of the tensor map
+  const uint8_t* w_packed;
 };
 
 constexpr int kGemmBK = 64;
@@ -189,6 +192,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     auto load_w = [&](int s, int kb) {
       uint8_t* a = smem + s * Shape::STAGE_BYTES;
+      if (args.w_packed != nullptr) {
+        bulk_load(a, args.w_packed + (size_t(tile) * (args.k / kGemmBK) + kb) * Shape::A_BYTES, Shape::A_BYTES,
+                  full_bar + s, pol_w);
+        return;
+      }
       if (EPI == kEpiSiluMul) {
         // 64 gate rows then the 64 up rows of the same intermediate features.
         tma_load_2d(a, &map_w, full_bar + s, kb * kGemmBK, tile * 64, pol_w);

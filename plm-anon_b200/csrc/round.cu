@@ -143,7 +143,8 @@ int row_map(plm_handle* h, const void* buffer, int k, int rows, const CUtensorMa
 }
 
 int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, const void* x, int rows,
-         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s, int splits = 0, int x_rows = 0) {
+         const plm_gemm_epilogue& epi, void* out, int ldo, cudaStream_t s, int splits = 0, int x_rows = 0,
+         const void* w_packed = nullptr) {
   plm_gemm_desc d = {};
   d.dtype = h->m.dtype;
   d.w = w;
@@ -159,7 +160,15 @@ int gemm(plm_handle* h, const void* w, const CUtensorMap* mw, int n_out, int k, 
   const CUtensorMap* mx = nullptr;
   int st = row_map(h, x, k, rows, &mx, x_rows);
   if (st != PLM_OK) return st;
-  return gemm_launch(h->ctx, d, mw, mx, s, true);
+  return gemm_launch(h->ctx, d, mw, mx, s, true, w_packed);
+}
+
+// The packed copy of layer l's o (which 0), gate_up (1) or down (2) weight when the handle holds one: the separate
+// launches read it too, so the caller's originals are not read after plm_create.
+const void* packed_weight(const plm_handle* h, int l, int which) {
+  if (h->block_tiles == nullptr) return nullptr;
+  const uint8_t* w = static_cast<const uint8_t*>(h->block_tiles) + size_t(l) * h->block_layer_bytes;
+  return which == 0 ? w : which == 1 ? w + h->block_o_bytes : w + h->block_o_bytes + h->block_gate_up_bytes;
 }
 
 // Layer `l`'s block (mlp.cu): o projection, the residual-add RMSNorm after it, gate_up + SiLU and down as k-split
@@ -364,7 +373,8 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
       st = lora_correction(h, l, 1, h->attn, q_size, gated_from, rows, hidden, s, &ld);
       if (st != PLM_OK) return st;
       const int s_o = gemm_partial_splits(h->ctx, hidden, q_size, rows);
-      st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, part, h->partials, hidden, s, s_o);
+      st = gemm(h, h->o[l], &h->map_o[l], hidden, q_size, h->attn, rows, part, h->partials, hidden, s, s_o, 0,
+                packed_weight(h, l, 0));
       if (st != PLM_OK) return st;
       AddNormArgs n1 = {nullptr, h->residual, h->x_norm, h->post_norm[l], hidden, m.rms_eps, -1, nullptr,
                         h->partials, s_o, slice};
@@ -386,13 +396,13 @@ int forward(plm_handle* h, int mode, int rows, const int64_t* offset_ptr, const 
         silu.corr_from = gated_from;
       }
       st = gemm(h, h->gate_up[l], &h->map_gate_up[l], 2 * m.intermediate, hidden, h->x_norm, rows, silu, h->act,
-                m.intermediate, s);
+                m.intermediate, s, 0, 0, packed_weight(h, l, 1));
       if (st != PLM_OK) return st;
       st = lora_correction(h, l, 3, h->act, m.intermediate, gated_from, rows, hidden, s, &down_ld);
       if (st != PLM_OK) return st;
       s_d = gemm_partial_splits(h->ctx, hidden, m.intermediate, rows);
       st = gemm(h, h->down[l], &h->map_down[l], hidden, m.intermediate, h->act, rows, part, h->partials, hidden, s,
-                s_d);
+                s_d, 0, packed_weight(h, l, 2));
       if (st != PLM_OK) return st;
     }
     const bool last = l + 1 == m.num_layers;
@@ -1025,3 +1035,10 @@ int plm_check(plm_handle* h, int32_t* device_error) {
 }
 
 }  // extern "C"
+
+extern "C" int plm_borrowed_weights(plm_handle* h, int32_t* groups) {
+  if (h == nullptr || groups == nullptr) return fail(PLM_ERR_INVALID, "plm_borrowed_weights: null argument");
+  // qkv, lm_head, the norms and embeddings are always read in place; o, gate_up and down only without packed copies
+  *groups = PLM_WEIGHTS_IN_PLACE | (h->block_tiles == nullptr ? PLM_WEIGHTS_BLOCK : 0);
+  return PLM_OK;
+}

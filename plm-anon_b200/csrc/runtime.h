@@ -103,8 +103,10 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 int gemm_cluster_splits(int tiles, int total_kb, int slots);
 
 // Internal GEMM launch used by plm_gemm and by the round engine (`map_w` encoded once per weight).
+// With `w_packed` the weight comes from its packed tiles (pack.cu) instead of map_w, which the kernel then only
+// prefetches.
 int gemm_launch(plm_ctx* ctx, const plm_gemm_desc& d, const CUtensorMap* map_w, const CUtensorMap* map_x,
-                cudaStream_t stream, bool pdl);
+                cudaStream_t stream, bool pdl, const void* w_packed = nullptr);
 int gemm_weight_map(CUtensorMap* map, const plm_gemm_desc& d);
 int gemm_row_map(CUtensorMap* map, const plm_gemm_desc& d);
 int gemm_token_tile(int rows);

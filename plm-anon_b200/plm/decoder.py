@@ -52,7 +52,8 @@ class RoundDecoder:
     def __init__(self, weights: PLMWeights, k: int, accept_rule: str = "nucleus", threshold: float | None = None,
                  chunk_widths: tuple[int, ...] = (), *, block_size: int = 64, kv_cache_bytes: int = 1 << 30,
                  max_model_len: int = 4096, tokenizer=None, eos_token_id: int | None = None,
-                 block_table: list[int] | None = None, max_prefill: int = 256, separate_mlp: bool = False) -> None:
+                 block_table: list[int] | None = None, max_prefill: int = 256, separate_mlp: bool = False,
+                 release_block_weights: bool = False) -> None:
         if accept_rule not in ("nucleus", "floor"):
             raise ValueError(f"accept rule {accept_rule!r}: nucleus or floor")
         if not torch.cuda.is_available():
@@ -104,6 +105,12 @@ class RoundDecoder:
             separate_mlp=1 if separate_mlp else 0)
         self.handle = native.Handle(model, ptrs, round_desc,
                                     keepalive=(weights, self.cos_sin, self._layer_arrays, ptp_desc))
+        # A handle that reads only its packed copies of o, gate_up and down leaves the originals to the caller; with
+        # release_block_weights (for weights this decoder owns, as RoundConfig.build's) they are dropped here.
+        self.released_block_weights = False
+        if release_block_weights and not (self.handle.borrowed_weights() & native.WEIGHTS_BLOCK):
+            weights.o = weights.gate_up = weights.down = None
+            self.released_block_weights = True
         if block_table is not None:
             self.handle.set_block_table(block_table)
         st = self.handle.state()

@@ -48,6 +48,7 @@ class GemmDesc(ctypes.Structure):
 
 RULE_NUCLEUS, RULE_FLOOR = 0, 1
 BOOK_NONE, BOOK_STEADY, BOOK_ROUND0, BOOK_FIRST_TOKEN = range(4)
+WEIGHTS_IN_PLACE, WEIGHTS_BLOCK = 1, 2  # plm_borrowed_weights
 
 
 class Bookkeeping(ctypes.Structure):
@@ -175,6 +176,7 @@ _SIGNATURES: dict[str, list] = {
     "plm_round0": [c_void_p, c_void_p],
     "plm_round": [c_void_p, c_void_p],
     "plm_layer_block": [c_void_p, c_int32, c_int32, c_void_p],
+    "plm_borrowed_weights": [c_void_p, ctypes.POINTER(c_int32)],
     "plm_state": [c_void_p, POINTER(StatePtrs)],
     "plm_check": [c_void_p, POINTER(c_int32)],
 }
@@ -380,6 +382,12 @@ class Handle:
 
     def round(self, stream=None) -> None:
         check(library().plm_round(self.handle, stream_handle(stream)), "plm_round")
+
+    def borrowed_weights(self) -> int:
+        """Bit mask of the caller's weight groups the handle still reads (WEIGHTS_IN_PLACE, WEIGHTS_BLOCK)."""
+        groups = c_int32(0)
+        check(library().plm_borrowed_weights(self.handle, ctypes.byref(groups)), "plm_borrowed_weights")
+        return groups.value
 
     def layer_block(self, layer: int, rows: int, stream=None) -> None:
         """One decoder layer's o projection, post-attention norm and MLP as the round runs it (plm_layer_block)."""

@@ -119,7 +119,9 @@ class RoundConfig:
                 tokenizer = AutoTokenizer.from_pretrained(self.model)
             except Exception:
                 tokenizer = None
+        # the decoder owns these weights: the o, gate_up and down originals go once the handle holds packed copies
         decoder = RoundDecoder(self.weights(), self.k, rule, threshold, PREFILL_BUCKETS, block_size=block_size,
-                               kv_cache_bytes=kv_cache_bytes, max_model_len=self.max_model_len, tokenizer=tokenizer)
+                               kv_cache_bytes=kv_cache_bytes, max_model_len=self.max_model_len, tokenizer=tokenizer,
+                               release_block_weights=True)
         decoder.prepare()
         return decoder

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} is declared but not exported"
     assert sorted(native.exported_symbols()) == declared, "ctypes signatures must cover exactly the header"
-    assert lib.plm_abi_version() == 7
+    assert lib.plm_abi_version() == 8
 
 
 STRUCTS = ["plm_gemm_epilogue", "plm_gemm_desc", "plm_bookkeeping", "plm_verify_desc", "plm_attention_desc",

@@ -118,3 +118,46 @@ def test_float16_export_runs_in_float16(tmp_path):
     assert a == b and len(a) == 24
     converted.close()
     same.close()
+
+
+def test_released_block_weights_decode_the_same():
+    """A decoder that frees its o, gate_up and down originals (the handle reads its packed copies everywhere, the
+    separate GEMMs of a 200-row prefill chunk included) decodes bit for bit what one keeping them decodes, and the
+    originals' memory is returned."""
+    from plm.decoder import RoundDecoder
+    from plm.model import PLMWeights, shape_config
+
+    cfg = shape_config("plm-tiny")
+    keep = RoundDecoder(PLMWeights.random(cfg, seed=6), 7, block_size=16, kv_cache_bytes=64 << 20,
+                        max_model_len=1024)
+    assert not keep.released_block_weights
+    weights = PLMWeights.random(cfg, seed=6)
+    layer_bytes = sum(t.numel() * t.element_size() for t in [*weights.o, *weights.gate_up, *weights.down])
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    freed = RoundDecoder(weights, 7, block_size=16, kv_cache_bytes=64 << 20, max_model_len=1024,
+                         release_block_weights=True)
+    torch.cuda.synchronize()
+    assert freed.released_block_weights and weights.o is None and weights.down is None
+    assert torch.cuda.memory_allocated() - before <= -layer_bytes + (1 << 20) + _allocated_by(freed)
+    prompt = torch.randint(0, cfg.vocab, (200,), generator=torch.Generator().manual_seed(2))
+    results = []
+    for decoder in (keep, freed):
+        decoder._fill_aux(3)
+        decoder.handle.set_stop(1 << 62)
+        decoder.handle.load_prompt(prompt.pin_memory())
+        decoder.handle.prefill()
+        decoder.handle.round0()
+        for _ in range(3):
+            decoder.handle.round()
+        torch.cuda.synchronize()
+        decoder.check()
+        results.append((decoder.out[:16].clone(), decoder.verify_logits.clone(), int(decoder.base_t)))
+    assert torch.equal(results[0][0], results[1][0]) and results[0][2] == results[1][2]
+    assert torch.equal(results[0][1], results[1][1])
+
+
+def _allocated_by(decoder) -> int:
+    """Bytes torch allocated for the decoder's own tensors (rotary table and pinned views are not device allocations
+    beyond the rotary cache)."""
+    return decoder.cos_sin.numel() * decoder.cos_sin.element_size()
