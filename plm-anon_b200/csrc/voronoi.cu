@@ -846,11 +846,12 @@ __global__ void __launch_bounds__(kThreads, 1) verify_decode_kernel(const Verify
         float p[kTargetsPerWarp];
 #pragma unroll
         for (int t = 0; t < kTargetsPerWarp; ++t) p[t] = lane < tn[t] ? s->wbuf[tb[t] + lane] : 0.0f;
-        if (chunks > 1) {
+        // entries l + 32, l + 64, ... chunk by chunk, the loads of all the warp's targets of a chunk in flight together;
+        // each target still adds its entries in order (past its end it adds 0, which leaves the nonnegative sum as is)
+        for (int c = 1; c < chunks; ++c) {
+          const int i = lane + 32 * c;
 #pragma unroll
-          for (int t = 0; t < kTargetsPerWarp; ++t) {
-            for (int i = lane + 32; i < ((tn[t] + 31) & ~31); i += 32) p[t] = p[t] + (i < tn[t] ? s->wbuf[tb[t] + i] : 0.0f);
-          }
+          for (int t = 0; t < kTargetsPerWarp; ++t) p[t] = p[t] + (i < tn[t] ? s->wbuf[tb[t] + i] : 0.0f);
         }
         const float total = transposed_warp_sum(p, lane);
         if ((lane & 1) == 0) s->mine[(lane >> 1) * kWarps + warp] = total;
