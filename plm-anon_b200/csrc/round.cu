@@ -498,7 +498,9 @@ int verify(plm_handle* h, int n_rows, int mode, const int64_t* aux_base, cudaStr
   a.err = h->ctx->err;
   int st = verify_validate(a, n_rows);
   if (st != PLM_OK) return st;
-  return verify_launch(a, h->m.dtype, n_rows, s, true);
+  // Launched without programmatic dependent launch: started early, its clusters were placed while lm_head's CTAs
+  // still held the SMs and the decode's critical path grew by ~9 us.
+  return verify_launch(a, h->m.dtype, n_rows, s, false);
 }
 
 // The accepted verify rows of the round just decided, from the round scratch into the pages (commit.cu).
