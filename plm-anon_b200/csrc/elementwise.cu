@@ -51,7 +51,6 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
   __shared__ float s_u;
   const int r = blockIdx.x, tid = threadIdx.x;
   grid_dependency_wait();
-  allow_dependents();
   if (r == 0 && a.counters != nullptr)
     for (int i = tid; i < a.n_counters; i += kRowThreads) a.counters[i] = 0;
   const int64_t offset = *a.offset;
@@ -159,9 +158,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
     }
   }
   ss = block_sum_rows(ss, red);
-  // The next kernel (the qkv projection's clusters) is let in only now: launched at this kernel's start, its
-  // clusters were placed while the layer block still held most SMs, and one launch in three ran half again as long.
-  allow_dependents();
+  allow_dependents();  // the first qkv projection is let in once the rows' sums are known, as after add_norm
   const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
 #pragma unroll
   for (int j = 0; j < kMaxVecs; ++j) {
