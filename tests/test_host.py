@@ -184,3 +184,31 @@ def test_oracle_commit_moves_rows_through_the_block_table():
     np.testing.assert_array_equal(cache[:, :, 0, :, 0, :], scratch[:, :, 1])  # logical 4 -> page 0, slot 0
     np.testing.assert_array_equal(cache[:, :, 0, :, 1, :], scratch[:, :, 2])  # logical 5 -> page 0, slot 1
     assert np.count_nonzero(cache) == np.count_nonzero(scratch[:, :, :3])
+
+
+def test_timeline_critical_path_adds_up_to_the_span():
+    """bench/timeline.py's accounting on synthetic kernel records of two rounds: a launch's critical path is the time
+    from the previous launch's end to its own, overlapping launches (programmatic dependent launch) included, and the
+    critical paths of a round add up to its span; the last GEMM of a round is lm_head."""
+    import importlib.util
+    from pathlib import Path
+
+    path = Path(__file__).resolve().parents[1] / "plm-anon_b200" / "bench" / "timeline.py"
+    spec = importlib.util.spec_from_file_location("plm_timeline", path)
+    tl = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tl)
+    one_round = [("embed_norm_kernel", 0, 4), ("skinny_gemm_kernel<2>", 3, 15), ("round_attention_kernel", 14, 16),
+                 ("mlp_block_kernel", 20, 44), ("add_norm_kernel", 60, 8), ("skinny_gemm_kernel<3>", 66, 40),
+                 ("verify_decode_kernel", 106, 110), ("commit_kernel", 214, 4)]
+    events = []
+    for r in range(2):
+        events += [{"name": n, "ts": 1000 * r + t, "dur": d, "cat": "kernel"} for n, t, d in one_round]
+    result = tl.summarise(events, rounds=2)
+    assert result["launches"] == len(one_round)
+    assert result["span_us"] == 218.0
+    crit = [x["critical_us"] for x in result["timeline"]]
+    assert crit == [4, 14, 12, 34, 4, 38, 110, 2]
+    assert abs(sum(crit) - result["span_us"]) < 1e-9
+    kinds = result["kinds"]
+    assert kinds["skinny_gemm (qkv)"]["launches"] == 1 and kinds["skinny_gemm (lm_head)"]["launches"] == 1
+    assert abs(sum(v["critical_share"] for v in kinds.values()) - 1.0) < 1e-3
