@@ -211,4 +211,4 @@ def test_timeline_critical_path_adds_up_to_the_span():
     assert abs(sum(crit) - result["span_us"]) < 1e-9
     kinds = result["kinds"]
     assert kinds["skinny_gemm (qkv)"]["launches"] == 1 and kinds["skinny_gemm (lm_head)"]["launches"] == 1
-    assert abs(sum(v["critical_share"] for v in kinds.values()) - 1.0) < 1e-3
+    assert abs(sum(v["critical_share"] for v in kinds.values()) - 1.0) < 5e-3  # shares rounded to 3 places
