@@ -423,6 +423,15 @@ template <typename T, int NTOK>
 __device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int et, float* red,
                                                volatile int* abort_flag) {
   constexpr int kThreads = kMlpEpiWarps * 32;
+  constexpr int kMaxChunks = 2;  // hidden <= 8 * 256 * 2
+  // The norm weight is never written: loaded before the wait for the o partials, so that no load follows the row's
+  // barrier.
+  uint4 wv[kMaxChunks];
+#pragma unroll
+  for (int j = 0; j < kMaxChunks; ++j) {
+    const int c = et + j * kThreads;
+    if (c < p.hidden / 8) wv[j] = reinterpret_cast<const uint4*>(p.norm_weight)[c];
+  }
   if (et == 0) {
     const int target = p.o_units;
     if (ld_acquire_gpu(p.ctr + 0) < target) {
@@ -440,8 +449,6 @@ __device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int 
   named_barrier_sync(4, kThreads);  // the partials of every o unit are visible from here on
   const int chunks = p.hidden / 8;
   T* res = reinterpret_cast<T*>(p.residual) + size_t(r) * p.hidden;
-  const T* w = reinterpret_cast<const T*>(p.norm_weight);
-  constexpr int kMaxChunks = 2;  // hidden <= 8 * 256 * 2
   float v[kMaxChunks][8];
   float ss = 0.f;
 #pragma unroll
@@ -501,8 +508,7 @@ __device__ __forceinline__ void block_norm_row(const BlockParams& p, int r, int 
   for (int j = 0; j < kMaxChunks; ++j) {
     const int c = et + j * kThreads;
     if (c >= chunks) continue;
-    const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
-    const T* w8 = reinterpret_cast<const T*>(&wv);
+    const T* w8 = reinterpret_cast<const T*>(&wv[j]);
     uint4 o;
     T* o8 = reinterpret_cast<T*>(&o);
 #pragma unroll
