@@ -288,6 +288,13 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of a cluster barrier, for work between them: every thread arrives, then later waits. An arrival
+// without release orders nothing; the wait returns once every thread of every CTA of the cluster has arrived, so a
+// CTA that passed it knows that all CTAs of its cluster have started.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 // Shared-memory address of `local` (an address in this CTA's shared memory) in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank) {
   uint32_t out;
@@ -298,6 +305,9 @@ __device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank
 __device__ __forceinline__ void st_dsmem_f32x4(uint32_t addr, float4 v) {
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 // One arrival on a cluster peer's mbarrier (`remote_bar` from cluster_map) with release semantics at cluster scope:
 // this thread's earlier writes, and those ordered before it by a CTA barrier, are visible to the peer's waiters.

@@ -11,6 +11,8 @@ constexpr int kRowThreads = 256;
 constexpr int kVec = 8;      // 16-byte vectors of bf16
 constexpr int kMaxVecs = 2;  // vectors per thread: hidden <= kRowThreads * kVec * kMaxVecs = 4096
 constexpr int kMaxNormPartials = 16;  // k-split partials an add_norm may sum
+constexpr int kNormThreads = 256;     // add_norm: at most, one or two quads of 4 elements a thread
+constexpr int kNormQuads = 2;         // hidden <= 4 * kNormThreads * kNormQuads * (cluster of 2) = 4096
 
 // The row's 16-byte vectors owned by this thread: vector j is elements [8 (tid + j 256), ... + 8).
 template <typename T>
@@ -173,109 +175,139 @@ __global__ void __launch_bounds__(kRowThreads) embed_norm_kernel(const PrologueA
   }
 }
 
-// One CTA per row: residual <- x + residual; normed <- RMSNorm(x + residual) * w (vLLM fused_add_rms_norm:
-// the sum is formed in fp32, stored rounded as the new residual, and normalised unrounded). With gather_row >= 0
+// A cluster of CS CTAs per row (CS = 4, or 2 when hidden is not a multiple of 16): residual <- x + residual;
+// normed <- RMSNorm(x + residual) * w (vLLM fused_add_rms_norm: the sum is formed in fp32, stored rounded as the new
+// residual, and normalised unrounded). CTA q of the row's cluster owns columns [q hidden / CS, (q + 1) hidden / CS),
+// in quads of 4 elements, one or two per thread, so each SM takes in a CS-th of the row's k-split partials. The
+// CTAs' sums of squares are exchanged through distributed shared memory and added in rank order. With gather_row >= 0
 // the normed row `gather_row` is also copied to `gathered` (the prefill's last prompt row).
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads) add_norm_kernel(const AddNormArgs a) {
-  __shared__ float red[32];
-  const int r = blockIdx.x, tid = threadIdx.x;
-  grid_dependency_wait();
+template <typename T, int CS>
+__global__ void __launch_bounds__(kNormThreads) add_norm_kernel(const AddNormArgs a) {
+  __shared__ float red[kNormThreads / 32];
+  __shared__ float row_ss[CS];  // every CTA's sum of squares, pushed by the CTA itself
+  const uint32_t rank = cluster_rank();
+  const int r = blockIdx.x / CS, tid = threadIdx.x, nthreads = blockDim.x;
+  const int quads = a.hidden / (4 * CS), q0 = int(rank) * quads;  // this CTA's quads [q0, q0 + quads)
+  cluster_arrive_relaxed();  // paired with the wait before the push: every CTA of the cluster has started by then
   const T* __restrict__ x = reinterpret_cast<const T*>(a.x) + size_t(r) * a.hidden;
   T* __restrict__ res = reinterpret_cast<T*>(a.residual) + size_t(r) * a.hidden;
   T* __restrict__ nrm = reinterpret_cast<T*>(a.normed) + size_t(r) * a.hidden;
-  const T* __restrict__ w = reinterpret_cast<const T*>(a.weight);
   T* gathered = (r == a.gather_row && a.gathered != nullptr) ? reinterpret_cast<T*>(a.gathered) : nullptr;
-  uint4 xv[kMaxVecs], rv[kMaxVecs], wv[kMaxVecs];  // every load of the row is issued before any store
-  load_row<T>(res, a.hidden, rv);
-  load_row<T>(w, a.hidden, wv);
+  uint2 wv[kNormQuads], rv[kNormQuads], xv[kNormQuads];
+  // The norm weight is never written: loaded before the dependency wait.
+#pragma unroll
+  for (int j = 0; j < kNormQuads; ++j) {
+    const int q = tid + j * nthreads;
+    if (q < quads) wv[j] = reinterpret_cast<const uint2*>(a.weight)[q0 + q];
+  }
+  grid_dependency_wait();
+  // Every load of the CTA's columns is issued before any store.
+#pragma unroll
+  for (int j = 0; j < kNormQuads; ++j) {
+    const int q = tid + j * nthreads;
+    if (q < quads) rv[j] = reinterpret_cast<const uint2*>(res)[q0 + q];
+  }
   if (a.partials != nullptr) {
     // The projection's k-split partials, summed in split order from 0 and rounded to the model dtype: the values the
-    // GEMM's own reduction and store would have produced.
-    // Per 8-element chunk, the loads of every split are issued before the in-order sum (one round trip).
+    // GEMM's own reduction and store would have produced. The loads of every split of a quad go out before the sum.
     const float* __restrict__ pp = a.partials + size_t(r) * a.hidden;
 #pragma unroll
-    for (int j = 0; j < kMaxVecs; ++j) {
-      const int c = tid + j * kRowThreads;
-      xv[j] = make_uint4(0, 0, 0, 0);
-      if (c * kVec >= a.hidden) continue;
-      float4 lo[kMaxNormPartials], hi[kMaxNormPartials];
+    for (int j = 0; j < kNormQuads; ++j) {
+      const int q = tid + j * nthreads;
+      xv[j] = make_uint2(0, 0);
+      if (q >= quads) continue;
+      float4 p[kMaxNormPartials];
+#pragma unroll
+      for (int sp = 0; sp < kMaxNormPartials; ++sp)
+        if (sp < a.n_partials) p[sp] = reinterpret_cast<const float4*>(pp + size_t(sp) * a.partial_stride)[q0 + q];
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int sp = 0; sp < kMaxNormPartials; ++sp) {
         if (sp < a.n_partials) {
-          const float4* ps = reinterpret_cast<const float4*>(pp + size_t(sp) * a.partial_stride);
-          lo[sp] = ps[2 * c];
-          hi[sp] = ps[2 * c + 1];
-        }
-      }
-      float acc[kVec] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int sp = 0; sp < kMaxNormPartials; ++sp) {
-        if (sp < a.n_partials) {
-          acc[0] += lo[sp].x;
-          acc[1] += lo[sp].y;
-          acc[2] += lo[sp].z;
-          acc[3] += lo[sp].w;
-          acc[4] += hi[sp].x;
-          acc[5] += hi[sp].y;
-          acc[6] += hi[sp].z;
-          acc[7] += hi[sp].w;
+          acc[0] += p[sp].x;
+          acc[1] += p[sp].y;
+          acc[2] += p[sp].z;
+          acc[3] += p[sp].w;
         }
       }
       T* xo = reinterpret_cast<T*>(&xv[j]);
 #pragma unroll
-      for (int q = 0; q < kVec; ++q) xo[q] = from_f32<T>(acc[q]);
+      for (int e = 0; e < 4; ++e) xo[e] = from_f32<T>(acc[e]);
     }
   } else {
-    load_row<T>(x, a.hidden, xv);
+#pragma unroll
+    for (int j = 0; j < kNormQuads; ++j) {
+      const int q = tid + j * nthreads;
+      if (q < quads) xv[j] = reinterpret_cast<const uint2*>(x)[q0 + q];
+    }
   }
   if (a.corr != nullptr && r >= a.corr_from) {
     // a gated-LoRA adapter's output on this row, added to the projection's rounded output and rounded again
     const float* __restrict__ cr = a.corr + size_t(r - a.corr_from) * a.corr_ld;
 #pragma unroll
-    for (int j = 0; j < kMaxVecs; ++j) {
-      const int c = tid + j * kRowThreads;
-      if (c * kVec >= a.hidden) continue;
-      const float4 lo = reinterpret_cast<const float4*>(cr)[2 * c], hi = reinterpret_cast<const float4*>(cr)[2 * c + 1];
-      const float add[kVec] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    for (int j = 0; j < kNormQuads; ++j) {
+      const int q = tid + j * nthreads;
+      if (q >= quads) continue;
+      const float4 add = reinterpret_cast<const float4*>(cr)[q0 + q];
+      const float av[4] = {add.x, add.y, add.z, add.w};
       T* xo = reinterpret_cast<T*>(&xv[j]);
 #pragma unroll
-      for (int q = 0; q < kVec; ++q) xo[q] = from_f32<T>(to_f32<T>(xo[q]) + add[q]);
+      for (int e = 0; e < 4; ++e) xo[e] = from_f32<T>(to_f32<T>(xo[e]) + av[e]);
     }
   }
-  float v[kMaxVecs][kVec];
+  float v[kNormQuads][4];
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxVecs; ++j) {
-    const int c = tid + j * kRowThreads;
-    if (c * kVec < a.hidden) {
-      uint4 o;
-      T* ov = reinterpret_cast<T*>(&o);
+  for (int j = 0; j < kNormQuads; ++j) {
+    const int q = tid + j * nthreads;
+    if (q >= quads) continue;
+    const T* x4 = reinterpret_cast<const T*>(&xv[j]);
+    const T* r4 = reinterpret_cast<const T*>(&rv[j]);
+    uint2 o;
+    T* o4 = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int q = 0; q < kVec; ++q) {
-        v[j][q] = elem<T>(xv[j], q) + elem<T>(rv[j], q);
-        ov[q] = from_f32<T>(v[j][q]);
-        ss += v[j][q] * v[j][q];
-      }
-      reinterpret_cast<uint4*>(res)[c] = o;
+    for (int e = 0; e < 4; ++e) {
+      v[j][e] = to_f32<T>(x4[e]) + to_f32<T>(r4[e]);
+      o4[e] = from_f32<T>(v[j][e]);
+      ss += v[j][e] * v[j][e];
     }
+    reinterpret_cast<uint2*>(res)[q0 + q] = o;
   }
-  ss = block_sum_rows(ss, red);
+  // CTA sum (lanes by butterfly, warps in order), pushed into slot `rank` of every CTA of the cluster; after the
+  // cluster barrier each CTA adds the CS sums in rank order.
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  cluster_wait();
+  if (tid < CS) {
+    float t = 0.f;
+    for (int w = 0; w < (nthreads + 31) / 32; ++w) t += red[w];
+    st_dsmem_f32(cluster_map(&row_ss[rank], uint32_t(tid)), t);
+  }
+  cluster_sync();
+  float total = 0.f;
+#pragma unroll
+  for (int c = 0; c < CS; ++c) total += row_ss[c];
   // The next kernel (the qkv projection's clusters) is let in only now: launched at this kernel's start, its
   // clusters were placed while the layer block still held most SMs, and one launch in three ran half again as long.
   allow_dependents();
-  const float rstd = rsqrtf(ss / float(a.hidden) + a.eps);
+  const float rstd = rsqrtf(total / float(a.hidden) + a.eps);
+  uint8_t* tiles = static_cast<uint8_t*>(a.row_tiles);
 #pragma unroll
-  for (int j = 0; j < kMaxVecs; ++j) {
-    const int c = tid + j * kRowThreads;
-    if (c * kVec < a.hidden) {
-      uint4 o;
-      T* ov = reinterpret_cast<T*>(&o);
+  for (int j = 0; j < kNormQuads; ++j) {
+    const int q = tid + j * nthreads;
+    if (q >= quads) continue;
+    const T* w4 = reinterpret_cast<const T*>(&wv[j]);
+    uint2 o;
+    T* o4 = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int q = 0; q < kVec; ++q) ov[q] = from_f32<T>(round_to<T>(v[j][q] * rstd) * elem<T>(wv[j], q));
-      reinterpret_cast<uint4*>(nrm)[c] = o;
-      if (gathered != nullptr) reinterpret_cast<uint4*>(gathered)[c] = o;
-      if (a.row_tiles != nullptr) reinterpret_cast<uint4*>(a.row_tiles)[row_tile_chunk(c >> 3, r, c & 7, a.tile_rows)] = o;
+    for (int e = 0; e < 4; ++e) o4[e] = from_f32<T>(round_to<T>(v[j][e] * rstd) * to_f32<T>(w4[e]));
+    const int g = q0 + q;  // quad of the row: elements [4 g, 4 g + 4), half (g & 1) of 8-element chunk g / 2
+    reinterpret_cast<uint2*>(nrm)[g] = o;
+    if (gathered != nullptr) reinterpret_cast<uint2*>(gathered)[g] = o;
+    if (tiles != nullptr) {
+      const int c = g >> 1;
+      *reinterpret_cast<uint2*>(tiles + row_tile_chunk(c >> 3, r, c & 7, a.tile_rows) * 16 + (g & 1) * 8) = o;
     }
   }
 }
@@ -321,14 +353,20 @@ int prologue_launch(const PrologueArgs& a, int rows, cudaStream_t stream, bool p
                     "embed_norm_kernel");
 }
 
+template <int CS>
+int launch_add_norm(const AddNormArgs& a, int rows, cudaStream_t stream, bool pdl) {
+  const int quads = a.hidden / (4 * CS);
+  const int threads = min(kNormThreads, (quads + 31) / 32 * 32);
+  auto kernel = a.dtype == PLM_F16 ? add_norm_kernel<__half, CS> : add_norm_kernel<__nv_bfloat16, CS>;
+  return check_cuda(launch_cluster(kernel, dim3(rows * CS), dim3(threads), 0, stream, pdl, CS, 1, a),
+                    "add_norm_kernel");
+}
+
 int add_norm_launch(const AddNormArgs& a, int rows, cudaStream_t stream, bool pdl) {
   if (a.hidden > kRowThreads * kVec * kMaxVecs || a.hidden % kVec != 0)
     return fail(PLM_ERR_UNSUPPORTED, "add_norm: hidden %d (a multiple of 8, at most 4096)", a.hidden);
-  if (a.dtype == PLM_F16)
-    return check_cuda(launch(add_norm_kernel<__half>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
-                      "add_norm_kernel");
-  return check_cuda(launch(add_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, stream, pdl, a),
-                    "add_norm_kernel");
+  if (a.n_partials > kMaxNormPartials) return fail(PLM_ERR_UNSUPPORTED, "add_norm: %d partials", a.n_partials);
+  return a.hidden % 16 == 0 ? launch_add_norm<4>(a, rows, stream, pdl) : launch_add_norm<2>(a, rows, stream, pdl);
 }
 
 int kv_append_launch(const KvAppendArgs& a, cudaStream_t stream, bool pdl) {
