@@ -197,7 +197,7 @@ typedef struct plm_attention_desc {
   const int32_t* own_start;    /* [rows] */
   int32_t num_heads, num_kv_heads, head_dim;
   void* out;                   /* [rows][num_heads * head_dim] */
-  int32_t splits;              /* 0 = choose from max_keys; else a power of two <= 8 (one cluster), or 16: two clusters of
+  int32_t splits;              /* 0 = choose from max_keys; else 1 to 8 (one cluster), or 16: two clusters of
                                   8 merged through buffers the context owns (the second cluster works only when every
                                   split gets four key tiles); not under stream capture on its first use */
   int64_t max_keys;

@@ -453,9 +453,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   }
   cluster_sync();
   const uint32_t rank = cluster_rank();
-  const int rpc = kQRowsPerCta / S;
+  const int rpc = (kQRowsPerCta + S - 1) / S;  // rows per rank; the last rank's share ends at the tile's edge
   const int row_begin = int(rank) * rpc;
-  if (tid < rpc) {
+  const int own_rows = max(0, min(rpc, kQRowsPerCta - row_begin));
+  if (tid < own_rows) {
     const int row = row_begin + tid;
     float ms[kClusterMax], ls[kClusterMax], mmax = -INFINITY;
 #pragma unroll
@@ -482,7 +483,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) round_attention_kernel(const 
   // 16-byte remote loads, two of the thread's row chunks x every rank in flight at a time; rows past a.rows are
   // skipped
   constexpr int Q4 = HD / 4;  // float4 per row
-  const int live = max(0, min(rpc, a.rows - (qt * kQRowsPerCta + row_begin)));
+  const int live = max(0, min(own_rows, a.rows - (qt * kQRowsPerCta + row_begin)));
   for (int idx0 = tid; idx0 < live * Q4; idx0 += 2 * kAttnThreads) {
     float4 part[2][kClusterMax];
 #pragma unroll
@@ -601,9 +602,8 @@ int attention_launch(plm_ctx* ctx, AttnArgs a, cudaStream_t stream, bool pdl) {
     return fail(PLM_ERR_INVALID, "attention: null operand");
   const int q_tiles = (a.rows + kQRowsPerCta - 1) / kQRowsPerCta;
   if (a.splits < 1) a.splits = 1;
-  if (a.part != nullptr ? a.splits != 2 * kClusterMax || a.arrive == nullptr
-                        : (a.splits & (a.splits - 1)) != 0 || a.splits > kClusterMax)
-    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits (a power of two <= %d, or %d with merge buffers)", a.splits,
+  if (a.part != nullptr ? a.splits != 2 * kClusterMax || a.arrive == nullptr : a.splits > kClusterMax)
+    return fail(PLM_ERR_UNSUPPORTED, "attention: %d splits (at most %d, or %d with merge buffers)", a.splits,
                 kClusterMax, 2 * kClusterMax);
   a.err = ctx->err;
   if (a.dtype == PLM_F16)

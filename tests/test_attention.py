@@ -67,6 +67,11 @@ def _reference(q, kc, vc, table, offset, depth, own, page, heads, kv_heads):
     ("round0", 7, 256, 16, 16, 16, 128, 0),
     ("chunk", 0, 0, 16, 16, 16, 128, 0),
     ("chunk", 0, 512, 32, 8, 8, 64, 0),
+    # split counts that are not powers of two: each cluster rank combines ceil(64 / splits) rows, the last fewer
+    ("steady", 7, 1024, 16, 16, 16, 128, 7),
+    ("chunk", 0, 512, 16, 16, 16, 128, 7),      # full 64-row query tiles: row 63 lies in the last rank's share
+    ("chunk", 0, 300, 32, 8, 8, 64, 5),
+    ("steady", 6, 190, 16, 8, 8, 64, 3),
 ])
 def test_attention_matches_fp32(ctx, kind, k, ctx_len, page, heads, kv_heads, hd, splits):
     from plm import native
@@ -111,7 +116,7 @@ def test_attention_split_invariance(ctx):
     depth_t = torch.as_tensor(depth, dtype=torch.int32, device="cuda")
     own_t = torch.as_tensor(own, dtype=torch.int32, device="cuda")
     outs = {}
-    for splits in (1, 4, 8, 8):
+    for splits in (1, 4, 7, 8, 8):
         out = torch.zeros(rows, heads * hd, dtype=torch.bfloat16, device="cuda")
         desc = native.AttentionDesc(dtype=native.PLM_BF16, q=q.data_ptr(), k_cache=kc.data_ptr(),
                                     v_cache=vc.data_ptr(), block_table=table.data_ptr(), max_pages=max_pages,
@@ -124,7 +129,7 @@ def test_attention_split_invariance(ctx):
         if splits in outs:
             assert torch.equal(outs[splits], out)
         outs[splits] = out
-    for splits in (4, 8):
+    for splits in (4, 7, 8):
         assert (outs[splits].float() - outs[1].float()).abs().max().item() < 2e-2
 
 

@@ -13,7 +13,9 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("rows,hidden,gather", [(56, 2048, -1), (7, 512, 3), (3, 2560, 0), (5, 4096, -1)])
+# 1032 and 4088 are multiples of 8 but not 16: clusters of 2 CTAs per row, 4088 with two quads on most threads
+@pytest.mark.parametrize("rows,hidden,gather", [(56, 2048, -1), (7, 512, 3), (3, 2560, 0), (5, 4096, -1), (4, 1032, 1),
+                                                (3, 4088, -1)])
 def test_add_rmsnorm_matches_fp32(ctx, rows, hidden, gather):
     from plm import native
 
@@ -52,7 +54,7 @@ def test_add_rmsnorm_rejects_unsupported_width(ctx):
         native.add_rmsnorm(ctx, desc)
 
 
-@pytest.mark.parametrize("rows,hidden,splits", [(56, 2048, 16), (7, 512, 3), (3, 2560, 1)])
+@pytest.mark.parametrize("rows,hidden,splits", [(56, 2048, 16), (7, 512, 3), (3, 2560, 1), (5, 1032, 16), (2, 4088, 9)])
 def test_add_rmsnorm_from_partials(ctx, rows, hidden, splits):
     """x given as fp32 k-split partials: summed in split order and rounded to bf16 first, then the same fused
     residual-add RMSNorm; equal bit for bit to the run with that bf16 x."""
