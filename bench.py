@@ -479,10 +479,10 @@ def shape_config_vocab() -> int:
 # separate-launch configuration.
 GEMM_DRAM_BYTES_PER_ROUND = 3.495e9
 # DRAM bytes (read + write) of one layer-block launch of the benchmark shape, from one ncu capture of a block of a
-# 2-layer model of the same shape: 134.92 MB read + 5.08 MB written. The reads are the block's own
+# 2-layer model of the same shape: 134.91 MB read + 4.53 MB written. The reads are the block's own
 # 109.7 MB (packed weights and row operands) plus the 25.2 MB of the next layer's qkv weights that its tail
 # prefetches into L2, which the qkv GEMM then reads from L2 instead of DRAM.
-BLOCK_DRAM_BYTES_PER_LAUNCH = 140.0e6
+BLOCK_DRAM_BYTES_PER_LAUNCH = 139.4e6
 BLOCK_PREFETCH_BYTES_PER_LAUNCH = 25.2e6
 
 
