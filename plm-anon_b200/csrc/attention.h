@@ -27,7 +27,7 @@ struct AttnArgs {
   void* out;                   // [rows][num_heads * head_dim]; may be null when row_tiles is set
   void* row_tiles;             // non-null: the output written as row tiles of tile_rows rows instead (common.cuh)
   int tile_rows;
-  int splits;                  // KV splits = cluster size, a power of two <= 8
+  int splits;                  // KV splits: 1 to 8 in one cluster, or 16 in two clusters with part/arrive set
   // non-null: keys at logical indices >= offset (the forward's own rows) are read from these [rows][kv_heads]
   // [head_dim] planes (the round scratch) instead of the paged cache
   const void* scratch_k;

@@ -271,7 +271,7 @@ def gemm(ctx: Context, w, x, rows: int, *, out=None, epi: GemmEpilogue | None = 
 
 
 def verify_decode(ctx: Context, desc: VerifyDesc, stream=None) -> None:
-    """Enqueue plm_verify_decode (one CTA per row)."""
+    """Enqueue plm_verify_decode (one cluster of 8 CTAs per verify row)."""
     check(library().plm_verify_decode(ctx.handle, ctypes.byref(desc), stream_handle(stream)), "plm_verify_decode")
 
 
